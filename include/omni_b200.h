@@ -1,0 +1,101 @@
+/* omni_b200.h -- op-level C ABI of the B200 (sm_100a) hot path.
+ *
+ * Plain pointers and sizes only.  Device pointers are CUDA device addresses on
+ * the caller's current device; `stream` is a cudaStream_t passed as void*
+ * (NULL = the legacy default stream).  Every function returns an
+ * omni_status code (include/omni/omni.h: 0 OK, 1 INVALID_ARGUMENT,
+ * 4 UNSUPPORTED, 5 OUT_OF_MEMORY, 7 INTERNAL_ERROR) and leaves a message in
+ * omni_b200_last_error() (thread local, valid until the next call on that
+ * thread).  Launches are asynchronous; kernel-side failures (a bounded
+ * pipeline wait that gave up) are reported by omni_b200_sync_check().
+ *
+ * These entry points are the batched/op-level form of the reference's inner
+ * backend interface omni::Ops (omni-tokenizer src/internal.h:52-90); the
+ * reference exposes that interface only to C++ (make_cuda(), used by
+ * tests/native_cuda_attention.cpp:24-41).  A consumer binds them the same way
+ * native.py binds omni.h.
+ */
+#ifndef OMNI_B200_H
+#define OMNI_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(_WIN32)
+#define OMNI_B200_API __declspec(dllexport)
+#else
+#define OMNI_B200_API __attribute__((visibility("default")))
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element types of tensors crossing this ABI. */
+enum omni_b200_dtype { OMNI_B200_F32 = 0, OMNI_B200_BF16 = 1, OMNI_B200_F16 = 2 };
+
+OMNI_B200_API const char *omni_b200_last_error(void);
+OMNI_B200_API const char *omni_b200_version(void);
+
+/* Synchronises `stream`, then reads and clears the current device's kernel
+ * error word.  Returns OMNI_INTERNAL_ERROR (7) if any kernel gave up a wait. */
+OMNI_B200_API int omni_b200_sync_check(void *stream);
+
+/* Batched attention on head-major tensors q, k, v, out of shape
+ * [batch, heads, L, head_dim], dtype BF16 or F16 (out may also be F32):
+ *   out[b,h,t,:] = softmax(scale * q[b,h,t,:] . k[b,h,s,:]) over s < limit(b,t)
+ * with limit(b,t) = min(L, lengths[b] (or L when lengths == NULL),
+ *                       block > 0 ? (t/block + 1)*block : inf).
+ * scale <= 0 selects head_dim^-1/2.  lengths is a DEVICE int32[batch]
+ * (key-padding mask for variable-length segments).  With skip_padded_queries
+ * != 0, 256-row query blocks lying wholly at or beyond lengths[b] are not
+ * computed and their output rows are left untouched.
+ * Generalises Ops::attention (omni-tokenizer src/internal.h:81-82) from one
+ * sequence of heads*head_dim columns to a batch of head-major sequences;
+ * head_dim 1..128 (64, 72 and 96 on the fast path with no repacking). */
+OMNI_B200_API int omni_b200_attention_bhld(const void *q, const void *k, const void *v, void *out,
+                                           int batch, int heads, int L, int head_dim, int dtype,
+                                           int out_dtype, const int32_t *lengths, int block,
+                                           int skip_padded_queries, float scale, void *stream);
+
+/* Ops::attention (omni-tokenizer src/internal.h:81-82, semantics of
+ * src/cpu.cpp:122-172) on the reference's row-major Value layout:
+ *   unfused: q, k, v are [n, heads*head_dim];
+ *   fused:   q is [n, 3*heads*head_dim] holding Q|K|V column blocks, k = v = NULL.
+ * out is [n, heads*head_dim] of out_dtype.  dtype F32 inputs (the audio fp32
+ * profile) and layouts that TMA cannot address directly are repacked into
+ * `workspace` first; omni_b200_attention_rows_workspace() gives the bytes
+ * needed (0 when no repacking is needed). */
+OMNI_B200_API size_t omni_b200_attention_rows_workspace(size_t n, int heads, int head_dim,
+                                                        int dtype, int fused);
+OMNI_B200_API int omni_b200_attention_rows(const void *q, const void *k, const void *v, void *out,
+                                           size_t n, int heads, int head_dim, size_t block,
+                                           size_t valid, int fused, int dtype, int out_dtype,
+                                           void *workspace, size_t workspace_bytes,
+                                           void *stream);
+
+/* Ops::squares (omni-tokenizer src/internal.h:86, semantics of
+ * src/cpu.cpp:216-226): out[r] = sum over columns in order of x[r,j]^2, with
+ * every square and the total rounded to bf16 when dtype is BF16.  x is
+ * [rows, cols] of dtype (F32 or BF16); out is [rows] of out_dtype. */
+OMNI_B200_API int omni_b200_squares(const void *x, void *out, size_t rows, size_t cols, int dtype,
+                                    int out_dtype, void *stream);
+
+/* Ops::quantize (omni-tokenizer src/internal.h:87-88, semantics of
+ * src/cpu.cpp:227-287): ids[r] = argmin over codes c of the profile's
+ * expanded L2 distance between x[r,:] and codebook[c,:], smallest id on ties.
+ * profile BF16: x, codebook and cbnorm (= squares(codebook), see above) are
+ * bf16; dist = bf16(bf16(|x|^2 + |c|^2) - bf16(2 bf16(x.c))).
+ * ids are uint16 (ids_u16 != 0, as the reference returns) or int32.
+ * workspace: omni_b200_vq_workspace() bytes of device memory (8 per row).
+ * x, codebook, cbnorm must be 16-byte aligned; codes <= 65536. */
+OMNI_B200_API size_t omni_b200_vq_workspace(size_t rows, size_t dim, size_t codes, int profile);
+OMNI_B200_API int omni_b200_vq_argmin(const void *x, const void *codebook, const void *cbnorm,
+                                      void *ids, size_t rows, size_t dim, size_t codes,
+                                      int profile, int ids_u16, void *workspace,
+                                      size_t workspace_bytes, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

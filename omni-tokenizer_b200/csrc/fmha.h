@@ -1,0 +1,55 @@
+// fmha.h -- host-side interface of the sm_100a attention kernel.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace omni_b200 {
+
+enum : int { kOutF32 = 0, kOutBF16 = 1, kOutF16 = 2 };
+
+// A (d, token, head, batch) view of 2-byte elements; strides in elements.
+struct TensorView {
+    int d = 0, tokens = 0, heads = 1, batch = 1;
+    long long s_token = 0, s_head = 0, s_batch = 0;
+};
+
+// Kernel parameters (passed as a __grid_constant__ argument).
+struct FmhaParams {
+    CUtensorMap tq0, tq1, tk0, tk1, tv0, tv1; // chunk 0 / chunk 1 tile maps
+    void *out;
+    long long o_sb, o_sh, o_st; // output strides in elements (batch, head, token)
+    const int *lengths;         // [batch] valid key counts, or nullptr
+    int batch, heads, L, hd;
+    int valid; // valid key count when lengths == nullptr
+    int block; // block-causal window (0: none)
+    int skip_padded_q;
+    int out_dtype;
+    int out_vec;
+    float scale_log2;
+    int *err;
+};
+
+struct FmhaArgs {
+    const void *q_ptr = nullptr, *k_ptr = nullptr, *v_ptr = nullptr;
+    TensorView q, k, v;
+    bool bf16 = true; // operand type: bf16 (true) or fp16 (false)
+    void *out = nullptr;
+    int out_dtype = kOutBF16;
+    long long o_sb = 0, o_sh = 0, o_st = 0;
+    const int *lengths = nullptr;
+    int valid = 0;
+    int block = 0;
+    int skip_padded_q = 0;
+    double scale = 0; // 0: out_d^-1/2
+    int out_d = 0;    // output columns per head (0: q.d); the operands may be zero-padded wider
+    int *err = nullptr;
+};
+
+// Returns 0 on success, a CUDA error code, or a negative/1000+ code for an
+// unsupported shape / tensor-map failure.
+int fmha_launch(const FmhaArgs &args, cudaStream_t stream);
+bool tma_view_ok(const void *base, const TensorView &v);
+int padded_head_dim(int hd);
+
+} // namespace omni_b200

@@ -1,0 +1,15 @@
+// tma.h -- tensor-map helpers (2-byte elements, swizzle chosen from the box row bytes:
+// 128 B -> 128B swizzle, 64 B -> 64B, 32 B -> 32B).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace omni_b200 {
+// Returns 0, -1 (no driver entry point) or 1000 + CUresult.
+int encode_tiled(CUtensorMap *map, const void *base, bool bf16, int rank, const uint64_t *dims,
+                 const uint64_t *byte_strides, const uint32_t *box);
+// Row-major [rows, cols] matrix; box of box_w columns x box_rows rows.
+int make_map_2d(CUtensorMap *map, const void *base, int cols, long long rows, int box_w,
+                int box_rows, bool bf16 = true);
+} // namespace omni_b200

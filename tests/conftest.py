@@ -15,3 +15,18 @@ if str(ROOT) not in sys.path:
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a)")
+
+
+def load_package():
+    """Import omni-tokenizer_b200/ as the module `omni_tokenizer_b200`."""
+    import importlib.util
+
+    name = "omni_tokenizer_b200"
+    if name in sys.modules:
+        return sys.modules[name]
+    pkg = ROOT / "omni-tokenizer_b200"
+    spec = importlib.util.spec_from_file_location(name, pkg / "__init__.py", submodule_search_locations=[str(pkg)])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod

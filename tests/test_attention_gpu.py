@@ -1,0 +1,168 @@
+"""GPU parity of the sm_100a attention kernel against the CPU oracle.
+
+Tolerance: for bf16/fp16 inputs, max-abs error <= 2e-2
+and mean-abs error <= 2e-3 against the reference's fp32 CPU attention
+(src/cpu.cpp:122-172) run on the same (bf16/fp16-representable) values.
+Every test calls the CUDA kernel through the C ABI (include/omni_b200.h).
+"""
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+MAX_ABS, MEAN_ABS = 2e-2, 2e-3
+
+
+@pytest.fixture(scope="module")
+def ob():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from tests.conftest import load_package
+
+    return load_package()
+
+
+def _close(got, want, what=""):
+    err = np.abs(got.astype(np.float64) - want.astype(np.float64))
+    assert np.isfinite(got).all(), f"{what}: non-finite output"
+    assert err.max() <= MAX_ABS, f"{what}: max-abs {err.max():.3e}"
+    assert err.mean() <= MEAN_ABS, f"{what}: mean-abs {err.mean():.3e}"
+    return err.max(), err.mean()
+
+
+def _bhld_inputs(B, H, L, D, dtype, seed, scale=1.0):
+    g = torch.Generator().manual_seed(seed)
+    qkv = [(torch.randn(B, H, L, D, generator=g) * scale).to(dtype) for _ in range(3)]
+    return qkv
+
+
+@pytest.mark.parametrize(
+    "B,H,L,D,dtype",
+    [
+        (1, 2, 300, 64, torch.bfloat16),   # Whisper-shaped head dim, partial tiles
+        (2, 2, 729, 72, torch.float16),    # SigLIP-shaped head dim (72 -> 80 in the tile)
+        (1, 3, 257, 96, torch.bfloat16),   # production image head dim
+        (1, 1, 1, 64, torch.bfloat16),     # single token
+        (1, 2, 1500, 64, torch.bfloat16),  # config 1 length
+        (1, 2, 130, 128, torch.float16),
+        (2, 1, 200, 32, torch.bfloat16),
+        (1, 2, 77, 16, torch.float16),
+    ],
+)
+def test_bhld_matches_oracle(ob, B, H, L, D, dtype):
+    q, k, v = _bhld_inputs(B, H, L, D, dtype, seed=B * 1000 + L + D, scale=0.5 if dtype == torch.float16 else 1.0)
+    out = ob.attention_bhld(q.cuda(), k.cuda(), v.cuda(), out_dtype=torch.float32)
+    ob.library().sync_check()
+    want = O.attention_bhld(q.float().numpy(), k.float().numpy(), v.float().numpy())
+    _close(out.cpu().numpy(), want, f"B{B} H{H} L{L} D{D}")
+
+
+def test_bhld_key_padding_lengths(ob):
+    """Config-3 style varlen batch: padded keys are masked, padded queries ignored."""
+    B, H, L, D = 4, 2, 700, 64
+    q, k, v = _bhld_inputs(B, H, L, D, torch.bfloat16, seed=7)
+    lengths = torch.tensor([100, 333, 700, 513], dtype=torch.int32)
+    out = ob.attention_bhld(q.cuda(), k.cuda(), v.cuda(), lengths=lengths.cuda(), skip_padded_queries=True,
+                            out_dtype=torch.float32)
+    ob.library().sync_check()
+    want = O.attention_bhld(q.float().numpy(), k.float().numpy(), v.float().numpy(), lengths=lengths.numpy())
+    got = out.cpu().numpy()
+    for b, n in enumerate(lengths.tolist()):
+        _close(got[b, :, :n], want[b, :, :n], f"segment {b} (valid {n})")
+
+
+def test_bhld_block_causal(ob):
+    B, H, L, D = 1, 2, 601, 64
+    q, k, v = _bhld_inputs(B, H, L, D, torch.bfloat16, seed=11)
+    lengths = torch.tensor([590], dtype=torch.int32)
+    out = ob.attention_bhld(q.cuda(), k.cuda(), v.cuda(), lengths=lengths.cuda(), block=200,
+                            out_dtype=torch.float32)
+    ob.library().sync_check()
+    want = O.attention_bhld(q.float().numpy(), k.float().numpy(), v.float().numpy(), lengths=lengths.numpy(),
+                            block=200)
+    _close(out.cpu().numpy(), want, "block 200")
+
+
+def test_bhld_bf16_output_dtype(ob):
+    q, k, v = _bhld_inputs(2, 4, 500, 64, torch.bfloat16, seed=5)
+    out = ob.attention_bhld(q.cuda(), k.cuda(), v.cuda())
+    ob.library().sync_check()
+    assert out.dtype == torch.bfloat16
+    want = O.attention_bhld(q.float().numpy(), k.float().numpy(), v.float().numpy())
+    _close(out.float().cpu().numpy(), want, "bf16 out")
+
+
+# Ops::attention on the reference's row-major layout (shapes of
+# tests/native_cuda_attention.cpp:233-245 and tests/native_cpu_attention.cpp:129-134).
+ROW_CASES = [
+    # n, heads, hd, block, valid, fused, dtype
+    (1, 2, 7, 0, 1, False, torch.float32),
+    (129, 2, 7, 0, 129, False, torch.float32),
+    (513, 4, 64, 200, 510, False, torch.float32),
+    (1500, 4, 64, 200, 1497, False, torch.float32),
+    (401, 2, 7, 7, 1, False, torch.float32),
+    (17, 3, 7, 5, 11, True, torch.bfloat16),
+    (257, 3, 17, 200, 205, False, torch.float32),
+    (31, 2, 96, 0, 31, True, torch.bfloat16),
+    (576, 16, 96, 0, 576, True, torch.bfloat16),
+    (2049, 2, 96, 0, 2049, True, torch.bfloat16),
+    (300, 2, 64, 0, 300, False, torch.bfloat16),
+    (150, 2, 72, 0, 150, False, torch.bfloat16),
+]
+
+
+@pytest.mark.parametrize("n,heads,hd,block,valid,fused,dtype", ROW_CASES)
+def test_rows_matches_oracle(ob, n, heads, hd, block, valid, fused, dtype):
+    d = heads * hd
+    cols = 3 * d if fused else d
+    q = O.lcg_values(n * cols, 123).reshape(n, cols)
+    k = O.lcg_values(n * d, 456).reshape(n, d)
+    v = O.lcg_values(n * d, 789).reshape(n, d)
+    bf16 = dtype == torch.bfloat16
+    tq = torch.from_numpy(q).to(dtype).cuda()
+    tk = torch.from_numpy(k).to(dtype).cuda()
+    tv = torch.from_numpy(v).to(dtype).cuda()
+    out = ob.attention_rows(tq, tk, tv, heads, block=block, valid=valid, fused=fused, out_dtype=torch.float32)
+    ob.library().sync_check()
+    # The oracle sees the same values the GPU saw (bf16-rounded when bf16), fp32 output.
+    want = O.attention(O.round_bf16(q) if bf16 else q, O.round_bf16(k) if bf16 else k,
+                       O.round_bf16(v) if bf16 else v, heads, block, valid, fused, bf16=False)
+    _close(out.cpu().numpy(), want, f"rows n{n} h{heads} hd{hd} block{block} valid{valid}")
+
+
+@pytest.mark.parametrize("n,hd", [(401, 64), (601, 7), (1025, 64)])
+def test_mask_semantics(ob, n, hd):
+    """tests/native_cuda_attention.cpp:199-218 through the rows entry point."""
+    heads, block, valid = 2, 200, 205
+    d = heads * hd
+    zero = torch.zeros(n, d, dtype=torch.float32)
+    v = torch.tensor([[t + j + 1 for j in range(d)] for t in range(n)], dtype=torch.float32)
+
+    def run(vv):
+        out = ob.attention_rows(zero.cuda(), zero.cuda(), vv.cuda(), heads, block=block, valid=valid)
+        ob.library().sync_check()
+        return out.cpu()
+
+    before = run(v)
+    v2 = v.clone()
+    v2[valid:] = 10000.0
+    invalid_changed = run(v2)
+    assert torch.equal(before, invalid_changed), "invalid keys affected attention"
+    v2[block:valid] = -10000.0
+    future_changed = run(v2)
+    assert torch.equal(before[:block], future_changed[:block]), "a future block affected earlier queries"
+    assert before[-1, -1] != 0 and before[-1, -1] != future_changed[-1, -1], "padded queries lost access"
+
+
+def test_invalid_arguments_fail_loudly(ob):
+    lib = ob.library()
+    q = torch.zeros(1, 1, 8, 60, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ob.NativeError) as e:
+        ob.attention_bhld(q, q, q)  # head_dim 60 is not a multiple of 8
+    assert e.value.status == 4
+    st = lib.lib.omni_b200_attention_bhld(None, None, None, None, 1, 1, 1, 64, 1, 1, None, 0, 0, 0.0, None)
+    assert st == 1 and b"null" in lib.lib.omni_b200_last_error()
