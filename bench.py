@@ -1,0 +1,475 @@
+#!/usr/bin/env python
+"""Benchmark of the omni-tokenizer hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c1|c3|vq_audio|vq_image]
+                    [--impl ours|reference]
+
+Default workload (--config c2): BASELINE config 2, the SigLIP-shaped encoder
+self-attention op -- batch 32, 16 heads, L=729, head_dim 72, fp16 Q/K/V drawn
+N(0,1)*0.5 from a seed -- the configuration BASELINE.json's metric
+("attn TFLOP/s vs B200 BF16 peak") is quoted on.  One step = one attention
+pass over that batch; FLOPs per step = 4*B*H*L^2*D (D = 72, not the padded 80).
+
+* value  -- device-resident inputs, K steps timed with CUDA events between a
+            barrier + synchronize on both sides, max over ranks, whole job.
+* e2e    -- the same metric through the C ABI host-buffer entry point
+            (omni_b200_attention_bhld_host): every step copies Q/K/V from
+            pinned host memory to the device and the output back.
+* roofline -- algorithmic FLOPs per launch / mean kernel duration (CUDA events
+            on the launching stream, measured in this run) vs the measured
+            dense bf16 peak in MEASURED_PEAKS.json.
+* cpu_baseline -- the reference's own CPU attention (src/cpu.cpp compiled into
+            oracle/_ref) on the host cores, on a bounded sample (rank 0, N=1).
+Under torchrun (N > 1) every rank runs its own batch (weak scaling); there is
+no collective on the data path (timing uses one all-reduce of a scalar).
+
+--impl reference times the reference's CPU implementation (oracle/_ref, or
+the oracle port when the reference was not compiled here) on the same metric.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+CONFIGS = {
+    "c2": dict(kind="attn", B=32, H=16, L=729, D=72, dtype="f16", std=0.5, seed=1002,
+               workload="SigLIP-shaped encoder self-attention op (BASELINE config 2)"),
+    "c1": dict(kind="attn", B=1, H=20, L=1500, D=64, dtype="bf16", std=1.0, seed=1001,
+               workload="Whisper-shaped encoder self-attention op (BASELINE config 1)"),
+    "c3": dict(kind="attn", B=64, H=20, L=1500, D=64, dtype="bf16", std=1.0, seed=1003, varlen=(100, 1500),
+               workload="variable-length audio attention batch, key-padding mask (BASELINE config 3)"),
+    "vq_audio": dict(kind="vq", N=24000, K=16384, dim=64, seed=1010,
+                     workload="VQ argmin op, audio-shaped (x 24000x64 vs codebook 16384x64, bf16)"),
+    "vq_image": dict(kind="vq", N=373248, K=16384, dim=32, seed=1011,
+                     workload="VQ argmin op, image-shaped (x 373248x32 vs codebook 16384x32, bf16)"),
+}
+METRIC = "attn TFLOP/s vs B200 BF16 peak"
+L2_BYTES = 126 * 1024 * 1024
+
+
+def load_package():
+    import importlib.util
+
+    name = "omni_tokenizer_b200"
+    if name in sys.modules:
+        return sys.modules[name]
+    pkg = ROOT / "omni-tokenizer_b200"
+    spec = importlib.util.spec_from_file_location(name, pkg / "__init__.py", submodule_search_locations=[str(pkg)])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def peaks():
+    try:
+        data = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        return data, "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML (read only)."""
+
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x2: "applications_clocks_setting",
+               0x10: "sync_boost"}
+
+    def __init__(self, cuda_index):
+        self.samples = []
+        self.ok = False
+        self._stop = threading.Event()
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            handle = None
+            try:
+                import torch
+
+                props = torch.cuda.get_device_properties(cuda_index)
+                bus = "%08x:%02x:%02x.0" % (props.pci_domain_id, props.pci_bus_id, props.pci_device_id)
+                handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+            except Exception:
+                handle = pynvml.nvmlDeviceGetHandleByIndex(cuda_index)
+            self.h = handle
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.max_mhz = None
+
+    def _reasons(self):
+        nv = self.nv
+        fn = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        return fn(self.h)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                mhz = self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)
+                self.samples.append((time.perf_counter(), mhz, self._reasons()))
+            except Exception:
+                pass
+            time.sleep(0.01)
+
+    def start(self):
+        if self.ok:
+            self.thread = threading.Thread(target=self._run, daemon=True)
+            self.thread.start()
+
+    def stop(self):
+        if self.ok:
+            self._stop.set()
+            self.thread.join()
+
+    def summary(self, t0, t1):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"], "samples": 0}
+        inside = [s for s in self.samples if t0 <= s[0] <= t1]
+        if not inside:  # a short region: take the samples nearest to it
+            inside = sorted(self.samples, key=lambda s: min(abs(s[0] - t0), abs(s[0] - t1)))[:3]
+        bits = 0
+        for _, _, r in inside:
+            bits |= r
+        names = sorted({name for b, name in self.REASONS.items() if bits & b})
+        return {"sm_mhz": statistics.median([s[1] for s in inside]) if inside else None,
+                "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(inside)}
+
+
+# ------------------------------------------------------------------ inputs
+def attn_inputs(cfg, rank):
+    import torch
+
+    B, H, L, D = cfg["B"], cfg["H"], cfg["L"], cfg["D"]
+    g = torch.Generator().manual_seed(cfg["seed"] + 7919 * rank)
+    dt = torch.float16 if cfg["dtype"] == "f16" else torch.bfloat16
+    qkv = [(torch.randn(B, H, L, D, generator=g) * cfg["std"]).to(dt).pin_memory() for _ in range(3)]
+    lengths = None
+    if cfg.get("varlen"):
+        rng = np.random.default_rng(cfg["seed"] + 7919 * rank)
+        lo, hi = cfg["varlen"]
+        lengths = torch.from_numpy(rng.integers(lo, hi + 1, size=B).astype(np.int32))
+    return qkv, lengths
+
+
+def attn_flops(cfg, lengths):
+    H, D, L, B = cfg["H"], cfg["D"], cfg["L"], cfg["B"]
+    if lengths is not None:
+        return 4.0 * H * D * float(np.sum(lengths.numpy().astype(np.float64) ** 2))
+    return 4.0 * B * H * L * L * D
+
+
+def vq_inputs(cfg, rank):
+    import torch
+
+    g = torch.Generator().manual_seed(cfg["seed"] + 7919 * rank)
+    x = torch.randn(cfg["N"], cfg["dim"], generator=g).to(torch.bfloat16).pin_memory()
+    cb = torch.randn(cfg["K"], cfg["dim"], generator=g).to(torch.bfloat16).pin_memory()
+    return x, cb
+
+
+# ------------------------------------------------------------------ CPU side
+def cpu_reference_sample(cfg, budget_s, items=None):
+    """Time the reference CPU attention / quantize on a bounded sample.
+
+    Returns (flops_or_work, seconds, threads, kind, sample_text)."""
+    from oracle import oracle as O
+
+    kind = "reference" if O.ref_available() else "port"
+    impl = "ref" if kind == "reference" else "oracle"
+    threads = O.cpu_threads()
+    rng = np.random.default_rng(cfg["seed"])
+    if cfg["kind"] == "attn":
+        H, L, D = cfg["H"], cfg["L"], cfg["D"]
+        done_heads, flops, t_total = 0, 0.0, 0.0
+        lengths = None
+        if cfg.get("varlen"):
+            lo, hi = cfg["varlen"]
+            lengths = rng.integers(lo, hi + 1, size=cfg["B"])
+        max_heads = cfg["B"] * H if items is None else items
+        while done_heads < max_heads and (items is not None or t_total < budget_s or done_heads == 0):
+            b = done_heads // H
+            n = int(lengths[b]) if lengths is not None else L
+            q = (rng.standard_normal((n, D)) * cfg["std"]).astype(np.float32)
+            k = (rng.standard_normal((n, D)) * cfg["std"]).astype(np.float32)
+            v = (rng.standard_normal((n, D)) * cfg["std"]).astype(np.float32)
+            t0 = time.perf_counter()
+            O.attention(q, k, v, 1, 0, n, False, False, impl=impl)
+            t_total += time.perf_counter() - t0
+            flops += 4.0 * n * n * D
+            done_heads += 1
+        sample = f"{done_heads} (item, head) slices of the workload, fp32, src/cpu.cpp Ops::attention"
+        return flops, t_total, threads, kind, sample
+    # VQ: a slice of rows against the full codebook.
+    dim, K = cfg["dim"], cfg["K"]
+    cb = O.round_bf16(rng.standard_normal((K, dim)).astype(np.float32))
+    norms = O.squares(cb, bf16=True)
+    rows, t_total, work = 64, 0.0, 0.0
+    done = chunks = 0
+    while done < cfg["N"] and (chunks < items if items is not None else (t_total < budget_s or chunks == 0)):
+        x = O.round_bf16(rng.standard_normal((rows, dim)).astype(np.float32))
+        t0 = time.perf_counter()
+        O.quantize(x, cb, norms, bf16=True, impl=impl)
+        t_total += time.perf_counter() - t0
+        work += 2.0 * rows * K * dim
+        done += rows
+        chunks += 1
+    return work, t_total, threads, kind, f"{done} rows x {K} codes, bf16 profile, src/cpu.cpp Ops::quantize"
+
+
+# ------------------------------------------------------------------ arms
+def run_reference(args, cfg):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from oracle import oracle as O
+
+    # Size each step's sample so that warmup + steps end within ~2 minutes.
+    probe_work, probe_t, threads, kind, _ = cpu_reference_sample(cfg, 0.0, items=1)
+    per_unit = max(probe_t, 1e-4)
+    budget = 120.0 / max(1, args.steps + args.warmup)
+    total_units = cfg["B"] * cfg["H"] if cfg["kind"] == "attn" else (cfg["N"] + 63) // 64
+    units = max(1, min(total_units, int(budget / per_unit)))
+    for _ in range(args.warmup):
+        cpu_reference_sample(cfg, 0.0, items=units)
+    work, seconds = 0.0, 0.0
+    for _ in range(args.steps):
+        w, s, threads, kind, sample = cpu_reference_sample(cfg, 0.0, items=units)
+        work += w
+        seconds += s
+    value = work / seconds / 1e12
+    unit = "TFLOP/s"
+    line = {
+        "impl": "reference", "metric": METRIC if cfg["kind"] == "attn" else "VQ TFLOP/s", "value": value,
+        "unit": unit, "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * seconds / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+        "config": {"workload": cfg["workload"], "sample_per_step": units},
+        "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": kind, "sample": sample},
+        "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args, cfg):
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    ob = load_package()
+    lib = ob.library()
+    stream = torch.cuda.Stream()
+    sp = stream.cuda_stream
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    if cfg["kind"] == "attn":
+        (hq, hk, hv), lengths = attn_inputs(cfg, rank)
+        q, k, v = (t.cuda() for t in (hq, hk, hv))
+        out = torch.empty_like(q)
+        dl = lengths.cuda() if lengths is not None else None
+        B, H, L, D = cfg["B"], cfg["H"], cfg["L"], cfg["D"]
+        dt = 2 if cfg["dtype"] == "f16" else 1
+        skip = 1 if lengths is not None else 0
+        flops_step = attn_flops(cfg, lengths)
+        launches_per_step = 1
+        in_bytes = 3 * q.numel() * q.element_size()
+        out_bytes = out.numel() * out.element_size()
+
+        def step():
+            lib.check(lib.lib.omni_b200_attention_bhld(
+                q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), B, H, L, D, dt, dt,
+                dl.data_ptr() if dl is not None else None, 0, skip, 0.0, sp))
+
+        hout = torch.empty_like(hq).pin_memory()
+        hlen = lengths.numpy() if lengths is not None else None
+
+        def e2e_step(ctx):
+            ctx.attention_bhld(hq, hk, hv, hout, B, H, L, D, dt, dt, lengths=hlen, skip_padded_queries=skip)
+
+        dtype_name = cfg["dtype"]
+        working_set = in_bytes + out_bytes
+    else:
+        hx, hcb = vq_inputs(cfg, rank)
+        x, cb = hx.cuda(), hcb.cuda()
+        N, K, dim = cfg["N"], cfg["K"], cfg["dim"]
+        norms = torch.empty(K, dtype=torch.bfloat16, device="cuda")
+        lib.check(lib.lib.omni_b200_squares(cb.data_ptr(), norms.data_ptr(), K, dim, 1, 1, sp))
+        ws_bytes = lib.lib.omni_b200_vq_workspace(N, dim, K, 1)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+        ids = torch.empty(N, dtype=torch.int32, device="cuda")
+        flops_step = 2.0 * N * K * dim
+        launches_per_step = 3
+
+        def step():
+            lib.check(lib.lib.omni_b200_vq_argmin(x.data_ptr(), cb.data_ptr(), norms.data_ptr(), ids.data_ptr(),
+                                                  N, dim, K, 1, 0, ws.data_ptr(), ws_bytes, sp))
+
+        hids = torch.empty(N, dtype=torch.int32).pin_memory()
+        in_bytes = hx.numel() * 2 + hcb.numel() * 2
+        out_bytes = N * 4
+
+        def e2e_step(ctx):
+            ctx.vq_argmin(hx, hcb, hids, N, dim, K, profile=1, ids_u16=False)
+
+        dtype_name = "bf16"
+        working_set = in_bytes + out_bytes
+
+    # ---- warm-up
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            step()
+    lib.sync_check(sp)
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    # ---- timed region (device-resident inputs)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    barrier()
+    t_wall0 = time.perf_counter()
+    with torch.cuda.stream(stream):
+        ev[0].record(stream)
+        for _ in range(args.steps):
+            step()
+        ev[1].record(stream)
+    stream.synchronize()
+    barrier()
+    t_wall1 = time.perf_counter()
+    lib.sync_check(sp)
+    elapsed = ev[0].elapsed_time(ev[1]) / 1e3
+
+    # ---- per-launch duration of the dominant kernel (events around single launches)
+    pairs = []
+    with torch.cuda.stream(stream):
+        for _ in range(min(args.steps, 50)):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            step()
+            b.record(stream)
+            pairs.append((a, b))
+    stream.synchronize()
+    launch_s = statistics.mean(a.elapsed_time(b) for a, b in pairs) / 1e3
+    sampler.stop()
+    clocks = sampler.summary(t_wall0, t_wall1)
+
+    # ---- end to end through the host-buffer C ABI
+    e2e_steps = max(3, min(args.steps, 30))
+    with ob.Context(local) as ctx:
+        e2e_step(ctx)  # allocate buffers
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            e2e_step(ctx)
+        e2e_elapsed = time.perf_counter() - t0
+    barrier()
+
+    if dist is not None:
+        t = torch.tensor([elapsed, e2e_elapsed / e2e_steps, launch_s], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed, e2e_per_step, launch_s = t.tolist()
+    else:
+        e2e_per_step = e2e_elapsed / e2e_steps
+
+    total_flops = flops_step * args.steps * world
+    value = total_flops / elapsed / 1e12
+    e2e_value = flops_step * world / e2e_per_step / 1e12
+    pk, pk_kind = peaks()
+    peak = float(pk.get("bf16_tflops", 1590.0))
+    achieved = flops_step / launch_s / 1e12
+    traffic = None
+    tf = ROOT / "profiles" / "traffic.json"
+    if tf.is_file():
+        try:
+            traffic = json.loads(tf.read_text()).get(args.config)
+        except Exception:
+            traffic = None
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        work, secs, threads, kind, sample = cpu_reference_sample(cfg, args.cpu_seconds)
+        cpu = {"value": work / secs / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": kind, "sample": sample}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC if cfg["kind"] == "attn" else "VQ TFLOP/s (distance GEMM + argmin)",
+            "value": value,
+            "unit": "TFLOP/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": max(args.warmup, 3),
+            "ms_per_step": 1e3 * elapsed / args.steps,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": dtype_name,
+            "data": "synthetic (seeded, BASELINE shapes)",
+            "config": {
+                "workload": cfg["workload"],
+                "config": args.config,
+                "per_gpu_flops_per_step": flops_step,
+                "parallelism": f"item-sharded replicas x{world}" if world > 1 else "single GPU",
+                "l2": f"working set {working_set / 2**20:.0f} MiB vs 126 MiB L2, no flush"
+                      if working_set > L2_BYTES else "working set below L2 size: L2-resident between steps",
+            },
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "peak_source": f"{pk_kind} bf16_tflops (burst)"},
+            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": in_bytes,
+                    "d2h_bytes_per_step": out_bytes},
+            "cpu_baseline": cpu,
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=5.0, help="CPU baseline sample budget")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        return run_reference(args, cfg)
+    return run_ours(args, cfg)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -95,6 +95,30 @@ OMNI_B200_API int omni_b200_vq_argmin(const void *x, const void *codebook, const
                                       int profile, int ids_u16, void *workspace,
                                       size_t workspace_bytes, void *stream);
 
+/* ---- Host-buffer entry points -------------------------------------------
+ * A context owns one CUDA device, one stream and grow-only device buffers
+ * (the role of omni_context in omni-tokenizer src/runtime.cpp:200-211).  The
+ * *_host calls take HOST pointers (pinned memory gives full copy bandwidth),
+ * copy inputs to the device, run the kernel, copy results back and
+ * synchronise.  One call per context at a time: a concurrent call fails with
+ * INVALID_ARGUMENT, as in src/runtime.cpp:152-163. */
+typedef struct omni_b200_context omni_b200_context;
+OMNI_B200_API int omni_b200_context_create(int device, omni_b200_context **out);
+OMNI_B200_API void omni_b200_context_free(omni_b200_context *context);
+/* Peak bytes of device buffers this context has held. */
+OMNI_B200_API uint64_t omni_b200_context_peak_workspace(const omni_b200_context *context);
+/* omni_b200_attention_bhld on host tensors; lengths (optional) is a HOST int32[batch]. */
+OMNI_B200_API int omni_b200_attention_bhld_host(omni_b200_context *context, const void *q,
+                                                const void *k, const void *v, void *out,
+                                                int batch, int heads, int L, int head_dim,
+                                                int dtype, int out_dtype, const int32_t *lengths,
+                                                int block, int skip_padded_queries, float scale);
+/* omni_b200_vq_argmin on host tensors; cbnorm may be NULL (computed on the device). */
+OMNI_B200_API int omni_b200_vq_argmin_host(omni_b200_context *context, const void *x,
+                                           const void *codebook, const void *cbnorm, void *ids,
+                                           size_t rows, size_t dim, size_t codes, int profile,
+                                           int ids_u16);
+
 #ifdef __cplusplus
 }
 #endif

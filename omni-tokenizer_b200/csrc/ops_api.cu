@@ -51,6 +51,8 @@ int *kernel_error_word() {
     return g_err_ptr[dev];
 }
 
+int ctx_fail(int code, const char *msg) { return fail(code, msg); }
+
 int launch_status(int rc, const char *what) {
     if (rc == 0)
         return 0;

@@ -48,6 +48,16 @@ SIGNATURES = {
         [_P, _P, _P, _P, C.c_size_t, C.c_size_t, C.c_size_t, C.c_int, C.c_int, _P, C.c_size_t, _P],
     ),
     "omni_b200_vq_workspace": (C.c_size_t, [C.c_size_t, C.c_size_t, C.c_size_t, C.c_int]),
+    "omni_b200_context_create": (C.c_int, [C.c_int, C.POINTER(_P)]),
+    "omni_b200_context_free": (None, [_P]),
+    "omni_b200_context_peak_workspace": (C.c_uint64, [_P]),
+    "omni_b200_attention_bhld_host": (
+        C.c_int,
+        [_P, _P, _P, _P, _P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _P, C.c_int, C.c_int, C.c_float],
+    ),
+    "omni_b200_vq_argmin_host": (
+        C.c_int, [_P, _P, _P, _P, _P, C.c_size_t, C.c_size_t, C.c_size_t, C.c_int, C.c_int],
+    ),
 }
 
 
@@ -119,6 +129,52 @@ def attention_bhld(q, k, v, out=None, lengths=None, block=0, skip_padded_queries
         _dtype_code(out), lengths.data_ptr() if lengths is not None else None, block,
         int(bool(skip_padded_queries)), float(scale), _stream_ptr(stream)))
     return out
+
+
+class Context:
+    """Host-buffer entry points bound to one device (omni_b200_context)."""
+
+    def __init__(self, device=0, lib=None):
+        self.lib = lib or library()
+        self.handle = C.c_void_p()
+        self.lib.check(self.lib.lib.omni_b200_context_create(int(device), C.byref(self.handle)))
+
+    def close(self):
+        if self.handle:
+            self.lib.lib.omni_b200_context_free(self.handle)
+            self.handle = C.c_void_p()
+
+    __del__ = close
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *_):
+        self.close()
+
+    @property
+    def peak_workspace_bytes(self):
+        return int(self.lib.lib.omni_b200_context_peak_workspace(self.handle))
+
+    def attention_bhld(self, q, k, v, out, batch, heads, L, head_dim, dtype, out_dtype, lengths=None, block=0,
+                       skip_padded_queries=False, scale=0.0):
+        """q, k, v, out, lengths: host addresses (ints) or objects with .ctypes.data / .data_ptr()."""
+        self.lib.check(self.lib.lib.omni_b200_attention_bhld_host(
+            self.handle, _addr(q), _addr(k), _addr(v), _addr(out), batch, heads, L, head_dim, dtype, out_dtype,
+            _addr(lengths) if lengths is not None else None, block, int(bool(skip_padded_queries)), float(scale)))
+
+    def vq_argmin(self, x, codebook, ids, rows, dim, codes, profile=BF16, ids_u16=True, cbnorm=None):
+        self.lib.check(self.lib.lib.omni_b200_vq_argmin_host(
+            self.handle, _addr(x), _addr(codebook), _addr(cbnorm) if cbnorm is not None else None, _addr(ids),
+            rows, dim, codes, profile, int(bool(ids_u16))))
+
+
+def _addr(obj):
+    if isinstance(obj, int):
+        return obj
+    if hasattr(obj, "data_ptr"):
+        return obj.data_ptr()
+    return obj.ctypes.data
 
 
 def attention_rows(q, k, v, heads, block=0, valid=None, fused=False, out_dtype=None, stream=None):
