@@ -95,6 +95,24 @@ OMNI_B200_API int omni_b200_vq_argmin(const void *x, const void *codebook, const
                                       int profile, int ids_u16, void *workspace,
                                       size_t workspace_bytes, void *stream);
 
+/* omni_b200_vq_argmin without caller-provided scratch.  No counterpart in the
+ * reference (its Ops::quantize allocates from the context's Pool).  For callers
+ * that cannot allocate device memory: processes whose HBM is owned by another
+ * allocator (a caching allocator or an engine that reserves nearly all of it),
+ * and streaming callers that must not call cudaMalloc/cudaFree in their serving
+ * loop.  The 8-byte-per-row scratch lives in a fixed device array of 65536
+ * rows (512 KiB per device, held by every GPU that loads this library until
+ * exit); more rows are rejected with INVALID_ARGUMENT.  The caller still passes
+ * x, codebook, cbnorm and ids (same meaning as omni_b200_vq_argmin).  The first
+ * call on a device looks up that device's address of the array
+ * (cudaGetSymbolAddress); make that first call before any stream capture.
+ * Every call shares the one array: the launch re-initialises the rows it uses,
+ * but calls that overlap on the GPU (other streams or threads) race on it. */
+OMNI_B200_API int omni_b200_vq_argmin_noalloc(const void *x, const void *codebook,
+                                              const void *cbnorm, void *ids, size_t rows,
+                                              size_t dim, size_t codes, int profile,
+                                              int ids_u16, void *stream);
+
 /* ---- Host-buffer entry points -------------------------------------------
  * A context owns one CUDA device, one stream and grow-only device buffers
  * (the role of omni_context in omni-tokenizer src/runtime.cpp:200-211).  The
