@@ -41,25 +41,45 @@
 
 namespace omni_b200 {
 
+#ifndef OMNI_FMHA_QBUF
+#define OMNI_FMHA_QBUF (HDP <= 96 ? 2 : 1)
+#endif
+
 template <int HDP> struct FmhaShape {
     static constexpr int C0 = HDP < 64 ? HDP : 64; // chunk 0 width (elements)
     static constexpr int C1 = HDP - C0;            // chunk 1 width: 0, 16, 32 or 64
     static constexpr int ROW0 = C0 * 2;            // bytes per row of chunk 0
     static constexpr int ROW1 = C1 * 2;
     static constexpr int CH0_BYTES = 128 * ROW0;
-    static constexpr int TILE_BYTES = 128 * HDP * 2; // one 128-row tile
-    static constexpr int STAGES = HDP <= 96 ? 3 : 2;
+    static constexpr int TILE_BYTES = 128 * HDP * 2; // one 128-row Q or K tile
+    // V tiles keep chunk 1 as a full 64-column 128-byte-swizzle atom (zero
+    // filled past the head dim) so that O += P V is ONE MMA of N = HDP per
+    // 16-key step: its two MN atoms are LBO = 16 KB apart.
+    static constexpr int V_BYTES = HDP > 64 ? 2 * 128 * 128 : TILE_BYTES;
+    static constexpr int V_CH0 = 128 * ROW0;
+    static constexpr int QBUF = OMNI_FMHA_QBUF;   // Q buffers (2: next item prefetch)
+    static constexpr int BUDGET = 226 * 1024;
+    static constexpr int STAGES_RAW = (BUDGET - QBUF * 2 * TILE_BYTES) / (TILE_BYTES + V_BYTES);
+    static constexpr int STAGES = STAGES_RAW > 4 ? 4 : STAGES_RAW;
     static constexpr int KSTEPS = HDP / 16;
-    static constexpr int BAR_BYTES = 256;
+    static constexpr int BAR_BYTES = 512;
     // At least 120 KB so that one CTA (which allocates all 512 TMEM columns)
     // occupies an SM by itself.
-    static constexpr int SMEM_RAW = (2 + 2 * STAGES) * TILE_BYTES + BAR_BYTES + 1024;
+    static constexpr int SMEM_RAW =
+        QBUF * 2 * TILE_BYTES + STAGES * (TILE_BYTES + V_BYTES) + BAR_BYTES + 1024;
     static constexpr int SMEM_BYTES = SMEM_RAW > 120 * 1024 ? SMEM_RAW : 120 * 1024;
     static_assert(C1 == 0 || C1 == 16 || C1 == 32 || C1 == 64, "unsupported head dim padding");
     static_assert(HDP % 16 == 0, "head dim padding must be a multiple of 16");
+    static_assert(STAGES >= 2, "K/V ring needs two stages");
 };
 
-constexpr int kThreads = 320;
+// 12 warps: 0-3 softmax tile 0, 4-7 softmax tile 1, 8 TMA producer, 9 MMA
+// issuer / TMEM owner, 10-11 idle.  Registers are rebalanced with setmaxnreg:
+// launch 168/thread; softmax warpgroups grow to 208, warpgroup 2 shrinks to
+// 88 (208 + 208 + 88 = 504 = 3*168 per SM sub-partition and lane).
+constexpr int kThreads = 384;
+constexpr int kSoftmaxRegs = 208;
+constexpr int kControlRegs = 88;
 
 // Loads one 128-row tile (both chunks) of a (token, head, batch) tensor.
 template <int HDP>
@@ -81,10 +101,40 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi, bool bf16) {
     return *reinterpret_cast<uint32_t *>(&v);
 }
 
+// Packed fp32 arithmetic (two lanes per instruction).
+__device__ __forceinline__ void ffma2(float &d0, float &d1, float a0, float a1, float b0, float b1,
+                                      float c0, float c1) {
+    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d0), "=f"(d1)
+        : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+__device__ __forceinline__ void fadd2(float &d0, float &d1, float a0, float a1, float b0,
+                                      float b1) {
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d0), "=f"(d1)
+        : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+template <int N> __device__ __forceinline__ void setmaxnreg_inc() {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N> __device__ __forceinline__ void setmaxnreg_dec() {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // Drain wait: bounded by time only (does not give up early on other threads'
 // errors), used so that no TMA write or MMA is still in flight when the CTA
 // releases its shared memory and TMEM.
-__device__ __noinline__ void wait_drain(uint64_t *bar, uint32_t parity, int *err) {
+__device__ __forceinline__ void wait_drain(uint64_t *bar, uint32_t parity, int *err) {
     const uint32_t a = smem_u32(bar);
     const uint64_t start = globaltimer_ns();
     while (!mbar_try_wait(a, parity)) {
@@ -95,59 +145,71 @@ __device__ __noinline__ void wait_drain(uint64_t *bar, uint32_t parity, int *err
     }
 }
 
+// One work item = 256 query rows of one (batch, head).
+struct Item {
+    int b, h, q0, valid, T; // T = KV tiles the item needs (0: write zeros)
+    bool skip;              // nothing to do (rows past the end / padded-query skip)
+};
+
+__device__ __forceinline__ Item decode_item(const FmhaParams &p, int u) {
+    const int qblocks = (p.L + 255) / 256;
+    Item it;
+    const int bh = u / qblocks;
+    it.q0 = (u - bh * qblocks) * 256;
+    it.b = bh / p.heads;
+    it.h = bh - it.b * p.heads;
+    int valid = p.lengths ? p.lengths[it.b] : p.valid;
+    valid = valid < p.L ? valid : p.L;
+    it.valid = valid < 0 ? 0 : valid;
+    it.skip = it.q0 >= p.L || (p.skip_padded_q && it.q0 >= it.valid);
+    const int last_row = min(it.q0 + 255, p.L - 1);
+    int kv_limit = it.valid;
+    if (p.block > 0)
+        kv_limit = min(kv_limit, (last_row / p.block + 1) * p.block);
+    it.T = (kv_limit + 127) / 128;
+    return it;
+}
+
 template <int HDP, bool BF16>
 __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_constant__ FmhaParams p) {
     using S = FmhaShape<HDP>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    uint8_t *sQ = smem;
-    uint8_t *sK = sQ + 2 * S::TILE_BYTES;
-    uint8_t *sV = sK + S::STAGES * S::TILE_BYTES;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(sV + S::STAGES * S::TILE_BYTES);
-    uint64_t *q_full = bars;
-    uint64_t *k_full = bars + 1;
-    uint64_t *k_empty = k_full + S::STAGES;
-    uint64_t *v_full = k_empty + S::STAGES;
-    uint64_t *v_empty = v_full + S::STAGES;
-    uint64_t *s_full = v_empty + S::STAGES; // [2]
-    uint64_t *p_full = s_full + 2;          // [2]
-    uint64_t *o_done = p_full + 2;
-    uint64_t *drain = o_done + 1;
+    uint8_t *sQ = smem;                                   // [QBUF][2 tiles]
+    uint8_t *sK = sQ + S::QBUF * 2 * S::TILE_BYTES;       // [STAGES]
+    uint8_t *sV = sK + S::STAGES * S::TILE_BYTES;         // [STAGES]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sV + S::STAGES * S::V_BYTES);
+    uint64_t *q_full = bars;                  // [2]
+    uint64_t *q_empty = bars + 2;             // [2]
+    uint64_t *k_full = bars + 4;              // [STAGES]
+    uint64_t *k_empty = k_full + S::STAGES;   // [STAGES]
+    uint64_t *v_full = k_empty + S::STAGES;   // [STAGES]
+    uint64_t *v_empty = v_full + S::STAGES;   // [STAGES]
+    uint64_t *s_full = v_empty + S::STAGES;   // [2]
+    uint64_t *p_full = s_full + 2;            // [2]
+    uint64_t *o_full = p_full + 2;
+    uint64_t *drain = o_full + 1;
     uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(drain + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int h = blockIdx.y, b = blockIdx.z;
-    const int L = p.L;
-    const int q0 = blockIdx.x * 256;
-    int valid = p.lengths ? p.lengths[b] : p.valid;
-    valid = valid < L ? valid : L;
-    if (valid < 0)
-        valid = 0;
-    if (q0 >= L || (p.skip_padded_q && q0 >= valid))
-        return; // uniform for the whole CTA, before any barrier or TMEM use
-
-    // Keys this CTA needs: the largest limit(t) over its rows (limit grows with t).
-    const int last_row = min(q0 + 255, L - 1);
-    int kv_limit = valid;
-    if (p.block > 0)
-        kv_limit = min(kv_limit, (last_row / p.block + 1) * p.block);
-    const int T = (kv_limit + 127) / 128;
+    const int items = p.batch * p.heads * ((p.L + 255) / 256);
     int *err = p.err;
 
     if (threadIdx.x == 0) {
-        mbar_init(q_full, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&q_full[i], 1);
+            mbar_init(&q_empty[i], 1);
+            mbar_init(&s_full[i], 1);
+            mbar_init(&p_full[i], 128);
+        }
         for (int s = 0; s < S::STAGES; ++s) {
             mbar_init(&k_full[s], 1);
             mbar_init(&k_empty[s], 1);
             mbar_init(&v_full[s], 1);
             mbar_init(&v_empty[s], 1);
         }
-        mbar_init(&s_full[0], 1);
-        mbar_init(&s_full[1], 1);
-        mbar_init(&p_full[0], 128);
-        mbar_init(&p_full[1], 128);
-        mbar_init(o_done, 1);
+        mbar_init(o_full, 1);
         mbar_init(drain, 1);
         fence_mbarrier_init();
     }
@@ -159,211 +221,313 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_holder;
+    if (tmem != 0) {
+        // Unexpected: the MMA issuer relies on a whole-TMEM allocation at 0.
+        if (threadIdx.x == 0)
+            atomicOr(err, kErrWaitDrain);
+        __syncthreads();
+        if (warp == 9)
+            tmem_dealloc(tmem, 512);
+        return;
+    }
 
-    if (warp == 8) {
-        // ------------------------------------------------------ TMA producer
-        if (lane == 0 && T > 0) {
-            tma_prefetch_desc(&p.tq0);
-            tma_prefetch_desc(&p.tk0);
-            tma_prefetch_desc(&p.tv0);
-            mbar_arrive_expect_tx(q_full, 2 * S::TILE_BYTES);
-            load_tile<HDP>(sQ, &p.tq0, &p.tq1, q_full, q0, h, b);
-            load_tile<HDP>(sQ + S::TILE_BYTES, &p.tq0, &p.tq1, q_full, q0 + 128, h, b);
-            int issued_k = 0, issued_v = 0;
-            for (int j = 0; j < T; ++j) {
-                const int st = j % S::STAGES;
-                const uint32_t ph = (j / S::STAGES) & 1;
-                if (!mbar_wait(&k_empty[st], ph ^ 1, err, kErrWaitEmpty))
+    if (warp >= 8) {
+        setmaxnreg_dec<kControlRegs>();
+        if (warp == 8) {
+            // -------------------------------------------------- TMA producer
+            // The whole warp runs this loop (warp-uniform state); one elected
+            // lane issues each barrier arrive and TMA copy.
+            if (elect_one()) {
+                tma_prefetch_desc(&p.tq0);
+                tma_prefetch_desc(&p.tk0);
+                tma_prefetch_desc(&p.tv0);
+            }
+            int nq = 0, kv = 0; // Q loads / K,V tile loads issued by this CTA
+            bool ok = true;
+            for (int u = blockIdx.x; ok && u < items; u += gridDim.x) {
+                const Item it = decode_item(p, u);
+                if (it.skip || it.T == 0)
+                    continue;
+                const int qs = nq % S::QBUF;
+                ok = __all_sync(0xffffffffu, mbar_wait(&q_empty[qs], ((nq / S::QBUF) & 1) ^ 1, err,
+                                                        kErrWaitEmpty));
+                if (!ok)
                     break;
-                mbar_arrive_expect_tx(&k_full[st], S::TILE_BYTES);
-                load_tile<HDP>(sK + st * S::TILE_BYTES, &p.tk0, &p.tk1, &k_full[st], j * 128, h, b);
-                issued_k = j + 1;
-                if (!mbar_wait(&v_empty[st], ph ^ 1, err, kErrWaitEmpty))
-                    break;
-                mbar_arrive_expect_tx(&v_full[st], S::TILE_BYTES);
-                load_tile<HDP>(sV + st * S::TILE_BYTES, &p.tv0, &p.tv1, &v_full[st], j * 128, h, b);
-                issued_v = j + 1;
+                uint8_t *qdst = sQ + qs * 2 * S::TILE_BYTES;
+                if (elect_one()) {
+                    mbar_arrive_expect_tx(&q_full[qs], 2 * S::TILE_BYTES);
+                    load_tile<HDP>(qdst, &p.tq0, &p.tq1, &q_full[qs], it.q0, it.h, it.b);
+                    load_tile<HDP>(qdst + S::TILE_BYTES, &p.tq0, &p.tq1, &q_full[qs], it.q0 + 128,
+                                   it.h, it.b);
+                }
+                __syncwarp();
+                ++nq;
+                for (int j = 0; j < it.T; ++j, ++kv) {
+                    const int st = kv % S::STAGES;
+                    const uint32_t ph = (kv / S::STAGES) & 1;
+                    ok = __all_sync(0xffffffffu, mbar_wait(&k_empty[st], ph ^ 1, err, kErrWaitEmpty));
+                    if (!ok)
+                        break;
+                    if (elect_one()) {
+                        mbar_arrive_expect_tx(&k_full[st], S::TILE_BYTES);
+                        load_tile<HDP>(sK + st * S::TILE_BYTES, &p.tk0, &p.tk1, &k_full[st],
+                                       j * 128, it.h, it.b);
+                    }
+                    __syncwarp();
+                    ok = __all_sync(0xffffffffu, mbar_wait(&v_empty[st], ph ^ 1, err, kErrWaitEmpty));
+                    if (!ok) {
+                        ++kv; // the K load above was issued
+                        break;
+                    }
+                    if (elect_one()) {
+                        mbar_arrive_expect_tx(&v_full[st], S::V_BYTES);
+                        uint8_t *vdst = sV + st * S::V_BYTES;
+                        tma_load_4d(vdst, &p.tv0, &v_full[st], 0, j * 128, it.h, it.b);
+                        if constexpr (HDP > 64)
+                            tma_load_4d(vdst + S::V_CH0, &p.tv1, &v_full[st], 64, j * 128, it.h,
+                                        it.b);
+                    }
+                    __syncwarp();
+                }
             }
             // Every issued copy must land before the CTA may exit.
-            wait_drain(q_full, 0, err);
-            for (int j = issued_k - S::STAGES < 0 ? 0 : issued_k - S::STAGES; j < issued_k; ++j)
-                wait_drain(&k_full[j % S::STAGES], (j / S::STAGES) & 1, err);
-            for (int j = issued_v - S::STAGES < 0 ? 0 : issued_v - S::STAGES; j < issued_v; ++j)
-                wait_drain(&v_full[j % S::STAGES], (j / S::STAGES) & 1, err);
-        }
-        __syncwarp();
-    } else if (warp == 9) {
-        // ------------------------------------------------------ MMA issuer
-        if (lane == 0 && T > 0) {
+            for (int n = nq - S::QBUF < 0 ? 0 : nq - S::QBUF; n < nq; ++n)
+                wait_drain(&q_full[n % S::QBUF], (n / S::QBUF) & 1, err);
+            for (int n = kv - S::STAGES < 0 ? 0 : kv - S::STAGES; n < kv; ++n) {
+                wait_drain(&k_full[n % S::STAGES], (n / S::STAGES) & 1, err);
+                if (ok || n + 1 < kv)
+                    wait_drain(&v_full[n % S::STAGES], (n / S::STAGES) & 1, err);
+            }
+        } else if (warp == 9) {
+            // ---------------------------------------------------- MMA issuer
+            // The whole warp runs this loop with warp-uniform values; one
+            // elected lane issues each tcgen05.mma / tcgen05.commit.
             constexpr uint32_t idesc_qk = make_idesc_f16(128, 128, BF16, false);
-            constexpr uint32_t idesc_pv0 = make_idesc_f16(128, S::C0, BF16, true);
-            constexpr uint32_t idesc_pv1 = make_idesc_f16(128, S::C1 > 0 ? S::C1 : 16, BF16, true);
+            constexpr uint32_t idesc_pv = make_idesc_f16(128, HDP, BF16, true);
             constexpr uint32_t lay0 = layout_for_row_bytes(S::ROW0);
             constexpr uint32_t lay1 = layout_for_row_bytes(S::ROW1 > 0 ? S::ROW1 : 32);
             const uint32_t sq = smem_u32(sQ), sk = smem_u32(sK), sv = smem_u32(sV);
-            auto qk = [&](int i, int st) {
+            // Descriptors are advanced by adding (byte offset >> 4) to the start
+            // address field; the K-step loops stay rolled so that the issuing
+            // thread does not keep every descriptor live in registers.
+            const uint32_t leader = elect_one() ? 1u : 0u;
+            // All 512 TMEM columns belong to this CTA, so the allocation starts
+            // at lane 0 / column 0: use the constant (warp-uniform, so MMA
+            // operands stay in uniform registers); the start of the kernel
+            // checked that the allocator returned exactly that address.
+            const uint32_t tmem = 0;
+            auto commit = [&](uint64_t *bar) { tc_commit_if(leader, bar); };
+            auto qk = [&](uint32_t qbase, int i, int st) {
                 const uint32_t d = tmem + i * 128;
-#pragma unroll
-                for (int kk = 0; kk < S::KSTEPS; ++kk) {
-                    const int e = kk * 16;
-                    const bool c1 = e >= S::C0;
-                    const uint32_t rowb = c1 ? S::ROW1 : S::ROW0;
-                    const uint32_t off = (c1 ? S::CH0_BYTES : 0) + (e - (c1 ? S::C0 : 0)) * 2;
-                    const uint64_t ad = make_smem_desc(sq + i * S::TILE_BYTES + off, 16, 8 * rowb,
-                                                       c1 ? lay1 : lay0);
-                    const uint64_t bd = make_smem_desc(sk + st * S::TILE_BYTES + off, 16, 8 * rowb,
-                                                       c1 ? lay1 : lay0);
-                    umma_ss(d, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+                const uint64_t a0 = make_smem_desc(qbase + i * S::TILE_BYTES, 16, 8 * S::ROW0, lay0);
+                const uint64_t b0 = make_smem_desc(sk + st * S::TILE_BYTES, 16, 8 * S::ROW0, lay0);
+#pragma unroll 1
+                for (int kk = 0; kk < S::C0 / 16; ++kk)
+                    umma_ss_if(leader, d, a0 + 2 * kk, b0 + 2 * kk, idesc_qk, kk > 0 ? 1u : 0u);
+                if constexpr (S::C1 > 0) {
+                    const uint64_t a1 = make_smem_desc(qbase + i * S::TILE_BYTES + S::CH0_BYTES, 16,
+                                                       8 * S::ROW1, lay1);
+                    const uint64_t b1 = make_smem_desc(sk + st * S::TILE_BYTES + S::CH0_BYTES, 16,
+                                                       8 * S::ROW1, lay1);
+#pragma unroll 1
+                    for (int kk = 0; kk < S::C1 / 16; ++kk)
+                        umma_ss_if(leader, d, a1 + 2 * kk, b1 + 2 * kk, idesc_qk, 1u);
                 }
             };
             auto pv = [&](int i, int st, bool accumulate) {
                 const uint32_t d = tmem + 256 + i * 128;
                 const uint32_t a = tmem + i * 128;
-                const uint32_t vb = sv + st * S::TILE_BYTES;
-#pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {
-                    const uint32_t acc = (accumulate || kk > 0) ? 1u : 0u;
-                    const uint64_t b0 = make_smem_desc(vb + kk * 16 * S::ROW0, S::CH0_BYTES,
-                                                       8 * S::ROW0, lay0);
-                    umma_ts(d, a + kk * 8, b0, idesc_pv0, acc);
-                    if constexpr (S::C1 > 0) {
-                        const uint64_t b1 = make_smem_desc(vb + S::CH0_BYTES + kk * 16 * S::ROW1,
-                                                           S::TILE_BYTES, 8 * S::ROW1, lay1);
-                        umma_ts(d + S::C0, a + kk * 8, b1, idesc_pv1, acc);
-                    }
-                }
+                const uint32_t vb = sv + st * S::V_BYTES;
+                constexpr uint32_t vrow = HDP >= 64 ? 128 : S::ROW0;
+                const uint64_t v0 = make_smem_desc(vb, S::V_CH0, 8 * vrow,
+                                                   HDP >= 64 ? kLayoutSW128 : lay0);
+#pragma unroll 1
+                for (int kk = 0; kk < 8; ++kk)
+                    umma_ts_if(leader, d, a + kk * 8,
+                               v0 + static_cast<uint64_t>((kk * 16 * vrow) >> 4), idesc_pv,
+                               (accumulate || kk > 0) ? 1u : 0u);
             };
-            bool ok = mbar_wait(q_full, 0, err, kErrWaitQ) && mbar_wait(&k_full[0], 0, err, kErrWaitK);
-            if (ok) {
-                tc_fence_after();
-                qk(0, 0);
-                tc_commit(&s_full[0]);
-                qk(1, 0);
-                tc_commit(&s_full[1]);
-                tc_commit(&k_empty[0]);
-            }
-            for (int j = 0; ok && j < T; ++j) {
-                const int st = j % S::STAGES;
-                const uint32_t ph = (j / S::STAGES) & 1;
-                const int j1 = j + 1, st1 = j1 % S::STAGES;
-                const uint32_t ph1 = (j1 / S::STAGES) & 1;
-                if (!(ok = mbar_wait(&v_full[st], ph, err, kErrWaitV)))
+            int nq = 0, kv = 0, n_items = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; ok && u < items; u += gridDim.x) {
+                const Item it = decode_item(p, u);
+                if (it.skip || it.T == 0)
+                    continue;
+                const int qs = nq % S::QBUF;
+                const uint32_t qbase = sq + qs * 2 * S::TILE_BYTES;
+                if (!(ok = __all_sync(0xffffffffu, mbar_wait(&q_full[qs], (nq / S::QBUF) & 1, err, kErrWaitQ))))
                     break;
-                if (!(ok = mbar_wait(&p_full[0], j & 1, err, kErrWaitP)))
-                    break;
-                tc_fence_after();
-                pv(0, st, j > 0);
-                if (j1 < T) {
-                    if (!(ok = mbar_wait(&k_full[st1], ph1, err, kErrWaitK)))
+                {
+                    const int st = kv % S::STAGES;
+                    if (!(ok = __all_sync(0xffffffffu, mbar_wait(&k_full[st], (kv / S::STAGES) & 1, err, kErrWaitK))))
                         break;
                     tc_fence_after();
-                    qk(0, st1);
-                    tc_commit(&s_full[0]);
+                    qk(qbase, 0, st);
+                    commit(&s_full[0]);
+                    qk(qbase, 1, st);
+                    commit(&s_full[1]);
+                    commit(&k_empty[st]);
                 }
-                if (!(ok = mbar_wait(&p_full[1], j & 1, err, kErrWaitP)))
+                for (int j = 0; j < it.T; ++j) {
+                    const int g = kv + j, st = g % S::STAGES;
+                    const uint32_t ph = (g / S::STAGES) & 1;
+                    const int g1 = g + 1, st1 = g1 % S::STAGES;
+                    const uint32_t ph1 = (g1 / S::STAGES) & 1;
+                    const bool more = j + 1 < it.T;
+                    if (!(ok = __all_sync(0xffffffffu, mbar_wait(&v_full[st], ph, err, kErrWaitV))))
+                        break;
+                    if (!(ok = __all_sync(0xffffffffu, mbar_wait(&p_full[0], g & 1, err, kErrWaitP))))
+                        break;
+                    tc_fence_after();
+                    pv(0, st, j > 0);
+                    if (more) {
+                        if (!(ok = __all_sync(0xffffffffu, mbar_wait(&k_full[st1], ph1, err, kErrWaitK))))
+                            break;
+                        tc_fence_after();
+                        qk(qbase, 0, st1);
+                        commit(&s_full[0]);
+                    }
+                    if (!(ok = __all_sync(0xffffffffu, mbar_wait(&p_full[1], g & 1, err, kErrWaitP))))
+                        break;
+                    tc_fence_after();
+                    pv(1, st, j > 0);
+                    commit(&v_empty[st]);
+                    if (more) {
+                        qk(qbase, 1, st1);
+                        commit(&s_full[1]);
+                        commit(&k_empty[st1]);
+                    }
+                }
+                if (!ok)
                     break;
-                tc_fence_after();
-                pv(1, st, j > 0);
-                tc_commit(&v_empty[st]);
-                if (j1 < T) {
-                    qk(1, st1);
-                    tc_commit(&s_full[1]);
-                    tc_commit(&k_empty[st1]);
-                }
+                commit(o_full);       // O_0, O_1 of this item are final
+                commit(&q_empty[qs]); // every MMA reading this Q slot is done
+                kv += it.T;
+                ++nq;
+                ++n_items;
             }
-            tc_commit(o_done);
-            tc_commit(drain);
+            commit(drain);
             wait_drain(drain, 0, err);
         }
         __syncwarp();
     } else {
         // ------------------------------------------------- softmax warpgroups
-        const int i = warp >> 2;                    // query tile
-        const int r = ((warp & 3) << 5) + lane;     // TMEM lane == row in tile
-        const int t = q0 + i * 128 + r;             // query token
-        int limit = valid;
-        if (p.block > 0)
-            limit = min(limit, (t / p.block + 1) * p.block);
+        setmaxnreg_inc<kSoftmaxRegs>();
+        const int i = warp >> 2;                // query tile
+        const int r = ((warp & 3) << 5) + lane; // TMEM lane == row in tile
         const uint32_t lane_base = static_cast<uint32_t>((warp & 3) << 5) << 16;
         const uint32_t tS = tmem + lane_base + i * 128;
         const uint32_t tO = tmem + lane_base + 256 + i * 128;
         const float sl2 = p.scale_log2;
-        float m = -INFINITY, l = 0.f;
+        int g = 0, n_items = 0;
         bool ok = true;
-        for (int j = 0; j < T; ++j) {
-            ok = __all_sync(0xffffffffu, mbar_wait(&s_full[i], j & 1, err, kErrWaitS));
+        for (int u = blockIdx.x; ok && u < items; u += gridDim.x) {
+            const Item it = decode_item(p, u);
+            if (it.skip)
+                continue;
+            const int t = it.q0 + i * 128 + r; // query token
+            int limit = it.valid;
+            if (p.block > 0)
+                limit = min(limit, (t / p.block + 1) * p.block);
+            float m = -INFINITY, l = 0.f;
+            for (int j = 0; j < it.T; ++j, ++g) {
+                ok = __all_sync(0xffffffffu, mbar_wait(&s_full[i], g & 1, err, kErrWaitS));
+                if (!ok)
+                    break;
+                tc_fence_after();
+                uint32_t sraw[128];
+                tmem_ld32(tS + 0, *reinterpret_cast<uint32_t(*)[32]>(&sraw[0]));
+                tmem_ld32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(&sraw[32]));
+                tmem_ld32(tS + 64, *reinterpret_cast<uint32_t(*)[32]>(&sraw[64]));
+                tmem_ld32(tS + 96, *reinterpret_cast<uint32_t(*)[32]>(&sraw[96]));
+                tmem_wait_ld();
+                float *s = reinterpret_cast<float *>(sraw);
+                const int kv0 = j * 128;
+                if (kv0 + 128 > limit) {
+#pragma unroll
+                    for (int c = 0; c < 128; ++c)
+                        if (kv0 + c >= limit)
+                            s[c] = -INFINITY;
+                }
+                // Row max: four independent 3-input max chains.
+                float m0 = fmax3(s[0], s[1], s[2]), m1 = fmax3(s[3], s[4], s[5]);
+                float m2 = fmax3(s[6], s[7], s[8]), m3 = fmax3(s[9], s[10], s[11]);
+#pragma unroll
+                for (int c = 12; c < 124; c += 8) {
+                    m0 = fmax3(m0, s[c], s[c + 1]);
+                    m1 = fmax3(m1, s[c + 2], s[c + 3]);
+                    m2 = fmax3(m2, s[c + 4], s[c + 5]);
+                    m3 = fmax3(m3, s[c + 6], s[c + 7]);
+                }
+                m0 = fmax3(m0, s[124], s[125]);
+                m1 = fmax3(m1, s[126], s[127]);
+                const float mt = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+                const float mnew = fmaxf(m, mt * sl2);
+                // Lazy rescale: a row keeps its stale max while P stays below 2^8.
+                const bool grow = mnew > m + 8.0f;
+                const float alpha = (grow && j > 0) ? ex2_approx(m - mnew) : 1.f;
+                if (grow) {
+                    l *= alpha;
+                    m = mnew;
+                }
+                // tcgen05.ld/st are warp-collective: rescale the warp's O rows
+                // together (alpha == 1 for rows whose max did not grow).
+                if (j > 0 && __any_sync(0xffffffffu, grow)) {
+#pragma unroll
+                    for (int c = 0; c < HDP; c += 16) {
+                        uint32_t o[16];
+                        tmem_ld16(tO + c, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int e = 0; e < 16; ++e)
+                            o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+                        tmem_st16(tO + c, o);
+                    }
+                }
+                const float neg_m = -m;
+                // P = 2^(s*scale - m): packed fp32 FMA, MUFU ex2, packed sums.
+                // P pair c is written over sraw[c]: its inputs s[2c], s[2c+1]
+                // (and every s below them) have been consumed by then.
+                float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
+#pragma unroll
+                for (int c = 0; c < 64; c += 2) {
+                    float x0, x1, x2, x3;
+                    ffma2(x0, x1, s[2 * c], s[2 * c + 1], sl2, sl2, neg_m, neg_m);
+                    ffma2(x2, x3, s[2 * c + 2], s[2 * c + 3], sl2, sl2, neg_m, neg_m);
+                    x0 = ex2_approx(x0);
+                    x1 = ex2_approx(x1);
+                    x2 = ex2_approx(x2);
+                    x3 = ex2_approx(x3);
+                    fadd2(a0, a1, a0, a1, x0, x1);
+                    fadd2(b0, b1, b0, b1, x2, x3);
+                    sraw[c] = pack2(x0, x1, BF16);
+                    sraw[c + 1] = pack2(x2, x3, BF16);
+                }
+                l += (a0 + a1) + (b0 + b1);
+                __syncwarp();
+                tmem_st32(tS + 0, *reinterpret_cast<uint32_t(*)[32]>(&sraw[0]));
+                tmem_st32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(&sraw[32]));
+                tmem_wait_st();
+                tc_fence_before();
+                mbar_arrive(&p_full[i]);
+            }
             if (!ok)
                 break;
-            tc_fence_after();
-            uint32_t sraw[128];
-            tmem_ld32(tS + 0, *reinterpret_cast<uint32_t(*)[32]>(&sraw[0]));
-            tmem_ld32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(&sraw[32]));
-            tmem_ld32(tS + 64, *reinterpret_cast<uint32_t(*)[32]>(&sraw[64]));
-            tmem_ld32(tS + 96, *reinterpret_cast<uint32_t(*)[32]>(&sraw[96]));
-            tmem_wait_ld();
-            float *s = reinterpret_cast<float *>(sraw);
-            const int kv0 = j * 128;
-            if (kv0 + 128 > limit) {
-#pragma unroll
-                for (int c = 0; c < 128; ++c)
-                    if (kv0 + c >= limit)
-                        s[c] = -INFINITY;
+            if (it.T > 0) {
+                ok = __all_sync(0xffffffffu, mbar_wait(o_full, n_items & 1, err, kErrWaitO));
+                if (!ok)
+                    break;
+                ++n_items;
+                tc_fence_after();
             }
-            float mt = s[0];
-#pragma unroll
-            for (int c = 1; c < 128; ++c)
-                mt = fmaxf(mt, s[c]);
-            const float mnew = fmaxf(m, mt * sl2);
-            // Lazy rescale: a row keeps its stale max while P stays below 2^8.
-            const bool grow = mnew > m + 8.0f;
-            const float alpha = (grow && j > 0) ? ex2_approx(m - mnew) : 1.f;
-            if (grow) {
-                l *= alpha;
-                m = mnew;
-            }
-            // tcgen05.ld/st are warp-collective: rescale the warp's O rows
-            // together (alpha == 1 for rows whose max did not grow).
-            if (j > 0 && __any_sync(0xffffffffu, grow)) {
-#pragma unroll
-                for (int c = 0; c < HDP; c += 16) {
-                    uint32_t o[16];
-                    tmem_ld16(tO + c, o);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int e = 0; e < 16; ++e)
-                        o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-                    tmem_st16(tO + c, o);
-                }
-            }
-            const float neg_m = -m;
-            float sum = 0.f;
-            uint32_t pk[64];
-#pragma unroll
-            for (int c = 0; c < 64; ++c) {
-                const float p0 = ex2_approx(fmaf(s[2 * c], sl2, neg_m));
-                const float p1 = ex2_approx(fmaf(s[2 * c + 1], sl2, neg_m));
-                sum += p0 + p1;
-                pk[c] = pack2(p0, p1, BF16);
-            }
-            l += sum;
-            __syncwarp();
-            tmem_st32(tS + 0, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
-            tmem_st32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
-            tmem_wait_st();
-            tc_fence_before();
-            mbar_arrive(&p_full[i]);
-        }
-        if (ok && T > 0)
-            ok = __all_sync(0xffffffffu, mbar_wait(o_done, 0, err, kErrWaitO));
-        if (ok) {
-            tc_fence_after();
-            const float inv = (T > 0 && l > 0.f) ? 1.f / l : 0.f;
-            const bool store = t < L;
-            const long long base = b * p.o_sb + h * p.o_sh + static_cast<long long>(t) * p.o_st;
+            const float inv = (it.T > 0 && l > 0.f) ? 1.f / l : 0.f;
+            const bool store = t < p.L;
+            const long long base =
+                it.b * p.o_sb + it.h * p.o_sh + static_cast<long long>(t) * p.o_st;
 #pragma unroll
             for (int c = 0; c < HDP; c += 16) {
                 uint32_t o[16];
-                if (T > 0) {
+                if (it.T > 0) {
                     tmem_ld16(tO + c, o);
                     tmem_wait_ld();
                 } else {
@@ -418,6 +582,7 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                     }
                 }
             }
+            __syncwarp();
         }
         __syncwarp();
     }
@@ -466,7 +631,7 @@ int padded_head_dim(int hd) {
     return -1;
 }
 
-template <int HDP, bool BF16> int launch_typed(FmhaParams &p, int grid_x, cudaStream_t stream) {
+template <int HDP, bool BF16> int launch_typed(FmhaParams &p, int grid, cudaStream_t stream) {
     using S = FmhaShape<HDP>;
     static std::once_flag once;
     static cudaError_t attr = cudaSuccess;
@@ -476,14 +641,13 @@ template <int HDP, bool BF16> int launch_typed(FmhaParams &p, int grid_x, cudaSt
     });
     if (attr != cudaSuccess)
         return static_cast<int>(attr);
-    dim3 grid(grid_x, p.heads, p.batch);
     fmha_fwd_kernel<HDP, BF16><<<grid, kThreads, S::SMEM_BYTES, stream>>>(p);
     return static_cast<int>(cudaGetLastError());
 }
 
-template <int HDP> int launch_hdp(FmhaParams &p, bool bf16, int grid_x, cudaStream_t stream) {
-    return bf16 ? launch_typed<HDP, true>(p, grid_x, stream)
-                : launch_typed<HDP, false>(p, grid_x, stream);
+template <int HDP> int launch_hdp(FmhaParams &p, bool bf16, int grid, cudaStream_t stream) {
+    return bf16 ? launch_typed<HDP, true>(p, grid, stream)
+                : launch_typed<HDP, false>(p, grid, stream);
 }
 
 int fmha_launch(const FmhaArgs &a, cudaStream_t stream) {
@@ -498,9 +662,10 @@ int fmha_launch(const FmhaArgs &a, cudaStream_t stream) {
         (rc = make_map(&p.tv0, a.v_ptr, a.bf16, a.v, w0, 128)))
         return rc;
     if (w1 > 0) {
+        // V's second chunk is always a 64-column box (see FmhaShape::V_BYTES).
         if ((rc = make_map(&p.tq1, a.q_ptr, a.bf16, a.q, w1, 128)) ||
             (rc = make_map(&p.tk1, a.k_ptr, a.bf16, a.k, w1, 128)) ||
-            (rc = make_map(&p.tv1, a.v_ptr, a.bf16, a.v, w1, 128)))
+            (rc = make_map(&p.tv1, a.v_ptr, a.bf16, a.v, 64, 128)))
             return rc;
     }
     p.out = a.out;
@@ -524,7 +689,16 @@ int fmha_launch(const FmhaArgs &a, cudaStream_t stream) {
     const double scale = a.scale > 0 ? a.scale : 1.0 / std::sqrt(static_cast<double>(p.hd));
     p.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
     p.err = a.err;
-    const int grid_x = (p.L + 255) / 256;
+    // Persistent grid: one CTA per SM, each looping over (batch, head, 256-row) items.
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+            sms = 148;
+    }
+    const long long items = static_cast<long long>(p.batch) * p.heads * ((p.L + 255) / 256);
+    const int grid_x = static_cast<int>(items < sms ? items : sms);
     switch (hdp) {
     case 16:
         return launch_hdp<16>(p, a.bf16, grid_x, stream);

@@ -79,7 +79,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // Waits for the phase with the given parity to complete.  Gives up after
 // kWaitLimitNs (recording `code` in *err) or as soon as another thread of the
 // launch has recorded an error; returns false in both cases.
-static __device__ __noinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int code) {
+static __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int code) {
     const uint32_t a = smem_u32(bar);
     if (mbar_try_wait(a, parity))
         return true;
@@ -161,6 +161,32 @@ __device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64
     asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
                  "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
                  "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+                 : "memory");
+}
+
+
+// ------------------------------------------- predicated (elected-lane) issue --
+// The whole warp executes these with warp-uniform operands; only lanes with
+// `issue` != 0 (one elected lane) perform the operation.
+__device__ __forceinline__ void umma_ss_if(uint32_t issue, uint32_t d_tmem, uint64_t a_desc,
+                                           uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.b32 p, %4, 0;\n\tsetp.ne.b32 q, %5, 0;\n\t"
+                 "@q tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+                 "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(issue)
+                 : "memory");
+}
+__device__ __forceinline__ void umma_ts_if(uint32_t issue, uint32_t d_tmem, uint32_t a_tmem,
+                                           uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.b32 p, %4, 0;\n\tsetp.ne.b32 q, %5, 0;\n\t"
+                 "@q tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+                 "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(issue)
+                 : "memory");
+}
+__device__ __forceinline__ void tc_commit_if(uint32_t issue, uint64_t *bar) {
+    asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %1, 0;\n\t"
+                 "@q tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
+                     smem_u32(bar)),
+                 "r"(issue)
                  : "memory");
 }
 
@@ -251,6 +277,16 @@ __host__ __device__ constexpr uint32_t layout_for_row_bytes(int bytes) {
 }
 
 __device__ __forceinline__ uint32_t lane_id() { return threadIdx.x & 31u; }
+
+// One lane of a converged warp: the whole warp executes the issue code with
+// warp-uniform values (so descriptors live in uniform registers) and only the
+// elected lane issues the TMA / tcgen05 instruction.
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred;
+    asm volatile("{\n\t.reg .pred p;\n\telect.sync _|p, 0xffffffff;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(pred));
+    return pred != 0;
+}
 
 __device__ __forceinline__ float ex2_approx(float x) {
     float y;
