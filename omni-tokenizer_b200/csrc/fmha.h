@@ -17,6 +17,7 @@ struct TensorView {
 // Kernel parameters (passed as a __grid_constant__ argument).
 struct FmhaParams {
     CUtensorMap tq0, tq1, tk0, tk1, tv0, tv1; // chunk 0 / chunk 1 tile maps
+    CUtensorMap to0, to1;                     // output tile maps (when o_tma)
     void *out;
     long long o_sb, o_sh, o_st; // output strides in elements (batch, head, token)
     const int *lengths;         // [batch] valid key counts, or nullptr
@@ -26,6 +27,9 @@ struct FmhaParams {
     int skip_padded_q;
     int out_dtype;
     int out_vec;
+    int ones_col; // >= 0: V column holding 1.0 so that O[:, ones_col] = row sum of P
+    int o_tma;    // 1: the output is staged in shared memory and written by TMA
+    int v1_width; // columns of V's second chunk loaded by TMA (0: none)
     float scale_log2;
     int *err;
 };

@@ -55,14 +55,17 @@ template <int HDP> struct FmhaShape {
     // V tiles keep chunk 1 as a full 64-column 128-byte-swizzle atom (zero
     // filled past the head dim) so that O += P V is ONE MMA of N = HDP per
     // 16-key step: its two MN atoms are LBO = 16 KB apart.
-    static constexpr int V_BYTES = HDP > 64 ? 2 * 128 * 128 : TILE_BYTES;
+    // PV output width: one spare column past the head dim for the row-sum
+    // column of ones (64 -> 80, 96 -> 112); O_i occupies HDPO <= 128 columns.
+    static constexpr int HDPO = HDP == 64 ? 80 : HDP == 96 ? 112 : HDP;
+    static constexpr int V_BYTES = HDPO > 64 ? 2 * 128 * 128 : TILE_BYTES;
     static constexpr int V_CH0 = 128 * ROW0;
     static constexpr int QBUF = OMNI_FMHA_QBUF;   // Q buffers (2: next item prefetch)
     static constexpr int BUDGET = 226 * 1024;
     static constexpr int STAGES_RAW = (BUDGET - QBUF * 2 * TILE_BYTES) / (TILE_BYTES + V_BYTES);
     static constexpr int STAGES = STAGES_RAW > 4 ? 4 : STAGES_RAW;
     static constexpr int KSTEPS = HDP / 16;
-    static constexpr int BAR_BYTES = 512;
+    static constexpr int BAR_BYTES = 512 + 2 * 2 * 2 * 128 * 4 + 2 * 2 * 128 * 4;
     // At least 120 KB so that one CTA (which allocates all 512 TMEM columns)
     // occupies an SM by itself.
     static constexpr int SMEM_RAW =
@@ -73,13 +76,17 @@ template <int HDP> struct FmhaShape {
     static_assert(STAGES >= 2, "K/V ring needs two stages");
 };
 
-// 12 warps: 0-3 softmax tile 0, 4-7 softmax tile 1, 8 TMA producer, 9 MMA
-// issuer / TMEM owner, 10-11 idle.  Registers are rebalanced with setmaxnreg:
-// launch 168/thread; softmax warpgroups grow to 208, warpgroup 2 shrinks to
-// 88 (208 + 208 + 88 = 504 = 3*168 per SM sub-partition and lane).
-constexpr int kThreads = 384;
-constexpr int kSoftmaxRegs = 208;
-constexpr int kControlRegs = 88;
+// 20 warps: 0-7 softmax tile 0, 8-15 softmax tile 1 (two warps per TMEM lane
+// quarter, each owning 64 of the 128 score columns), 16 TMA producer, 17 MMA
+// issuer / TMEM owner, 18-19 output stores of tile 0 / tile 1.  Registers are rebalanced with setmaxnreg:
+// launch 96/thread; the softmax warpgroups grow to 104 and the control
+// warpgroup shrinks to 64 (16*104 + 4*64 = 1920 = 20*96 per lane; 4*104 + 64 =
+// 480 <= 512 per SM sub-partition).
+constexpr int kThreads = 640;
+constexpr int kSoftmaxRegs = 104;
+constexpr int kControlRegs = 64;
+constexpr int kProducerWarp = 16;
+constexpr int kMmaWarp = 17;
 
 // Loads one 128-row tile (both chunks) of a (token, head, batch) tensor.
 template <int HDP>
@@ -122,6 +129,58 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
     float d;
     asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
     return d;
+}
+
+// 2^x0, 2^x1 with one packed half-precision MUFU ex2; returns the pair as
+// bf16x2 (bf16) or f16x2, low half = x0.
+__device__ __forceinline__ uint32_t ex2_pair(float x0, float x1, bool bf16) {
+    uint32_t r;
+    if (bf16)
+        asm("{\n\t.reg .b32 t;\n\tcvt.rn.bf16x2.f32 t, %2, %1;\n\tex2.approx.ftz.bf16x2 %0, t;\n\t}"
+            : "=r"(r)
+            : "f"(x0), "f"(x1));
+    else
+        asm("{\n\t.reg .b32 t;\n\tcvt.rn.f16x2.f32 t, %2, %1;\n\tex2.approx.f16x2 %0, t;\n\t}"
+            : "=r"(r)
+            : "f"(x0), "f"(x1));
+    return r;
+}
+
+// 2^x on the FMA pipe for a pair of lanes: round-to-nearest range reduction
+// (adding 1.5 * 2^23 leaves round(x) in the low mantissa bits), a degree-3
+// polynomial for 2^f on [-1/2, 1/2] and exponent insertion by integer add.
+// The coefficients are a relative-error fit made for this kernel (weighted
+// least squares on Chebyshev nodes); max relative error 7.5e-5, below the
+// half-ulp of fp16 and bf16.  Inputs are clamped at -125 so that the exponent
+// add cannot wrap (2^-125 is far below any P that reaches the sum); masked
+// (-inf) scores never take this path.
+__device__ __forceinline__ void exp2_poly2(float &y0, float &y1, float x0, float x1) {
+    constexpr float kRound = 12582912.0f; // 1.5 * 2^23
+    constexpr float c0 = 0.9999280571937561f, c1 = 0.6932610273361206f;
+    constexpr float c2 = 0.2426111102104187f, c3 = 0.05517149344086647f;
+    x0 = fmaxf(x0, -125.f);
+    x1 = fmaxf(x1, -125.f);
+    float t0, t1, j0, j1, f0, f1, p0, p1;
+    fadd2(t0, t1, x0, x1, kRound, kRound);
+    fadd2(j0, j1, t0, t1, -kRound, -kRound);
+    ffma2(f0, f1, j0, j1, -1.f, -1.f, x0, x1);
+    ffma2(p0, p1, f0, f1, c3, c3, c2, c2);
+    ffma2(p0, p1, p0, p1, f0, f1, c1, c1);
+    ffma2(p0, p1, p0, p1, f0, f1, c0, c0);
+    y0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
+    y1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
+}
+
+// Which pairs of a 128-score row use the polynomial (the rest use MUFU ex2):
+// 3 of every 8, balancing the MUFU, FMA and issue budgets of a sub-partition.
+#ifndef OMNI_FMHA_POLY
+#define OMNI_FMHA_POLY 0
+#endif
+#ifndef OMNI_FMHA_TURN
+#define OMNI_FMHA_TURN 1
+#endif
+__device__ __forceinline__ constexpr bool poly_pair(int pair) {
+    return OMNI_FMHA_POLY && ((pair & 7) == 1 || (pair & 7) == 4 || (pair & 7) == 6);
 }
 
 template <int N> __device__ __forceinline__ void setmaxnreg_inc() {
@@ -190,7 +249,13 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
     uint64_t *p_full = s_full + 2;            // [2]
     uint64_t *o_full = p_full + 2;
     uint64_t *drain = o_full + 1;
-    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(drain + 1);
+    uint64_t *xbar = drain + 1;               // [2] half-row max exchange, per tile
+    uint64_t *lbar = xbar + 2;                // [2] half-row sum exchange, per tile
+    uint64_t *ebar = lbar + 2;                // [2] output tile staged, per tile
+    uint64_t *turn = ebar + 2;                // [2] exp-phase hand-off between the tiles
+    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(turn + 2);
+    float *xmax = reinterpret_cast<float *>(tmem_holder + 4); // [2 parity][2 tile][2 half][128]
+    float *xsum = xmax + 2 * 2 * 2 * 128;                       // [2 tile][2 half][128]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int items = p.batch * p.heads * ((p.L + 255) / 256);
@@ -199,9 +264,15 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
     if (threadIdx.x == 0) {
         for (int i = 0; i < 2; ++i) {
             mbar_init(&q_full[i], 1);
-            mbar_init(&q_empty[i], 1);
+            // Released by the MMA warp (TMA-free output) or by the two tiles'
+            // output stores, which stage O in this Q slot.
+            mbar_init(&q_empty[i], p.o_tma ? 2 : 1);
+            mbar_init(&ebar[i], 256);
+            mbar_init(&turn[i], 256);
             mbar_init(&s_full[i], 1);
-            mbar_init(&p_full[i], 128);
+            mbar_init(&p_full[i], 256);
+            mbar_init(&xbar[i], 256);
+            mbar_init(&lbar[i], 256);
         }
         for (int s = 0; s < S::STAGES; ++s) {
             mbar_init(&k_full[s], 1);
@@ -213,9 +284,23 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
         mbar_init(drain, 1);
         fence_mbarrier_init();
     }
-    if (warp == 9) {
+    if (warp == kMmaWarp) {
         tmem_alloc(tmem_holder, 512);
         tmem_relinquish();
+    }
+    if constexpr (S::HDPO > 64) {
+        // V's second chunk: zeros, except the ones column (row-sum trick).  TMA
+        // later rewrites only the first v1_width columns of each row.
+        const uint32_t one = BF16 ? 0x3F80u : 0x3C00u;
+        for (int idx = threadIdx.x; idx < S::STAGES * 128 * 8; idx += kThreads) {
+            const int st = idx / (128 * 8), row = (idx / 8) % 128, c16 = idx % 8;
+            uint4 w = make_uint4(0u, 0u, 0u, 0u);
+            if (p.ones_col >= 64 && c16 == ((p.ones_col - 64) >> 3))
+                w.x = one; // element (ones_col - 64) % 8 == 0 of its 16-byte chunk
+            uint8_t *row_base = sV + st * S::V_BYTES + S::V_CH0 + row * 128;
+            *reinterpret_cast<uint4 *>(row_base + ((c16 ^ (row & 7)) << 4)) = w;
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
     tc_fence_before();
     __syncthreads();
@@ -226,14 +311,14 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
         if (threadIdx.x == 0)
             atomicOr(err, kErrWaitDrain);
         __syncthreads();
-        if (warp == 9)
+        if (warp == kMmaWarp)
             tmem_dealloc(tmem, 512);
         return;
     }
 
-    if (warp >= 8) {
+    if (warp >= kProducerWarp) {
         setmaxnreg_dec<kControlRegs>();
-        if (warp == 8) {
+        if (warp == kProducerWarp) {
             // -------------------------------------------------- TMA producer
             // The whole warp runs this loop (warp-uniform state); one elected
             // lane issues each barrier arrive and TMA copy.
@@ -280,10 +365,10 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                         break;
                     }
                     if (elect_one()) {
-                        mbar_arrive_expect_tx(&v_full[st], S::V_BYTES);
+                        mbar_arrive_expect_tx(&v_full[st], 128 * 2 * (S::C0 + p.v1_width));
                         uint8_t *vdst = sV + st * S::V_BYTES;
                         tma_load_4d(vdst, &p.tv0, &v_full[st], 0, j * 128, it.h, it.b);
-                        if constexpr (HDP > 64)
+                        if (S::HDPO > 64 && p.v1_width > 0)
                             tma_load_4d(vdst + S::V_CH0, &p.tv1, &v_full[st], 64, j * 128, it.h,
                                         it.b);
                     }
@@ -298,18 +383,19 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                 if (ok || n + 1 < kv)
                     wait_drain(&v_full[n % S::STAGES], (n / S::STAGES) & 1, err);
             }
-        } else if (warp == 9) {
+        } else if (warp == kMmaWarp) {
             // ---------------------------------------------------- MMA issuer
             // The whole warp runs this loop with warp-uniform values; one
             // elected lane issues each tcgen05.mma / tcgen05.commit.
             constexpr uint32_t idesc_qk = make_idesc_f16(128, 128, BF16, false);
-            constexpr uint32_t idesc_pv = make_idesc_f16(128, HDP, BF16, true);
+            constexpr uint32_t idesc_pv = make_idesc_f16(128, S::HDPO, BF16, true);
             constexpr uint32_t lay0 = layout_for_row_bytes(S::ROW0);
             constexpr uint32_t lay1 = layout_for_row_bytes(S::ROW1 > 0 ? S::ROW1 : 32);
             const uint32_t sq = smem_u32(sQ), sk = smem_u32(sK), sv = smem_u32(sV);
             // Descriptors are advanced by adding (byte offset >> 4) to the start
-            // address field; the K-step loops stay rolled so that the issuing
-            // thread does not keep every descriptor live in registers.
+            // address field; the K-step loops are unrolled so that every offset
+            // is a compile-time constant (the issue path then runs at the
+            // tensor core's rate).
             const uint32_t leader = elect_one() ? 1u : 0u;
             // All 512 TMEM columns belong to this CTA, so the allocation starts
             // at lane 0 / column 0: use the constant (warp-uniform, so MMA
@@ -321,7 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                 const uint32_t d = tmem + i * 128;
                 const uint64_t a0 = make_smem_desc(qbase + i * S::TILE_BYTES, 16, 8 * S::ROW0, lay0);
                 const uint64_t b0 = make_smem_desc(sk + st * S::TILE_BYTES, 16, 8 * S::ROW0, lay0);
-#pragma unroll 1
+#pragma unroll
                 for (int kk = 0; kk < S::C0 / 16; ++kk)
                     umma_ss_if(leader, d, a0 + 2 * kk, b0 + 2 * kk, idesc_qk, kk > 0 ? 1u : 0u);
                 if constexpr (S::C1 > 0) {
@@ -329,7 +415,7 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                                                        8 * S::ROW1, lay1);
                     const uint64_t b1 = make_smem_desc(sk + st * S::TILE_BYTES + S::CH0_BYTES, 16,
                                                        8 * S::ROW1, lay1);
-#pragma unroll 1
+#pragma unroll
                     for (int kk = 0; kk < S::C1 / 16; ++kk)
                         umma_ss_if(leader, d, a1 + 2 * kk, b1 + 2 * kk, idesc_qk, 1u);
                 }
@@ -338,10 +424,10 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                 const uint32_t d = tmem + 256 + i * 128;
                 const uint32_t a = tmem + i * 128;
                 const uint32_t vb = sv + st * S::V_BYTES;
-                constexpr uint32_t vrow = HDP >= 64 ? 128 : S::ROW0;
+                constexpr uint32_t vrow = S::HDPO >= 64 ? 128 : S::ROW0;
                 const uint64_t v0 = make_smem_desc(vb, S::V_CH0, 8 * vrow,
-                                                   HDP >= 64 ? kLayoutSW128 : lay0);
-#pragma unroll 1
+                                                   S::HDPO >= 64 ? kLayoutSW128 : lay0);
+#pragma unroll
                 for (int kk = 0; kk < 8; ++kk)
                     umma_ts_if(leader, d, a + kk * 8,
                                v0 + static_cast<uint64_t>((kk * 16 * vrow) >> 4), idesc_pv,
@@ -400,26 +486,71 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                 }
                 if (!ok)
                     break;
-                commit(o_full);       // O_0, O_1 of this item are final
-                commit(&q_empty[qs]); // every MMA reading this Q slot is done
+                commit(o_full); // O_0, O_1 of this item are final
+                if (!p.o_tma)
+                    commit(&q_empty[qs]); // every MMA reading this Q slot is done
                 kv += it.T;
                 ++nq;
                 ++n_items;
             }
             commit(drain);
             wait_drain(drain, 0, err);
+        } else if (p.o_tma) {
+            // ---------------------------------------------- output stores
+            // Warp 18 + i stores tile i of every item: it waits until the 256
+            // softmax threads of the tile have staged O in the item's Q slot,
+            // writes the tile with TMA, waits until the copy has read shared
+            // memory and hands the Q slot back to the producer.
+            const int i = warp - (kMmaWarp + 1);
+            int n_items = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; ok && u < items; u += gridDim.x) {
+                const Item it = decode_item(p, u);
+                if (it.skip || it.T == 0)
+                    continue;
+                const int qs_out = n_items % S::QBUF;
+                ok = __all_sync(0xffffffffu, mbar_wait(&ebar[i], n_items & 1, err, kErrWaitO));
+                if (!ok)
+                    break;
+                ++n_items;
+                if (elect_one()) {
+                    uint8_t *stile = sQ + (qs_out * 2 + i) * S::TILE_BYTES;
+                    const int row0 = it.q0 + i * 128;
+                    if (row0 < p.L) { // a tile wholly past the end stores nothing
+                        tma_store_4d(&p.to0, stile, 0, row0, it.h, it.b);
+                        if constexpr (S::C1 > 0)
+                            tma_store_4d(&p.to1, stile + S::CH0_BYTES, S::C0, row0, it.h, it.b);
+                        tma_store_commit();
+                        tma_store_wait_read();
+                    }
+                    mbar_arrive(&q_empty[qs_out]);
+                }
+                __syncwarp();
+            }
         }
         __syncwarp();
     } else {
         // ------------------------------------------------- softmax warpgroups
+        // Tile i = warp / 8; each TMEM lane quarter q (= warp % 4, fixed by
+        // the hardware) is served by two warps: half hh = (warp / 4) % 2 owns
+        // score columns [64 hh, 64 hh + 64) of rows 32 q .. 32 q + 31.  The
+        // halves exchange their row maxima (and, without the ones column,
+        // their row sums) through shared memory.
         setmaxnreg_inc<kSoftmaxRegs>();
-        const int i = warp >> 2;                // query tile
-        const int r = ((warp & 3) << 5) + lane; // TMEM lane == row in tile
-        const uint32_t lane_base = static_cast<uint32_t>((warp & 3) << 5) << 16;
-        const uint32_t tS = tmem + lane_base + i * 128;
+        const int i = warp >> 3, hh = (warp >> 2) & 1, qd = warp & 3;
+        const int r = (qd << 5) + lane; // TMEM lane == row in tile
+        const uint32_t lane_base = static_cast<uint32_t>(qd << 5) << 16;
+        const uint32_t tS = tmem + lane_base + i * 128 + hh * 64; // this half's scores
+        const uint32_t tP = tmem + lane_base + i * 128 + hh * 32; // this half's P pairs
         const uint32_t tO = tmem + lane_base + 256 + i * 128;
         const float sl2 = p.scale_log2;
-        int g = 0, n_items = 0;
+        const bool ones = S::HDPO > 64 && p.ones_col >= 0;
+        // 16-column chunk ranges of O owned by this half (rescale / epilogue).
+        constexpr int kOch = S::HDPO / 16, kOsplit = (kOch + 1) / 2;
+        const int oc_begin = hh ? kOsplit : 0, oc_end = hh ? kOch : kOsplit;
+        constexpr int kEch = HDP / 16, kEsplit = (kEch + 1) / 2;
+        const int ec_begin = hh ? kEsplit : 0, ec_end = hh ? kEch : kEsplit;
+        int g = 0, n_items = 0, n_sum = 0;
         bool ok = true;
         for (int u = blockIdx.x; ok && u < items; u += gridDim.x) {
             const Item it = decode_item(p, u);
@@ -435,33 +566,42 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                 if (!ok)
                     break;
                 tc_fence_after();
-                uint32_t sraw[128];
+                uint32_t sraw[64];
                 tmem_ld32(tS + 0, *reinterpret_cast<uint32_t(*)[32]>(&sraw[0]));
                 tmem_ld32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(&sraw[32]));
-                tmem_ld32(tS + 64, *reinterpret_cast<uint32_t(*)[32]>(&sraw[64]));
-                tmem_ld32(tS + 96, *reinterpret_cast<uint32_t(*)[32]>(&sraw[96]));
                 tmem_wait_ld();
                 float *s = reinterpret_cast<float *>(sraw);
-                const int kv0 = j * 128;
-                if (kv0 + 128 > limit) {
+                const int kv0 = j * 128 + hh * 64;
+                const bool masked = kv0 + 64 > limit;
+                if (masked) {
 #pragma unroll
-                    for (int c = 0; c < 128; ++c)
+                    for (int c = 0; c < 64; ++c)
                         if (kv0 + c >= limit)
                             s[c] = -INFINITY;
                 }
-                // Row max: four independent 3-input max chains.
+                // Half-row max: four independent 3-input max chains.
                 float m0 = fmax3(s[0], s[1], s[2]), m1 = fmax3(s[3], s[4], s[5]);
                 float m2 = fmax3(s[6], s[7], s[8]), m3 = fmax3(s[9], s[10], s[11]);
 #pragma unroll
-                for (int c = 12; c < 124; c += 8) {
+                for (int c = 12; c < 60; c += 8) {
                     m0 = fmax3(m0, s[c], s[c + 1]);
                     m1 = fmax3(m1, s[c + 2], s[c + 3]);
                     m2 = fmax3(m2, s[c + 4], s[c + 5]);
                     m3 = fmax3(m3, s[c + 6], s[c + 7]);
                 }
-                m0 = fmax3(m0, s[124], s[125]);
-                m1 = fmax3(m1, s[126], s[127]);
-                const float mt = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+                m0 = fmax3(m0, s[60], s[61]);
+                m1 = fmax3(m1, s[62], s[63]);
+                const float mh = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+                // Exchange with the other half (double-buffered by iteration
+                // parity).  After this wait both halves have also finished
+                // reading their scores, so P may overwrite them.
+                float *xm = xmax + (((g & 1) * 2 + i) * 2) * 128;
+                xm[hh * 128 + r] = mh;
+                mbar_arrive(&xbar[i]);
+                ok = __all_sync(0xffffffffu, mbar_wait(&xbar[i], g & 1, err, kErrWaitP));
+                if (!ok)
+                    break;
+                const float mt = fmaxf(mh, xm[(hh ^ 1) * 128 + r]);
                 const float mnew = fmaxf(m, mt * sl2);
                 // Lazy rescale: a row keeps its stale max while P stays below 2^8.
                 const bool grow = mnew > m + 8.0f;
@@ -470,43 +610,68 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                     l *= alpha;
                     m = mnew;
                 }
-                // tcgen05.ld/st are warp-collective: rescale the warp's O rows
+                const float neg_m = -m;
+                if (OMNI_FMHA_TURN && (i == 1 || g > 0)) {
+                    // The tiles take turns for the exp phase: tile 0 runs
+                    // iteration g after tile 1 finished g-1, tile 1 after tile 0
+                    // finished g, so one tile's exps overlap the other's MMAs.
+                    const uint32_t par = i == 1 ? (g & 1) : ((g - 1) & 1);
+                    ok = __all_sync(0xffffffffu, mbar_wait(&turn[i], par, err, kErrWaitP));
+                    if (!ok)
+                        break;
+                }
+                // P = 2^(s*scale - m) (packed fp32 FMA), exp2 split between the
+                // MUFU and the FMA-pipe polynomial; P pair c is written over
+                // sraw[c] (its inputs s[2c], s[2c+1] are consumed by then).
+                // Rows of a masked tile use MUFU only (exact zeros for -inf).
+                float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
+#pragma unroll
+                for (int c = 0; c < 32; c += 2) {
+                    float x0, x1, x2, x3;
+                    ffma2(x0, x1, s[2 * c], s[2 * c + 1], sl2, sl2, neg_m, neg_m);
+                    ffma2(x2, x3, s[2 * c + 2], s[2 * c + 3], sl2, sl2, neg_m, neg_m);
+                    if (poly_pair(c) && !masked) {
+                        exp2_poly2(x0, x1, x0, x1);
+                    } else {
+                        x0 = ex2_approx(x0);
+                        x1 = ex2_approx(x1);
+                    }
+                    if (poly_pair(c + 1) && !masked) {
+                        exp2_poly2(x2, x3, x2, x3);
+                    } else {
+                        x2 = ex2_approx(x2);
+                        x3 = ex2_approx(x3);
+                    }
+                    if (!ones) {
+                        fadd2(a0, a1, a0, a1, x0, x1);
+                        fadd2(b0, b1, b0, b1, x2, x3);
+                    }
+                    sraw[c] = pack2(x0, x1, BF16);
+                    sraw[c + 1] = pack2(x2, x3, BF16);
+                }
+                if (!ones)
+                    l += (a0 + a1) + (b0 + b1);
+                if (OMNI_FMHA_TURN)
+                    mbar_arrive(&turn[i ^ 1]); // the other tile's turn
+                // O rescale (after the scores are dead, to keep registers low).
+                // tcgen05.ld/st are warp-collective: the warp's rows rescale
                 // together (alpha == 1 for rows whose max did not grow).
                 if (j > 0 && __any_sync(0xffffffffu, grow)) {
 #pragma unroll
-                    for (int c = 0; c < HDP; c += 16) {
+                    for (int c = 0; c < kOch; ++c) {
+                        if (c < oc_begin || c >= oc_end)
+                            continue;
                         uint32_t o[16];
-                        tmem_ld16(tO + c, o);
+                        tmem_ld16(tO + c * 16, o);
                         tmem_wait_ld();
 #pragma unroll
                         for (int e = 0; e < 16; ++e)
                             o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-                        tmem_st16(tO + c, o);
+                        tmem_st16(tO + c * 16, o);
                     }
                 }
-                const float neg_m = -m;
-                // P = 2^(s*scale - m): packed fp32 FMA, MUFU ex2, packed sums.
-                // P pair c is written over sraw[c]: its inputs s[2c], s[2c+1]
-                // (and every s below them) have been consumed by then.
-                float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
-#pragma unroll
-                for (int c = 0; c < 64; c += 2) {
-                    float x0, x1, x2, x3;
-                    ffma2(x0, x1, s[2 * c], s[2 * c + 1], sl2, sl2, neg_m, neg_m);
-                    ffma2(x2, x3, s[2 * c + 2], s[2 * c + 3], sl2, sl2, neg_m, neg_m);
-                    x0 = ex2_approx(x0);
-                    x1 = ex2_approx(x1);
-                    x2 = ex2_approx(x2);
-                    x3 = ex2_approx(x3);
-                    fadd2(a0, a1, a0, a1, x0, x1);
-                    fadd2(b0, b1, b0, b1, x2, x3);
-                    sraw[c] = pack2(x0, x1, BF16);
-                    sraw[c + 1] = pack2(x2, x3, BF16);
-                }
-                l += (a0 + a1) + (b0 + b1);
                 __syncwarp();
-                tmem_st32(tS + 0, *reinterpret_cast<uint32_t(*)[32]>(&sraw[0]));
-                tmem_st32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(&sraw[32]));
+                tmem_st32(tP, *reinterpret_cast<uint32_t(*)[32]>(&sraw[0]));
                 tmem_wait_st();
                 tc_fence_before();
                 mbar_arrive(&p_full[i]);
@@ -520,12 +685,72 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                 ++n_items;
                 tc_fence_after();
             }
+            if (ones && it.T > 0) {
+                // Row sum of P = O[:, ones_col] (rescaled together with O).
+                uint32_t o[16];
+                tmem_ld16(tO + (p.ones_col & ~15), o);
+                tmem_wait_ld();
+                const int e1 = p.ones_col & 15;
+                l = 0.f;
+#pragma unroll
+                for (int e = 0; e < 16; ++e)
+                    l = e == e1 ? __uint_as_float(o[e]) : l;
+            } else if (it.T > 0) {
+                // Sum of the two halves' partial row sums.
+                xsum[(i * 2 + hh) * 128 + r] = l;
+                mbar_arrive(&lbar[i]);
+                ok = __all_sync(0xffffffffu, mbar_wait(&lbar[i], n_sum & 1, err, kErrWaitO));
+                if (!ok)
+                    break;
+                ++n_sum;
+                l += xsum[(i * 2 + (hh ^ 1)) * 128 + r];
+            }
             const float inv = (it.T > 0 && l > 0.f) ? 1.f / l : 0.f;
+            if (p.o_tma && it.T > 0) {
+                // Stage this half's O columns in the item's Q slot (the same
+                // swizzled chunk layout as a Q tile; every MMA reading Q is
+                // complete once o_full fired), then one thread per tile stores
+                // the tile with TMA (rows past L and columns past hd clipped).
+                const int qs_out = (n_items - 1) % S::QBUF;
+                uint8_t *stile = sQ + (qs_out * 2 + i) * S::TILE_BYTES;
+#pragma unroll
+                for (int cq = 0; cq < kEch; ++cq) {
+                    if (cq < ec_begin || cq >= ec_end)
+                        continue;
+                    const int c = cq * 16;
+                    uint32_t o[16];
+                    tmem_ld16(tO + c, o);
+                    tmem_wait_ld();
+                    uint4 w0, w1;
+                    w0.x = pack2(__uint_as_float(o[0]) * inv, __uint_as_float(o[1]) * inv, BF16);
+                    w0.y = pack2(__uint_as_float(o[2]) * inv, __uint_as_float(o[3]) * inv, BF16);
+                    w0.z = pack2(__uint_as_float(o[4]) * inv, __uint_as_float(o[5]) * inv, BF16);
+                    w0.w = pack2(__uint_as_float(o[6]) * inv, __uint_as_float(o[7]) * inv, BF16);
+                    w1.x = pack2(__uint_as_float(o[8]) * inv, __uint_as_float(o[9]) * inv, BF16);
+                    w1.y = pack2(__uint_as_float(o[10]) * inv, __uint_as_float(o[11]) * inv, BF16);
+                    w1.z = pack2(__uint_as_float(o[12]) * inv, __uint_as_float(o[13]) * inv, BF16);
+                    w1.w = pack2(__uint_as_float(o[14]) * inv, __uint_as_float(o[15]) * inv, BF16);
+                    const bool ch1 = c >= S::C0;
+                    const int rowb = ch1 ? S::ROW1 : S::ROW0;
+                    const int k16 = ((ch1 ? c - S::C0 : c) * 2) >> 4; // 16-byte chunk in the row
+                    const int sw = ((r * rowb) >> 7) & ((rowb >> 4) - 1);
+                    uint8_t *rowp = stile + (ch1 ? S::CH0_BYTES : 0) + r * rowb;
+                    *reinterpret_cast<uint4 *>(rowp + ((k16 ^ sw) << 4)) = w0;
+                    *reinterpret_cast<uint4 *>(rowp + (((k16 + 1) ^ sw) << 4)) = w1;
+                }
+                fence_proxy_async_smem();
+                mbar_arrive(&ebar[i]); // the tile's store warp takes it from here
+                __syncwarp();
+                continue;
+            }
             const bool store = t < p.L;
             const long long base =
                 it.b * p.o_sb + it.h * p.o_sh + static_cast<long long>(t) * p.o_st;
 #pragma unroll
-            for (int c = 0; c < HDP; c += 16) {
+            for (int cq = 0; cq < kEch; ++cq) {
+                if (cq < ec_begin || cq >= ec_end)
+                    continue;
+                const int c = cq * 16;
                 uint32_t o[16];
                 if (it.T > 0) {
                     tmem_ld16(tO + c, o);
@@ -590,7 +815,7 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 9)
+    if (warp == kMmaWarp)
         tmem_dealloc(tmem, 512);
 }
 
@@ -598,14 +823,14 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
 // Builds a 4-D (d, token, head, batch) tiled map with a box of
 // box_w x box_rows x 1 x 1 elements.
 int make_map(CUtensorMap *map, const void *base, bool bf16, const TensorView &v, int box_w,
-             int box_rows) {
+             int box_rows, int swizzle_bytes = 0) {
     const uint64_t dims[4] = {static_cast<uint64_t>(v.d), static_cast<uint64_t>(v.tokens),
                               static_cast<uint64_t>(v.heads), static_cast<uint64_t>(v.batch)};
     const uint64_t strides[3] = {static_cast<uint64_t>(v.s_token) * 2,
                                  static_cast<uint64_t>(v.s_head) * 2,
                                  static_cast<uint64_t>(v.s_batch) * 2};
     const uint32_t box[4] = {static_cast<uint32_t>(box_w), static_cast<uint32_t>(box_rows), 1, 1};
-    return encode_tiled(map, base, bf16, 4, dims, strides, box);
+    return encode_tiled(map, base, bf16, 4, dims, strides, box, swizzle_bytes);
 }
 
 bool tma_view_ok(const void *base, const TensorView &v) {
@@ -662,11 +887,41 @@ int fmha_launch(const FmhaArgs &a, cudaStream_t stream) {
         (rc = make_map(&p.tv0, a.v_ptr, a.bf16, a.v, w0, 128)))
         return rc;
     if (w1 > 0) {
-        // V's second chunk is always a 64-column box (see FmhaShape::V_BYTES).
         if ((rc = make_map(&p.tq1, a.q_ptr, a.bf16, a.q, w1, 128)) ||
-            (rc = make_map(&p.tk1, a.k_ptr, a.bf16, a.k, w1, 128)) ||
-            (rc = make_map(&p.tv1, a.v_ptr, a.bf16, a.v, 64, 128)))
+            (rc = make_map(&p.tk1, a.k_ptr, a.bf16, a.k, w1, 128)))
             return rc;
+    }
+    // Row-sum column: V column `d` (first column past the data) holds 1.0 when
+    // the PV output has room for it and the data ends on a 16-byte boundary.
+    const int hdpo = hdp == 64 ? 80 : hdp == 96 ? 112 : hdp;
+    const int dv = a.v.d;
+    p.ones_col = (hdpo > 64 && dv >= 64 && dv % 8 == 0 && dv < hdpo) ? dv : -1;
+    // V's second chunk: TMA loads only the data columns [64, dv), 16-byte
+    // granular; the rest of the 64-column atom keeps its zeros (and the ones).
+    p.v1_width = dv > 64 ? ((dv - 64 + 7) / 8) * 8 : 0;
+    if (p.v1_width > 64)
+        p.v1_width = 64;
+    // 128-byte swizzle whatever the box width: chunk 1 is a 64-column SW128 atom.
+    if (p.v1_width > 0 && (rc = make_map(&p.tv1, a.v_ptr, a.bf16, a.v, p.v1_width, 128, 128)))
+        return rc;
+    // TMA output: 2-byte outputs whose layout TMA can address (same 16-byte
+    // rules as the inputs); the tile geometry is the Q tile's.
+    {
+        TensorView ov;
+        ov.d = a.out_d > 0 ? a.out_d : a.q.d;
+        ov.tokens = a.q.tokens;
+        ov.heads = a.q.heads;
+        ov.batch = a.q.batch;
+        ov.s_token = a.o_st;
+        ov.s_head = a.o_sh;
+        ov.s_batch = a.o_sb > 0 ? a.o_sb : a.o_st * a.q.tokens;
+        p.o_tma = 0;
+        if (a.out_dtype != kOutF32 && tma_view_ok(a.out, ov) && ov.d % 8 == 0 && ov.d <= hdp) {
+            const bool obf = a.out_dtype == kOutBF16;
+            if (make_map(&p.to0, a.out, obf, ov, w0, 128) == 0 &&
+                (w1 == 0 || make_map(&p.to1, a.out, obf, ov, w1, 128) == 0))
+                p.o_tma = (obf == a.bf16) ? 1 : 0; // staging packs with the operand type
+        }
     }
     p.out = a.out;
     p.o_sb = a.o_sb;

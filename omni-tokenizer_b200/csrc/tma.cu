@@ -34,7 +34,7 @@ CUtensorMapSwizzle swizzle_for(int row_bytes) {
 } // namespace
 
 int encode_tiled(CUtensorMap *map, const void *base, bool bf16, int rank, const uint64_t *dims,
-                 const uint64_t *byte_strides, const uint32_t *box) {
+                 const uint64_t *byte_strides, const uint32_t *box, int swizzle_bytes) {
     EncodeTiledFn fn = encode_fn();
     if (!fn)
         return -1;
@@ -51,7 +51,8 @@ int encode_tiled(CUtensorMap *map, const void *base, bool bf16, int rank, const 
     const CUresult r =
         fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
            static_cast<cuuint32_t>(rank), const_cast<void *>(base), d, s, b, e,
-           CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle_for(static_cast<int>(box[0]) * 2),
+           CU_TENSOR_MAP_INTERLEAVE_NONE,
+           swizzle_for(swizzle_bytes > 0 ? swizzle_bytes : static_cast<int>(box[0]) * 2),
            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? 0 : static_cast<int>(r) + 1000;
 }

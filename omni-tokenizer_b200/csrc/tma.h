@@ -6,9 +6,10 @@
 #include <stdint.h>
 
 namespace omni_b200 {
-// Returns 0, -1 (no driver entry point) or 1000 + CUresult.
+// Returns 0, -1 (no driver entry point) or 1000 + CUresult.  swizzle_bytes
+// (32, 64 or 128) overrides the swizzle implied by the box row bytes.
 int encode_tiled(CUtensorMap *map, const void *base, bool bf16, int rank, const uint64_t *dims,
-                 const uint64_t *byte_strides, const uint32_t *box);
+                 const uint64_t *byte_strides, const uint32_t *box, int swizzle_bytes = 0);
 // Row-major [rows, cols] matrix; box of box_w columns x box_rows rows.
 int make_map_2d(CUtensorMap *map, const void *base, int cols, long long rows, int box_w,
                 int box_rows, bool bf16 = true);
