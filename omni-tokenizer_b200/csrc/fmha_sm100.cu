@@ -41,6 +41,9 @@
 
 namespace omni_b200 {
 
+#ifndef OMNI_FMHA_PT
+#define OMNI_FMHA_PT 1
+#endif
 #ifndef OMNI_FMHA_QBUF
 #define OMNI_FMHA_QBUF (HDP <= 96 ? 2 : 1)
 #endif
@@ -60,12 +63,20 @@ template <int HDP> struct FmhaShape {
     static constexpr int HDPO = HDP == 64 ? 80 : HDP == 96 ? 112 : HDP;
     static constexpr int V_BYTES = HDPO > 64 ? 2 * 128 * 128 : TILE_BYTES;
     static constexpr int V_CH0 = 128 * ROW0;
-    static constexpr int QBUF = OMNI_FMHA_QBUF;   // Q buffers (2: next item prefetch)
-    static constexpr int BUDGET = 226 * 1024;
+    // HDPO <= 80 (PT schedule): P gets TMEM columns of its own, the 48 free
+    // columns after each O tile -- keys [0, 64) at kPcol0, [64, 128) at
+    // kPcol1 -- shared by the two query tiles.  S_i is then free as soon as
+    // the softmax has read it, so the next S_i = Q_i K^T is computed while the
+    // softmax still works on the current tile, and the MMAs leave the
+    // softmax's critical path.  Wider heads write P over S (no spare columns).
+    static constexpr bool PT = OMNI_FMHA_PT && HDPO <= 80;
+    static constexpr uint32_t kPcol0 = 256 + 80, kPcol1 = 384 + 80;
+    static constexpr int QBUF = OMNI_FMHA_QBUF; // Q buffers (2: next item prefetch)
+    static constexpr int BUDGET = 226 * 1024 - 8 * 1024;
     static constexpr int STAGES_RAW = (BUDGET - QBUF * 2 * TILE_BYTES) / (TILE_BYTES + V_BYTES);
     static constexpr int STAGES = STAGES_RAW > 4 ? 4 : STAGES_RAW;
     static constexpr int KSTEPS = HDP / 16;
-    static constexpr int BAR_BYTES = 512 + 2 * 2 * 2 * 128 * 4 + 2 * 2 * 128 * 4;
+    static constexpr int BAR_BYTES = 512;
     // At least 120 KB so that one CTA (which allocates all 512 TMEM columns)
     // occupies an SM by itself.
     static constexpr int SMEM_RAW =
@@ -76,17 +87,18 @@ template <int HDP> struct FmhaShape {
     static_assert(STAGES >= 2, "K/V ring needs two stages");
 };
 
-// 20 warps: 0-7 softmax tile 0, 8-15 softmax tile 1 (two warps per TMEM lane
-// quarter, each owning 64 of the 128 score columns), 16 TMA producer, 17 MMA
-// issuer / TMEM owner, 18-19 output stores of tile 0 / tile 1.  Registers are rebalanced with setmaxnreg:
-// launch 96/thread; the softmax warpgroups grow to 104 and the control
-// warpgroup shrinks to 64 (16*104 + 4*64 = 1920 = 20*96 per lane; 4*104 + 64 =
-// 480 <= 512 per SM sub-partition).
-constexpr int kThreads = 640;
-constexpr int kSoftmaxRegs = 104;
-constexpr int kControlRegs = 64;
-constexpr int kProducerWarp = 16;
-constexpr int kMmaWarp = 17;
+// 12 warps: 0-3 softmax tile 0, 4-7 softmax tile 1 (warp w serves TMEM lane
+// quarter w % 4; each thread owns one query row, all 128 score columns), 8 TMA
+// producer, 9 MMA issuer / TMEM owner, 10-11 output stores of tile 0 / tile 1.
+// Registers are rebalanced with setmaxnreg: launch 168/thread; the softmax
+// warpgroups grow to 208 and the control warpgroup shrinks to 72
+// (8*32*208 + 4*32*72 = 62464 <= 384*168 = 64512 per CTA; 2*208 + 72 = 488
+// <= 512 per SM sub-partition).
+constexpr int kThreads = 384;
+constexpr int kSoftmaxRegs = 208;
+constexpr int kControlRegs = 72;
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
 
 // Loads one 128-row tile (both chunks) of a (token, head, batch) tensor.
 template <int HDP>
@@ -177,7 +189,7 @@ __device__ __forceinline__ void exp2_poly2(float &y0, float &y1, float x0, float
 #define OMNI_FMHA_POLY 0
 #endif
 #ifndef OMNI_FMHA_TURN
-#define OMNI_FMHA_TURN 1
+#define OMNI_FMHA_TURN 0
 #endif
 __device__ __forceinline__ constexpr bool poly_pair(int pair) {
     return OMNI_FMHA_POLY && ((pair & 7) == 1 || (pair & 7) == 4 || (pair & 7) == 6);
@@ -229,6 +241,18 @@ __device__ __forceinline__ Item decode_item(const FmhaParams &p, int u) {
     return it;
 }
 
+// Barriers between the softmax warps of a tile (and their consumers) count
+// one arrive per warp: the warp's lanes first synchronise (which orders their
+// shared-memory and tensor-memory accesses before lane 0's release), then
+// lane 0 arrives.  256 per-thread arrives on one barrier word would serialise
+// in the shared-memory atomic unit (~2 clk each, on the softmax critical path).
+constexpr int kTileWarps = 4;
+__device__ __forceinline__ void warp_arrive(uint64_t *bar) {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0)
+        mbar_arrive(bar);
+}
+
 template <int HDP, bool BF16>
 __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_constant__ FmhaParams p) {
     using S = FmhaShape<HDP>;
@@ -249,13 +273,11 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
     uint64_t *p_full = s_full + 2;            // [2]
     uint64_t *o_full = p_full + 2;
     uint64_t *drain = o_full + 1;
-    uint64_t *xbar = drain + 1;               // [2] half-row max exchange, per tile
-    uint64_t *lbar = xbar + 2;                // [2] half-row sum exchange, per tile
-    uint64_t *ebar = lbar + 2;                // [2] output tile staged, per tile
+    uint64_t *ebar = drain + 1;               // [2] output tile staged, per tile
     uint64_t *turn = ebar + 2;                // [2] exp-phase hand-off between the tiles
-    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(turn + 2);
-    float *xmax = reinterpret_cast<float *>(tmem_holder + 4); // [2 parity][2 tile][2 half][128]
-    float *xsum = xmax + 2 * 2 * 2 * 128;                       // [2 tile][2 half][128]
+    uint64_t *s_free = turn + 2;              // [2] softmax has read S_i (PT)
+    uint64_t *pv_done = s_free + 2;           // [2] O_i += P_i V complete (PT)
+    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(pv_done + 2);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int items = p.batch * p.heads * ((p.L + 255) / 256);
@@ -264,15 +286,15 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
     if (threadIdx.x == 0) {
         for (int i = 0; i < 2; ++i) {
             mbar_init(&q_full[i], 1);
-            // Released by the MMA warp (TMA-free output) or by the two tiles'
+            // Released by the MMA warp, or (TMA output) by the two tiles'
             // output stores, which stage O in this Q slot.
             mbar_init(&q_empty[i], p.o_tma ? 2 : 1);
-            mbar_init(&ebar[i], 256);
-            mbar_init(&turn[i], 256);
+            mbar_init(&ebar[i], kTileWarps);
+            mbar_init(&turn[i], kTileWarps);
+            mbar_init(&s_free[i], kTileWarps);
+            mbar_init(&pv_done[i], 1);
             mbar_init(&s_full[i], 1);
-            mbar_init(&p_full[i], 256);
-            mbar_init(&xbar[i], 256);
-            mbar_init(&lbar[i], 256);
+            mbar_init(&p_full[i], kTileWarps);
         }
         for (int s = 0; s < S::STAGES; ++s) {
             mbar_init(&k_full[s], 1);
@@ -433,72 +455,149 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                                v0 + static_cast<uint64_t>((kk * 16 * vrow) >> 4), idesc_pv,
                                (accumulate || kk > 0) ? 1u : 0u);
             };
-            int nq = 0, kv = 0, n_items = 0;
-            bool ok = true;
-            for (int u = blockIdx.x; ok && u < items; u += gridDim.x) {
-                const Item it = decode_item(p, u);
-                if (it.skip || it.T == 0)
-                    continue;
-                const int qs = nq % S::QBUF;
-                const uint32_t qbase = sq + qs * 2 * S::TILE_BYTES;
-                if (!(ok = __all_sync(0xffffffffu, mbar_wait(&q_full[qs], (nq / S::QBUF) & 1, err, kErrWaitQ))))
-                    break;
-                {
-                    const int st = kv % S::STAGES;
-                    if (!(ok = __all_sync(0xffffffffu, mbar_wait(&k_full[st], (kv / S::STAGES) & 1, err, kErrWaitK))))
+            // O_i += P_i V_st with P in its own TMEM columns (PT).
+            auto pv_pt = [&](int i, int st, bool accumulate) {
+                const uint32_t d = tmem + 256 + i * 128;
+                const uint32_t vb = sv + st * S::V_BYTES;
+                constexpr uint32_t vrow = S::HDPO >= 64 ? 128 : S::ROW0;
+                const uint64_t v0 = make_smem_desc(vb, S::V_CH0, 8 * vrow,
+                                                   S::HDPO >= 64 ? kLayoutSW128 : lay0);
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk)
+                    umma_ts_if(leader, d, tmem + (kk < 4 ? S::kPcol0 : S::kPcol1) + (kk & 3) * 8,
+                               v0 + static_cast<uint64_t>((kk * 16 * vrow) >> 4), idesc_pv,
+                               (accumulate || kk > 0) ? 1u : 0u);
+            };
+            if constexpr (S::PT) {
+                // Per KV tile g: S_0(g+1), S_1(g+1) as soon as the softmax has
+                // read S_0(g), S_1(g); then O_0 += P_0(g) V_g and O_1 += P_1(g) V_g
+                // as each P arrives.  pv_done[i] fires after O_i += P_i V.
+                int nq = 0, kv = 0;
+                bool ok = true;
+                for (int u = blockIdx.x; ok && u < items; u += gridDim.x) {
+                    const Item it = decode_item(p, u);
+                    if (it.skip || it.T == 0)
+                        continue;
+                    const int qs = nq % S::QBUF;
+                    const uint32_t qbase = sq + qs * 2 * S::TILE_BYTES;
+                    if (!(ok = __all_sync(0xffffffffu, mbar_wait(&q_full[qs], (nq / S::QBUF) & 1, err, kErrWaitQ))))
                         break;
-                    tc_fence_after();
-                    qk(qbase, 0, st);
-                    commit(&s_full[0]);
-                    qk(qbase, 1, st);
-                    commit(&s_full[1]);
-                    commit(&k_empty[st]);
+                    // S_i(g0) for the item's first KV tile g0 = kv.
+                    auto issue_s = [&](int g, int st) {
+                        for (int i = 0; i < 2; ++i) {
+                            if (g > 0 && !__all_sync(0xffffffffu, mbar_wait(&s_free[i], (g - 1) & 1, err, kErrWaitS)))
+                                return false;
+                            tc_fence_after();
+                            qk(qbase, i, st);
+                            commit(&s_full[i]);
+                        }
+                        commit(&k_empty[st]);
+                        return true;
+                    };
+                    {
+                        const int st = kv % S::STAGES;
+                        if (!(ok = __all_sync(0xffffffffu, mbar_wait(&k_full[st], (kv / S::STAGES) & 1, err, kErrWaitK))))
+                            break;
+                        if (!(ok = issue_s(kv, st)))
+                            break;
+                    }
+                    for (int j = 0; ok && j < it.T; ++j) {
+                        const int g = kv + j, st = g % S::STAGES;
+                        if (j + 1 < it.T) {
+                            const int st1 = (g + 1) % S::STAGES;
+                            if (!(ok = __all_sync(0xffffffffu, mbar_wait(&k_full[st1], ((g + 1) / S::STAGES) & 1, err, kErrWaitK))))
+                                break;
+                            if (!(ok = issue_s(g + 1, st1)))
+                                break;
+                        }
+                        if (!(ok = __all_sync(0xffffffffu, mbar_wait(&v_full[st], (g / S::STAGES) & 1, err, kErrWaitV))))
+                            break;
+                        for (int i = 0; i < 2; ++i) {
+                            if (!(ok = __all_sync(0xffffffffu, mbar_wait(&p_full[i], g & 1, err, kErrWaitP))))
+                                break;
+                            tc_fence_after();
+                            pv_pt(i, st, j > 0);
+                            commit(&pv_done[i]);
+                        }
+                        if (!ok)
+                            break;
+                        commit(&v_empty[st]);
+                    }
+                    if (!ok)
+                        break;
+                    if (!p.o_tma)
+                        commit(&q_empty[qs]); // every MMA reading this Q slot is done
+                    kv += it.T;
+                    ++nq;
                 }
-                for (int j = 0; j < it.T; ++j) {
-                    const int g = kv + j, st = g % S::STAGES;
-                    const uint32_t ph = (g / S::STAGES) & 1;
-                    const int g1 = g + 1, st1 = g1 % S::STAGES;
-                    const uint32_t ph1 = (g1 / S::STAGES) & 1;
-                    const bool more = j + 1 < it.T;
-                    if (!(ok = __all_sync(0xffffffffu, mbar_wait(&v_full[st], ph, err, kErrWaitV))))
+            } else {
+                int nq = 0, kv = 0, n_items = 0;
+                bool ok = true;
+                for (int u = blockIdx.x; ok && u < items; u += gridDim.x) {
+                    const Item it = decode_item(p, u);
+                    if (it.skip || it.T == 0)
+                        continue;
+                    const int qs = nq % S::QBUF;
+                    const uint32_t qbase = sq + qs * 2 * S::TILE_BYTES;
+                    if (!(ok = __all_sync(0xffffffffu, mbar_wait(&q_full[qs], (nq / S::QBUF) & 1, err, kErrWaitQ))))
                         break;
-                    if (!(ok = __all_sync(0xffffffffu, mbar_wait(&p_full[0], g & 1, err, kErrWaitP))))
-                        break;
-                    tc_fence_after();
-                    pv(0, st, j > 0);
-                    if (more) {
-                        if (!(ok = __all_sync(0xffffffffu, mbar_wait(&k_full[st1], ph1, err, kErrWaitK))))
+                    {
+                        const int st = kv % S::STAGES;
+                        if (!(ok = __all_sync(0xffffffffu, mbar_wait(&k_full[st], (kv / S::STAGES) & 1, err, kErrWaitK))))
                             break;
                         tc_fence_after();
-                        qk(qbase, 0, st1);
+                        qk(qbase, 0, st);
                         commit(&s_full[0]);
-                    }
-                    if (!(ok = __all_sync(0xffffffffu, mbar_wait(&p_full[1], g & 1, err, kErrWaitP))))
-                        break;
-                    tc_fence_after();
-                    pv(1, st, j > 0);
-                    commit(&v_empty[st]);
-                    if (more) {
-                        qk(qbase, 1, st1);
+                        qk(qbase, 1, st);
                         commit(&s_full[1]);
-                        commit(&k_empty[st1]);
+                        commit(&k_empty[st]);
                     }
+                    for (int j = 0; j < it.T; ++j) {
+                        const int g = kv + j, st = g % S::STAGES;
+                        const uint32_t ph = (g / S::STAGES) & 1;
+                        const int g1 = g + 1, st1 = g1 % S::STAGES;
+                        const uint32_t ph1 = (g1 / S::STAGES) & 1;
+                        const bool more = j + 1 < it.T;
+                        if (!(ok = __all_sync(0xffffffffu, mbar_wait(&v_full[st], ph, err, kErrWaitV))))
+                            break;
+                        if (!(ok = __all_sync(0xffffffffu, mbar_wait(&p_full[0], g & 1, err, kErrWaitP))))
+                            break;
+                        tc_fence_after();
+                        pv(0, st, j > 0);
+                        if (more) {
+                            if (!(ok = __all_sync(0xffffffffu, mbar_wait(&k_full[st1], ph1, err, kErrWaitK))))
+                                break;
+                            tc_fence_after();
+                            qk(qbase, 0, st1);
+                            commit(&s_full[0]);
+                        }
+                        if (!(ok = __all_sync(0xffffffffu, mbar_wait(&p_full[1], g & 1, err, kErrWaitP))))
+                            break;
+                        tc_fence_after();
+                        pv(1, st, j > 0);
+                        commit(&v_empty[st]);
+                        if (more) {
+                            qk(qbase, 1, st1);
+                            commit(&s_full[1]);
+                            commit(&k_empty[st1]);
+                        }
+                    }
+                    if (!ok)
+                        break;
+                    commit(o_full); // O_0, O_1 of this item are final
+                    if (!p.o_tma)
+                        commit(&q_empty[qs]); // every MMA reading this Q slot is done
+                    kv += it.T;
+                    ++nq;
+                    ++n_items;
                 }
-                if (!ok)
-                    break;
-                commit(o_full); // O_0, O_1 of this item are final
-                if (!p.o_tma)
-                    commit(&q_empty[qs]); // every MMA reading this Q slot is done
-                kv += it.T;
-                ++nq;
-                ++n_items;
             }
             commit(drain);
             wait_drain(drain, 0, err);
         } else if (p.o_tma) {
             // ---------------------------------------------- output stores
-            // Warp 18 + i stores tile i of every item: it waits until the 256
-            // softmax threads of the tile have staged O in the item's Q slot,
+            // Warp 10 + i stores tile i of every item: it waits until the four
+            // softmax warps of the tile have staged O in the item's Q slot,
             // writes the tile with TMA, waits until the copy has read shared
             // memory and hands the Q slot back to the producer.
             const int i = warp - (kMmaWarp + 1);
@@ -531,26 +630,19 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
         __syncwarp();
     } else {
         // ------------------------------------------------- softmax warpgroups
-        // Tile i = warp / 8; each TMEM lane quarter q (= warp % 4, fixed by
-        // the hardware) is served by two warps: half hh = (warp / 4) % 2 owns
-        // score columns [64 hh, 64 hh + 64) of rows 32 q .. 32 q + 31.  The
-        // halves exchange their row maxima (and, without the ones column,
-        // their row sums) through shared memory.
+        // Tile i = warp / 4; warp w serves TMEM lane quarter w % 4 (fixed by
+        // the hardware) and each of its threads owns one query row: all 128
+        // score columns, the running max / sum and the row of O.
         setmaxnreg_inc<kSoftmaxRegs>();
-        const int i = warp >> 3, hh = (warp >> 2) & 1, qd = warp & 3;
+        const int i = warp >> 2, qd = warp & 3;
         const int r = (qd << 5) + lane; // TMEM lane == row in tile
         const uint32_t lane_base = static_cast<uint32_t>(qd << 5) << 16;
-        const uint32_t tS = tmem + lane_base + i * 128 + hh * 64; // this half's scores
-        const uint32_t tP = tmem + lane_base + i * 128 + hh * 32; // this half's P pairs
+        const uint32_t tS = tmem + lane_base + i * 128;
         const uint32_t tO = tmem + lane_base + 256 + i * 128;
         const float sl2 = p.scale_log2;
         const bool ones = S::HDPO > 64 && p.ones_col >= 0;
-        // 16-column chunk ranges of O owned by this half (rescale / epilogue).
-        constexpr int kOch = S::HDPO / 16, kOsplit = (kOch + 1) / 2;
-        const int oc_begin = hh ? kOsplit : 0, oc_end = hh ? kOch : kOsplit;
-        constexpr int kEch = HDP / 16, kEsplit = (kEch + 1) / 2;
-        const int ec_begin = hh ? kEsplit : 0, ec_end = hh ? kEch : kEsplit;
-        int g = 0, n_items = 0, n_sum = 0;
+        constexpr int kOch = S::HDPO / 16, kEch = HDP / 16;
+        int g = 0, n_items = 0;
         bool ok = true;
         for (int u = blockIdx.x; ok && u < items; u += gridDim.x) {
             const Item it = decode_item(p, u);
@@ -566,43 +658,38 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                 if (!ok)
                     break;
                 tc_fence_after();
-                uint32_t sraw[64];
-                tmem_ld32(tS + 0, *reinterpret_cast<uint32_t(*)[32]>(&sraw[0]));
-                tmem_ld32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(&sraw[32]));
+                uint32_t sraw[128];
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    tmem_ld32(tS + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&sraw[32 * c]));
                 tmem_wait_ld();
+                if constexpr (S::PT) {
+                    // S_i is in registers: the MMA warp may compute S_i(j+1).
+                    tc_fence_before();
+                    warp_arrive(&s_free[i]);
+                }
                 float *s = reinterpret_cast<float *>(sraw);
-                const int kv0 = j * 128 + hh * 64;
-                const bool masked = kv0 + 64 > limit;
+                const int kv0 = j * 128;
+                const bool masked = kv0 + 128 > limit;
                 if (masked) {
 #pragma unroll
-                    for (int c = 0; c < 64; ++c)
+                    for (int c = 0; c < 128; ++c)
                         if (kv0 + c >= limit)
                             s[c] = -INFINITY;
                 }
-                // Half-row max: four independent 3-input max chains.
+                // Row max: four independent 3-input max chains.
                 float m0 = fmax3(s[0], s[1], s[2]), m1 = fmax3(s[3], s[4], s[5]);
                 float m2 = fmax3(s[6], s[7], s[8]), m3 = fmax3(s[9], s[10], s[11]);
 #pragma unroll
-                for (int c = 12; c < 60; c += 8) {
+                for (int c = 12; c < 124; c += 8) {
                     m0 = fmax3(m0, s[c], s[c + 1]);
                     m1 = fmax3(m1, s[c + 2], s[c + 3]);
                     m2 = fmax3(m2, s[c + 4], s[c + 5]);
                     m3 = fmax3(m3, s[c + 6], s[c + 7]);
                 }
-                m0 = fmax3(m0, s[60], s[61]);
-                m1 = fmax3(m1, s[62], s[63]);
-                const float mh = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
-                // Exchange with the other half (double-buffered by iteration
-                // parity).  After this wait both halves have also finished
-                // reading their scores, so P may overwrite them.
-                float *xm = xmax + (((g & 1) * 2 + i) * 2) * 128;
-                xm[hh * 128 + r] = mh;
-                mbar_arrive(&xbar[i]);
-                ok = __all_sync(0xffffffffu, mbar_wait(&xbar[i], g & 1, err, kErrWaitP));
-                if (!ok)
-                    break;
-                const float mt = fmaxf(mh, xm[(hh ^ 1) * 128 + r]);
-                const float mnew = fmaxf(m, mt * sl2);
+                m0 = fmax3(m0, s[124], s[125]);
+                m1 = fmax3(m1, s[126], s[127]);
+                const float mnew = fmaxf(m, fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)) * sl2);
                 // Lazy rescale: a row keeps its stale max while P stays below 2^8.
                 const bool grow = mnew > m + 8.0f;
                 const float alpha = (grow && j > 0) ? ex2_approx(m - mnew) : 1.f;
@@ -614,19 +701,19 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                 if (OMNI_FMHA_TURN && (i == 1 || g > 0)) {
                     // The tiles take turns for the exp phase: tile 0 runs
                     // iteration g after tile 1 finished g-1, tile 1 after tile 0
-                    // finished g, so one tile's exps overlap the other's MMAs.
+                    // finished g.
                     const uint32_t par = i == 1 ? (g & 1) : ((g - 1) & 1);
                     ok = __all_sync(0xffffffffu, mbar_wait(&turn[i], par, err, kErrWaitP));
                     if (!ok)
                         break;
                 }
-                // P = 2^(s*scale - m) (packed fp32 FMA), exp2 split between the
-                // MUFU and the FMA-pipe polynomial; P pair c is written over
-                // sraw[c] (its inputs s[2c], s[2c+1] are consumed by then).
-                // Rows of a masked tile use MUFU only (exact zeros for -inf).
+                // P = 2^(s*scale - m) (packed fp32 FMA, MUFU ex2 or the FMA-pipe
+                // polynomial); P pair c (keys 2c, 2c+1) is written over sraw[c]
+                // (its inputs s[2c], s[2c+1] are consumed by then).  Rows of a
+                // masked tile use MUFU only (exact zeros for -inf).
                 float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
 #pragma unroll
-                for (int c = 0; c < 32; c += 2) {
+                for (int c = 0; c < 64; c += 2) {
                     float x0, x1, x2, x3;
                     ffma2(x0, x1, s[2 * c], s[2 * c + 1], sl2, sl2, neg_m, neg_m);
                     ffma2(x2, x3, s[2 * c + 2], s[2 * c + 3], sl2, sl2, neg_m, neg_m);
@@ -652,15 +739,28 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                 if (!ones)
                     l += (a0 + a1) + (b0 + b1);
                 if (OMNI_FMHA_TURN)
-                    mbar_arrive(&turn[i ^ 1]); // the other tile's turn
+                    warp_arrive(&turn[i ^ 1]); // the other tile's turn
+                if constexpr (S::PT) {
+                    // The P columns are shared by the two tiles: tile 0 writes
+                    // P(g) once O_1 += P_1(g-1) V is complete, tile 1 once
+                    // O_0 += P_0(g) V is.  Each of those MMAs was issued after
+                    // this tile's own previous O += P V, so O_i may be rescaled
+                    // after the wait too.
+                    if (i == 1 || g > 0) {
+                        ok = __all_sync(0xffffffffu,
+                                        mbar_wait(&pv_done[i ^ 1], i == 0 ? (g - 1) & 1 : g & 1,
+                                                  err, kErrWaitO));
+                        if (!ok)
+                            break;
+                        tc_fence_after();
+                    }
+                }
                 // O rescale (after the scores are dead, to keep registers low).
                 // tcgen05.ld/st are warp-collective: the warp's rows rescale
                 // together (alpha == 1 for rows whose max did not grow).
                 if (j > 0 && __any_sync(0xffffffffu, grow)) {
 #pragma unroll
                     for (int c = 0; c < kOch; ++c) {
-                        if (c < oc_begin || c >= oc_end)
-                            continue;
                         uint32_t o[16];
                         tmem_ld16(tO + c * 16, o);
                         tmem_wait_ld();
@@ -671,15 +771,27 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                     }
                 }
                 __syncwarp();
-                tmem_st32(tP, *reinterpret_cast<uint32_t(*)[32]>(&sraw[0]));
-                tmem_wait_st();
+                if constexpr (S::PT) {
+                    tmem_st32(tmem + lane_base + S::kPcol0,
+                              *reinterpret_cast<uint32_t(*)[32]>(&sraw[0]));
+                    tmem_st32(tmem + lane_base + S::kPcol1,
+                              *reinterpret_cast<uint32_t(*)[32]>(&sraw[32]));
+                } else {
+                    // P over the first 64 columns of S_i (all of S_i was read).
+                    tmem_st32(tS, *reinterpret_cast<uint32_t(*)[32]>(&sraw[0]));
+                    tmem_st32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(&sraw[32]));
+                }
+                tmem_wait_st(); // P, and the O rescale above
                 tc_fence_before();
-                mbar_arrive(&p_full[i]);
+                warp_arrive(&p_full[i]);
             }
             if (!ok)
                 break;
             if (it.T > 0) {
-                ok = __all_sync(0xffffffffu, mbar_wait(o_full, n_items & 1, err, kErrWaitO));
+                if constexpr (S::PT)
+                    ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[i], (g - 1) & 1, err, kErrWaitO));
+                else
+                    ok = __all_sync(0xffffffffu, mbar_wait(o_full, n_items & 1, err, kErrWaitO));
                 if (!ok)
                     break;
                 ++n_items;
@@ -695,28 +807,17 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
 #pragma unroll
                 for (int e = 0; e < 16; ++e)
                     l = e == e1 ? __uint_as_float(o[e]) : l;
-            } else if (it.T > 0) {
-                // Sum of the two halves' partial row sums.
-                xsum[(i * 2 + hh) * 128 + r] = l;
-                mbar_arrive(&lbar[i]);
-                ok = __all_sync(0xffffffffu, mbar_wait(&lbar[i], n_sum & 1, err, kErrWaitO));
-                if (!ok)
-                    break;
-                ++n_sum;
-                l += xsum[(i * 2 + (hh ^ 1)) * 128 + r];
             }
             const float inv = (it.T > 0 && l > 0.f) ? 1.f / l : 0.f;
             if (p.o_tma && it.T > 0) {
-                // Stage this half's O columns in the item's Q slot (the same
-                // swizzled chunk layout as a Q tile; every MMA reading Q is
-                // complete once o_full fired), then one thread per tile stores
-                // the tile with TMA (rows past L and columns past hd clipped).
+                // Stage the row of O in the item's Q slot (the same swizzled
+                // chunk layout as a Q tile; every MMA reading Q is complete once
+                // O is final), then the tile's store warp writes it with TMA
+                // (rows past L and columns past hd clipped).
                 const int qs_out = (n_items - 1) % S::QBUF;
                 uint8_t *stile = sQ + (qs_out * 2 + i) * S::TILE_BYTES;
 #pragma unroll
                 for (int cq = 0; cq < kEch; ++cq) {
-                    if (cq < ec_begin || cq >= ec_end)
-                        continue;
                     const int c = cq * 16;
                     uint32_t o[16];
                     tmem_ld16(tO + c, o);
@@ -739,8 +840,7 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                     *reinterpret_cast<uint4 *>(rowp + (((k16 + 1) ^ sw) << 4)) = w1;
                 }
                 fence_proxy_async_smem();
-                mbar_arrive(&ebar[i]); // the tile's store warp takes it from here
-                __syncwarp();
+                warp_arrive(&ebar[i]); // the tile's store warp takes it from here
                 continue;
             }
             const bool store = t < p.L;
@@ -748,8 +848,6 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                 it.b * p.o_sb + it.h * p.o_sh + static_cast<long long>(t) * p.o_st;
 #pragma unroll
             for (int cq = 0; cq < kEch; ++cq) {
-                if (cq < ec_begin || cq >= ec_end)
-                    continue;
                 const int c = cq * 16;
                 uint32_t o[16];
                 if (it.T > 0) {
