@@ -241,6 +241,39 @@ __device__ __forceinline__ Item decode_item(const FmhaParams &p, int u) {
     return it;
 }
 
+// The first item at or after u (in steps of the grid) that has KV work, or
+// `items` when there is none: the items whose Q, K and V are loaded and whose
+// MMAs are issued.
+__device__ __forceinline__ int next_work_item(const FmhaParams &p, int u, int items) {
+    for (; u < items; u += gridDim.x) {
+        const Item it = decode_item(p, u);
+        if (!it.skip && it.T > 0)
+            break;
+    }
+    return u;
+}
+
+// Loads the two Q tiles of item u into Q slot nq % QBUF once the slot is free.
+template <int HDP>
+__device__ __forceinline__ bool load_q_tiles(const FmhaParams &p, int u, int nq, uint8_t *sQ,
+                                             uint64_t *q_full, uint64_t *q_empty, int *err) {
+    using S = FmhaShape<HDP>;
+    const Item it = decode_item(p, u);
+    const int qs = nq % S::QBUF;
+    if (!__all_sync(0xffffffffu,
+                    mbar_wait(&q_empty[qs], ((nq / S::QBUF) & 1) ^ 1, err, kErrWaitEmpty)))
+        return false;
+    uint8_t *qdst = sQ + qs * 2 * S::TILE_BYTES;
+    if (elect_one()) {
+        mbar_arrive_expect_tx(&q_full[qs], 2 * S::TILE_BYTES);
+        load_tile<HDP>(qdst, &p.tq0, &p.tq1, &q_full[qs], it.q0, it.h, it.b);
+        load_tile<HDP>(qdst + S::TILE_BYTES, &p.tq0, &p.tq1, &q_full[qs], it.q0 + 128, it.h,
+                       it.b);
+    }
+    __syncwarp();
+    return true;
+}
+
 // Barriers between the softmax warps of a tile (and their consumers) count
 // one arrive per warp: the warp's lanes first synchronise (which orders their
 // shared-memory and tensor-memory accesses before lane 0's release), then
@@ -349,29 +382,15 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                 tma_prefetch_desc(&p.tk0);
                 tma_prefetch_desc(&p.tv0);
             }
-            int nq = 0, kv = 0; // Q loads / K,V tile loads issued by this CTA
+            // K and V loads issued by this CTA (Q tiles are loaded by warp 10).
+            int nk = 0, nv = 0;
             bool ok = true;
-            for (int u = blockIdx.x; ok && u < items; u += gridDim.x) {
+            for (int u = next_work_item(p, blockIdx.x, items); ok && u < items;
+                 u = next_work_item(p, u + gridDim.x, items)) {
                 const Item it = decode_item(p, u);
-                if (it.skip || it.T == 0)
-                    continue;
-                const int qs = nq % S::QBUF;
-                ok = __all_sync(0xffffffffu, mbar_wait(&q_empty[qs], ((nq / S::QBUF) & 1) ^ 1, err,
-                                                        kErrWaitEmpty));
-                if (!ok)
-                    break;
-                uint8_t *qdst = sQ + qs * 2 * S::TILE_BYTES;
-                if (elect_one()) {
-                    mbar_arrive_expect_tx(&q_full[qs], 2 * S::TILE_BYTES);
-                    load_tile<HDP>(qdst, &p.tq0, &p.tq1, &q_full[qs], it.q0, it.h, it.b);
-                    load_tile<HDP>(qdst + S::TILE_BYTES, &p.tq0, &p.tq1, &q_full[qs], it.q0 + 128,
-                                   it.h, it.b);
-                }
-                __syncwarp();
-                ++nq;
-                for (int j = 0; j < it.T; ++j, ++kv) {
-                    const int st = kv % S::STAGES;
-                    const uint32_t ph = (kv / S::STAGES) & 1;
+                for (int j = 0; j < it.T; ++j) {
+                    const int st = nk % S::STAGES;
+                    const uint32_t ph = (nk / S::STAGES) & 1;
                     ok = __all_sync(0xffffffffu, mbar_wait(&k_empty[st], ph ^ 1, err, kErrWaitEmpty));
                     if (!ok)
                         break;
@@ -381,11 +400,10 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                                        j * 128, it.h, it.b);
                     }
                     __syncwarp();
+                    ++nk;
                     ok = __all_sync(0xffffffffu, mbar_wait(&v_empty[st], ph ^ 1, err, kErrWaitEmpty));
-                    if (!ok) {
-                        ++kv; // the K load above was issued
+                    if (!ok)
                         break;
-                    }
                     if (elect_one()) {
                         mbar_arrive_expect_tx(&v_full[st], 128 * 2 * (S::C0 + p.v1_width));
                         uint8_t *vdst = sV + st * S::V_BYTES;
@@ -395,16 +413,14 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                                         it.b);
                     }
                     __syncwarp();
+                    ++nv;
                 }
             }
             // Every issued copy must land before the CTA may exit.
-            for (int n = nq - S::QBUF < 0 ? 0 : nq - S::QBUF; n < nq; ++n)
-                wait_drain(&q_full[n % S::QBUF], (n / S::QBUF) & 1, err);
-            for (int n = kv - S::STAGES < 0 ? 0 : kv - S::STAGES; n < kv; ++n) {
+            for (int n = nk - S::STAGES < 0 ? 0 : nk - S::STAGES; n < nk; ++n)
                 wait_drain(&k_full[n % S::STAGES], (n / S::STAGES) & 1, err);
-                if (ok || n + 1 < kv)
-                    wait_drain(&v_full[n % S::STAGES], (n / S::STAGES) & 1, err);
-            }
+            for (int n = nv - S::STAGES < 0 ? 0 : nv - S::STAGES; n < nv; ++n)
+                wait_drain(&v_full[n % S::STAGES], (n / S::STAGES) & 1, err);
         } else if (warp == kMmaWarp) {
             // ---------------------------------------------------- MMA issuer
             // The whole warp runs this loop with warp-uniform values; one
@@ -594,37 +610,61 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
             }
             commit(drain);
             wait_drain(drain, 0, err);
-        } else if (p.o_tma) {
-            // ---------------------------------------------- output stores
-            // Warp 10 + i stores tile i of every item: it waits until the four
-            // softmax warps of the tile have staged O in the item's Q slot,
-            // writes the tile with TMA, waits until the copy has read shared
-            // memory and hands the Q slot back to the producer.
+        } else {
+            // ------------------------------------- Q loads and output stores
+            // Warp 10 + i stores tile i of every item (TMA output): it waits
+            // until the four softmax warps of the tile have staged O in the
+            // item's Q slot, writes the tile with TMA and waits until the copy
+            // has read shared memory before it releases the Q slot.  Warp 10
+            // also loads the Q tiles: the first QBUF items' at the start, then
+            // item n + QBUF's as soon as item n has released its slot, so that
+            // the K/V producer never waits for a Q slot.
             const int i = warp - (kMmaWarp + 1);
-            int n_items = 0;
+            int n_items = 0, nq = 0;
+            int uq = next_work_item(p, blockIdx.x, items); // next item whose Q is due
             bool ok = true;
-            for (int u = blockIdx.x; ok && u < items; u += gridDim.x) {
-                const Item it = decode_item(p, u);
-                if (it.skip || it.T == 0)
-                    continue;
-                const int qs_out = n_items % S::QBUF;
-                ok = __all_sync(0xffffffffu, mbar_wait(&ebar[i], n_items & 1, err, kErrWaitO));
-                if (!ok)
-                    break;
-                ++n_items;
-                if (elect_one()) {
-                    uint8_t *stile = sQ + (qs_out * 2 + i) * S::TILE_BYTES;
-                    const int row0 = it.q0 + i * 128;
-                    if (row0 < p.L) { // a tile wholly past the end stores nothing
-                        tma_store_4d(&p.to0, stile, 0, row0, it.h, it.b);
-                        if constexpr (S::C1 > 0)
-                            tma_store_4d(&p.to1, stile + S::CH0_BYTES, S::C0, row0, it.h, it.b);
-                        tma_store_commit();
-                        tma_store_wait_read();
-                    }
-                    mbar_arrive(&q_empty[qs_out]);
+            if (i == 0) {
+                for (int k = 0; ok && k < S::QBUF && uq < items; ++k) {
+                    ok = load_q_tiles<HDP>(p, uq, nq, sQ, q_full, q_empty, err);
+                    ++nq;
+                    uq = next_work_item(p, uq + gridDim.x, items);
                 }
-                __syncwarp();
+            }
+            for (int u = next_work_item(p, blockIdx.x, items); ok && u < items;
+                 u = next_work_item(p, u + gridDim.x, items)) {
+                if (p.o_tma) {
+                    const Item it = decode_item(p, u);
+                    const int qs_out = n_items % S::QBUF;
+                    ok = __all_sync(0xffffffffu, mbar_wait(&ebar[i], n_items & 1, err, kErrWaitO));
+                    if (!ok)
+                        break;
+                    ++n_items;
+                    if (elect_one()) {
+                        uint8_t *stile = sQ + (qs_out * 2 + i) * S::TILE_BYTES;
+                        const int row0 = it.q0 + i * 128;
+                        if (row0 < p.L) { // a tile wholly past the end stores nothing
+                            tma_store_4d(&p.to0, stile, 0, row0, it.h, it.b);
+                            if constexpr (S::C1 > 0)
+                                tma_store_4d(&p.to1, stile + S::CH0_BYTES, S::C0, row0, it.h,
+                                             it.b);
+                            tma_store_commit();
+                            tma_store_wait_read();
+                        }
+                        mbar_arrive(&q_empty[qs_out]);
+                    }
+                    __syncwarp();
+                }
+                if (i == 0 && uq < items) {
+                    if (!(ok = load_q_tiles<HDP>(p, uq, nq, sQ, q_full, q_empty, err)))
+                        break;
+                    ++nq;
+                    uq = next_work_item(p, uq + gridDim.x, items);
+                }
+            }
+            if (i == 0) {
+                // Every issued Q copy must land before the CTA may exit.
+                for (int n = nq - S::QBUF < 0 ? 0 : nq - S::QBUF; n < nq; ++n)
+                    wait_drain(&q_full[n % S::QBUF], (n / S::QBUF) & 1, err);
             }
         }
         __syncwarp();
