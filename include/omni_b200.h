@@ -85,10 +85,15 @@ OMNI_B200_API int omni_b200_squares(const void *x, void *out, size_t rows, size_
  * src/cpu.cpp:227-287): ids[r] = argmin over codes c of the profile's
  * expanded L2 distance between x[r,:] and codebook[c,:], smallest id on ties.
  * profile BF16: x, codebook and cbnorm (= squares(codebook), see above) are
- * bf16; dist = bf16(bf16(|x|^2 + |c|^2) - bf16(2 bf16(x.c))).
+ * bf16; dist = bf16(bf16(|x|^2 + |c|^2) - bf16(2 bf16(x.c))); dim % 8 == 0.
+ * profile F32: x, codebook and cbnorm are fp32 (cbnorm = squares(codebook));
+ * the result is the reference's: the code with the smallest direct fp64
+ * distance sum_k (x_k - c_k)^2 among the codes whose expanded-L2 distance lies
+ * within the error bound of the best one (src/cpu.cpp:260-283); dim % 4 == 0.
  * ids are uint16 (ids_u16 != 0, as the reference returns) or int32.
- * workspace: omni_b200_vq_workspace() bytes of device memory (8 per row).
- * x, codebook, cbnorm must be 16-byte aligned; codes <= 65536. */
+ * workspace: omni_b200_vq_workspace() bytes of device memory (BF16 with
+ * dim <= 128: 8 per row; BF16 with larger dim: 12 per row; F32: 144 per row).
+ * x, codebook, cbnorm must be 16-byte aligned; codes <= 65536, dim <= 65536. */
 OMNI_B200_API size_t omni_b200_vq_workspace(size_t rows, size_t dim, size_t codes, int profile);
 OMNI_B200_API int omni_b200_vq_argmin(const void *x, const void *codebook, const void *cbnorm,
                                       void *ids, size_t rows, size_t dim, size_t codes,
@@ -103,7 +108,8 @@ OMNI_B200_API int omni_b200_vq_argmin(const void *x, const void *codebook, const
  * loop.  The 8-byte-per-row scratch lives in a fixed device array of 65536
  * rows (512 KiB per device, held by every GPU that loads this library until
  * exit); more rows are rejected with INVALID_ARGUMENT.  The caller still passes
- * x, codebook, cbnorm and ids (same meaning as omni_b200_vq_argmin).  The first
+ * x, codebook, cbnorm and ids (same meaning as omni_b200_vq_argmin; BF16
+ * profile with dim <= 128 only, other shapes are rejected).  The first
  * call on a device looks up that device's address of the array
  * (cudaGetSymbolAddress); make that first call before any stream capture.
  * Every call shares the one array: the launch re-initialises the rows it uses,

@@ -253,9 +253,11 @@ int omni_b200_squares(const void *x, void *out, size_t rows, size_t cols, int dt
 }
 
 size_t omni_b200_vq_workspace(size_t rows, size_t dim, size_t codes, int profile) {
-    (void)dim;
     (void)codes;
-    (void)profile;
+    if (profile == OMNI_B200_F32)
+        return vq_stream_workspace(rows, 1);
+    if (dim > 128)
+        return vq_stream_workspace(rows, 0);
     return (rows * 8 + 255) / 256 * 256;
 }
 
@@ -269,10 +271,14 @@ int omni_b200_vq_argmin(const void *x, const void *codebook, const void *cbnorm,
         return 0;
     if (dim == 0 || codes == 0 || codes > 65536 || rows > (1u << 30))
         return fail(1, "vq_argmin: need dim > 0 and 0 < codes <= 65536");
-    if (profile != OMNI_B200_BF16)
-        return fail(4, "vq_argmin: only the BF16 profile is available in this build");
-    if (dim % 8 != 0 || dim > 128)
-        return fail(4, "vq_argmin: dim must be a multiple of 8 and at most 128");
+    if (profile != OMNI_B200_BF16 && profile != OMNI_B200_F32)
+        return fail(1, "vq_argmin: profile must be OMNI_B200_BF16 or OMNI_B200_F32");
+    const bool fp32 = profile == OMNI_B200_F32;
+    if (fp32 ? dim % 4 != 0 : dim % 8 != 0)
+        return fail(4, fp32 ? "vq_argmin: fp32 profile needs dim % 4 == 0 (16-byte rows)"
+                            : "vq_argmin: bf16 profile needs dim % 8 == 0 (16-byte rows)");
+    if (dim > 65536)
+        return fail(4, "vq_argmin: dim must be at most 65536");
     const uintptr_t align = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(codebook) |
                             reinterpret_cast<uintptr_t>(cbnorm);
     if (align % 16 != 0)
@@ -293,6 +299,9 @@ int omni_b200_vq_argmin(const void *x, const void *codebook, const void *cbnorm,
     a.err = kernel_error_word();
     if (!a.err)
         return fail(7, "vq_argmin: no CUDA device");
+    if (fp32 || dim > 128)
+        return launch_status(vq_stream_launch(a, fp32 ? 1 : 0, static_cast<cudaStream_t>(stream)),
+                             "vq_argmin");
     return launch_status(vq_bf16_launch(a, static_cast<cudaStream_t>(stream)), "vq_argmin");
 }
 

@@ -33,8 +33,10 @@ CUtensorMapSwizzle swizzle_for(int row_bytes) {
 }
 } // namespace
 
-int encode_tiled(CUtensorMap *map, const void *base, bool bf16, int rank, const uint64_t *dims,
-                 const uint64_t *byte_strides, const uint32_t *box, int swizzle_bytes) {
+namespace {
+int encode_typed(CUtensorMap *map, const void *base, CUtensorMapDataType type, int elem_bytes,
+                 int rank, const uint64_t *dims, const uint64_t *byte_strides,
+                 const uint32_t *box, int swizzle_bytes) {
     EncodeTiledFn fn = encode_fn();
     if (!fn)
         return -1;
@@ -49,12 +51,27 @@ int encode_tiled(CUtensorMap *map, const void *base, bool bf16, int rank, const 
             s[i] = byte_strides[i];
     }
     const CUresult r =
-        fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-           static_cast<cuuint32_t>(rank), const_cast<void *>(base), d, s, b, e,
+        fn(map, type, static_cast<cuuint32_t>(rank), const_cast<void *>(base), d, s, b, e,
            CU_TENSOR_MAP_INTERLEAVE_NONE,
-           swizzle_for(swizzle_bytes > 0 ? swizzle_bytes : static_cast<int>(box[0]) * 2),
+           swizzle_for(swizzle_bytes > 0 ? swizzle_bytes : static_cast<int>(box[0]) * elem_bytes),
            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? 0 : static_cast<int>(r) + 1000;
+}
+} // namespace
+
+int encode_tiled(CUtensorMap *map, const void *base, bool bf16, int rank, const uint64_t *dims,
+                 const uint64_t *byte_strides, const uint32_t *box, int swizzle_bytes) {
+    return encode_typed(map, base,
+                        bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                        rank, dims, byte_strides, box, swizzle_bytes);
+}
+
+int make_map_2d_f32(CUtensorMap *map, const void *base, int cols, long long rows, int box_w,
+                    int box_rows) {
+    const uint64_t dims[2] = {static_cast<uint64_t>(cols), static_cast<uint64_t>(rows)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(cols) * 4};
+    const uint32_t box[2] = {static_cast<uint32_t>(box_w), static_cast<uint32_t>(box_rows)};
+    return encode_typed(map, base, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, 2, dims, strides, box, 0);
 }
 
 int make_map_2d(CUtensorMap *map, const void *base, int cols, long long rows, int box_w,

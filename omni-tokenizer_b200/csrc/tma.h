@@ -1,4 +1,4 @@
-// tma.h -- tensor-map helpers (2-byte elements, swizzle chosen from the box row bytes:
+// tma.h -- tensor-map helpers (2- or 4-byte elements, swizzle chosen from the box row bytes:
 // 128 B -> 128B swizzle, 64 B -> 64B, 32 B -> 32B).
 #pragma once
 #include <cuda.h>
@@ -13,4 +13,8 @@ int encode_tiled(CUtensorMap *map, const void *base, bool bf16, int rank, const 
 // Row-major [rows, cols] matrix; box of box_w columns x box_rows rows.
 int make_map_2d(CUtensorMap *map, const void *base, int cols, long long rows, int box_w,
                 int box_rows, bool bf16 = true);
+// Row-major fp32 [rows, cols] matrix; box of box_w columns x box_rows rows
+// (box_w * 4 bytes = 32, 64 or 128 selects the swizzle).
+int make_map_2d_f32(CUtensorMap *map, const void *base, int cols, long long rows, int box_w,
+                    int box_rows);
 } // namespace omni_b200

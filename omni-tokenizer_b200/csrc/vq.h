@@ -28,4 +28,26 @@ struct VqArgs {
 int vq_padded_dim(int dim);
 int vq_bf16_launch(const VqArgs &args, cudaStream_t stream);
 
+// ---- streamed kernels (vq_stream_sm100.cu): bf16 profile with dim > 128 and
+// the fp32 profile.
+constexpr int kVqCandCap = 32; // fp32 profile: candidates kept per row
+enum VqsMode { kVqsBf16 = 0, kVqsApprox = 1, kVqsCand = 2 };
+
+struct VqsParams {
+    CUtensorMap tx, tc;           // x / codebook maps, 128-byte column chunks
+    float *xn;                    // [rows] |x|^2 (bf16 profile: the bf16 value)
+    const void *cbnorm;           // bf16 [codes] (bf16 profile) or f32 [codes]
+    unsigned long long *keys;     // [rows] (order bits of dist) << 32 | id
+    unsigned *cand_count;         // fp32 profile: [rows]
+    unsigned *cand;               // fp32 profile: [rows][kVqCandCap]
+    int rows, dim, codes, chunks;
+    int slices, slice_codes;
+    float delta;                  // fp32 profile: candidate window factor
+    int *err;
+};
+
+// Scratch bytes for vq_stream_launch (VqArgs::keys points at it).
+size_t vq_stream_workspace(size_t rows, int profile_fp32);
+int vq_stream_launch(const VqArgs &args, int profile_fp32, cudaStream_t stream);
+
 } // namespace omni_b200

@@ -83,7 +83,7 @@ extern "C" int omni_b200_vq_argmin_noalloc(const void *x, const void *codebook,
     if (dim == 0 || codes == 0 || codes > 65536)
         return ctx_fail(1, "vq_argmin_noalloc: need dim > 0 and 0 < codes <= 65536");
     if (profile != OMNI_B200_BF16)
-        return ctx_fail(4, "vq_argmin_noalloc: only the BF16 profile is available in this build");
+        return ctx_fail(4, "vq_argmin_noalloc: only the BF16 profile runs without scratch; use omni_b200_vq_argmin");
     if (dim % 8 != 0 || dim > 128)
         return ctx_fail(4, "vq_argmin_noalloc: dim must be a multiple of 8 and at most 128");
     const uintptr_t align = reinterpret_cast<uintptr_t>(x) |

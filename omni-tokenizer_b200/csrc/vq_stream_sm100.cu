@@ -1,0 +1,491 @@
+// vq_stream_sm100.cu -- VQ argmin with the code dimension streamed through
+// shared memory (sm_100a): the bf16 profile for wide codes (dim > 128, e.g.
+// the production 1280 / 2048) and the exact fp32 profile for every dim.
+//
+// Reference semantics (omni-tokenizer src/cpu.cpp:227-287, Cpu::quantize):
+//   bf16 profile  dist = bf16(bf16(|x|^2 + |c|^2) - bf16(2 x.c)), smallest
+//                 dist wins, ties -> smallest id (same epilogue arithmetic as
+//                 vq_sm100.cu);
+//   fp32 profile  approximate search with dist = fma(-2, x.c, |x|^2 + |c|^2),
+//                 then every code whose approximate distance lies within the
+//                 error bound of the best one is re-scored with the direct
+//                 fp64 sum  sum_k (double(x_k) - double(c_k))^2  in column
+//                 order; the smallest direct distance wins, ties -> smallest
+//                 id (src/cpu.cpp:260-283, src/internal.h:13-18).
+//
+// fp32 profile on B200.  The tensor cores have no fp32 MMA, so the
+// approximate distances come from kind::tf32 (inputs keep 10 mantissa bits).
+// The candidate window is therefore a bound written for this kernel, not the
+// reference's fp32 gamma: for every code
+//   |approx(c) - exact(c)| <= delta * (|x|^2 + |c|^2),
+//   delta = 2^-8 + (2 dim + 8) 2^-23
+// (TF32 input error 2^-10 per factor, fp32 accumulation, the fp32 norms and
+// the final fma; 2|x.c| <= |x|^2 + |c|^2 bounds the dot-product terms, and
+// delta carries a factor of two of slack).  With b the code of the smallest
+// approximate distance, the exact nearest code c* satisfies
+//   approx(c*) - delta(|x|^2 + |c*|^2) <= approx(b) + delta(|x|^2 + |b|^2),
+// so the candidate set {c : approx(c) - delta(...c) <= approx(b) + delta(...b)}
+// contains c* and every code whose direct distance ties with it.  The
+// reference's own candidate set also contains c* (its gamma bound), and both
+// pick the smallest (direct distance, id) among candidates, so the ids agree.
+// Non-finite approximate distances are always candidates; a row with more than
+// kVqCandCap candidates is scored against every code (brute force).
+//
+// Passes (one launch each):
+//   kVqsBf16    bf16 profile, keys[row] = (order bits of dist) << 32 | id
+//   kVqsApprox  fp32 profile, keys[row] = approximate best (same key form)
+//   kVqsCand    fp32 profile, appends candidates to cand[row][kVqCandCap]
+// followed by vq_refine_fp64 (fp32) or vqs_finish (bf16).
+//
+// Kernel layout: persistent grid over units (128-row tile, codebook slice);
+// warp 4 TMA producer, warp 5 TMEM owner and tcgen05.mma issuer, warps 0-3
+// epilogue (thread r owns TMEM lane r = row r of the tile).  Each 256-code
+// tile accumulates over 128-byte column chunks of x (128 rows) and of the
+// codebook (256 codes) that stream through a 4-stage ring; TMEM holds two
+// 256-column fp32 accumulators so the epilogue of one code tile overlaps the
+// MMAs of the next.
+#include "norms.h"
+#include "sm100.cuh"
+#include "tma.h"
+#include "vq.h"
+
+#include <cuda_bf16.h>
+#include <cmath>
+#include <mutex>
+
+namespace omni_b200 {
+
+template <bool TF32> struct VqsShape {
+    static constexpr int EB = TF32 ? 4 : 2;      // bytes per element
+    static constexpr int KC = 128 / EB;          // elements per 128-byte column chunk
+    static constexpr int X_CHUNK = 128 * 128;    // 128 rows x 128 bytes
+    static constexpr int C_CHUNK = 256 * 128;    // 256 codes x 128 bytes
+    static constexpr int STAGE = X_CHUNK + C_CHUNK;
+    static constexpr int STAGES = 4;
+    static constexpr int SMEM_BYTES = STAGES * STAGE + 512 + 1024;
+};
+
+constexpr int kVqsThreads = 192;
+
+__device__ __forceinline__ uint32_t vqs_order_bits(float f) {
+    const uint32_t u = __float_as_uint(f);
+    if ((u & 0x7fffffffu) > 0x7f800000u)
+        return 0xffffffffu; // NaN never wins
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float vqs_from_order_bits(uint32_t b) {
+    return __uint_as_float((b & 0x80000000u) ? (b & 0x7fffffffu) : ~b);
+}
+
+__device__ __noinline__ void vqs_wait_drain(uint64_t *bar, uint32_t parity, int *err) {
+    const uint32_t a = smem_u32(bar);
+    const uint64_t start = globaltimer_ns();
+    while (!mbar_try_wait(a, parity)) {
+        if (globaltimer_ns() - start > kWaitLimitNs) {
+            atomicOr(err, kErrWaitDrain);
+            return;
+        }
+    }
+}
+
+template <bool TF32, int MODE>
+__global__ void __launch_bounds__(kVqsThreads, 1) vq_stream_kernel(const __grid_constant__ VqsParams p) {
+    using S = VqsShape<TF32>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + S::STAGES * S::STAGE);
+    uint64_t *full = bars;                  // [STAGES]
+    uint64_t *empty = full + S::STAGES;     // [STAGES]
+    uint64_t *acc_full = empty + S::STAGES; // [2]
+    uint64_t *acc_empty = acc_full + 2;     // [2]
+    uint64_t *drain = acc_empty + 2;
+    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(drain + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int *err = p.err;
+    const int row_tiles = (p.rows + 127) / 128;
+    const int units = row_tiles * p.slices;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S::STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(&acc_full[0], 1);
+        mbar_init(&acc_full[1], 1);
+        mbar_init(&acc_empty[0], 4); // one arrive per epilogue warp
+        mbar_init(&acc_empty[1], 4);
+        mbar_init(drain, 1);
+        fence_mbarrier_init();
+    }
+    if (warp == 5) {
+        tmem_alloc(tmem_holder, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_holder;
+
+    if (warp == 4) {
+        // ------------------------------------------------------ TMA producer
+        if (elect_one()) {
+            tma_prefetch_desc(&p.tx);
+            tma_prefetch_desc(&p.tc);
+        }
+        int n = 0; // stage fills issued
+        bool ok = true;
+        for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
+            const int rt = u / p.slices, sl = u % p.slices;
+            const int c_begin = sl * p.slice_codes;
+            const int c_end = min(p.codes, c_begin + p.slice_codes);
+            for (int c = c_begin; ok && c < c_end; c += 256) {
+                for (int kc = 0; kc < p.chunks; ++kc, ++n) {
+                    const int st = n % S::STAGES;
+                    ok = __all_sync(0xffffffffu, mbar_wait(&empty[st], ((n / S::STAGES) & 1) ^ 1,
+                                                           err, kErrWaitEmpty));
+                    if (!ok)
+                        break;
+                    if (elect_one()) {
+                        uint8_t *dst = smem + st * S::STAGE;
+                        mbar_arrive_expect_tx(&full[st], S::STAGE);
+                        tma_load_2d(dst, &p.tx, &full[st], kc * S::KC, rt * 128);
+                        tma_load_2d(dst + S::X_CHUNK, &p.tc, &full[st], kc * S::KC, c);
+                    }
+                    __syncwarp();
+                }
+            }
+        }
+        // Every issued fill must land before the CTA may exit.
+        for (int j = n - S::STAGES < 0 ? 0 : n - S::STAGES; j < n; ++j)
+            vqs_wait_drain(&full[j % S::STAGES], (j / S::STAGES) & 1, err);
+    } else if (warp == 5) {
+        // ------------------------------------------------------ MMA issuer
+        constexpr uint32_t idesc = TF32 ? make_idesc_tf32(128, 256) : make_idesc_f16(128, 256, true, false);
+        const uint32_t leader = elect_one() ? 1u : 0u;
+        const uint32_t sbase = smem_u32(smem);
+        int n = 0, n_acc = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
+            const int sl = u % p.slices;
+            const int c_begin = sl * p.slice_codes;
+            const int c_end = min(p.codes, c_begin + p.slice_codes);
+            for (int c = c_begin; ok && c < c_end; c += 256, ++n_acc) {
+                const int buf = n_acc & 1;
+                if (!(ok = __all_sync(0xffffffffu, mbar_wait(&acc_empty[buf], ((n_acc >> 1) & 1) ^ 1,
+                                                             err, kErrWaitAcc))))
+                    break;
+                const uint32_t d = tmem + buf * 256;
+                for (int kc = 0; kc < p.chunks; ++kc, ++n) {
+                    const int st = n % S::STAGES;
+                    if (!(ok = __all_sync(0xffffffffu,
+                                          mbar_wait(&full[st], (n / S::STAGES) & 1, err, kErrWaitK))))
+                        break;
+                    tc_fence_after();
+                    const uint32_t xs = sbase + st * S::STAGE;
+                    const uint64_t ad = make_smem_desc(xs, 16, 1024, kLayoutSW128);
+                    const uint64_t bd = make_smem_desc(xs + S::X_CHUNK, 16, 1024, kLayoutSW128);
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) { // 32 bytes of K per MMA
+                        const uint32_t acc = (kc > 0 || kk > 0) ? 1u : 0u;
+                        if constexpr (TF32)
+                            umma_ss_tf32_if(leader, d, ad + 2 * kk, bd + 2 * kk, idesc, acc);
+                        else
+                            umma_ss_if(leader, d, ad + 2 * kk, bd + 2 * kk, idesc, acc);
+                    }
+                    tc_commit_if(leader, &empty[st]);
+                }
+                if (!ok)
+                    break;
+                tc_commit_if(leader, &acc_full[buf]);
+            }
+        }
+        tc_commit_if(leader, drain);
+        __syncwarp();
+        vqs_wait_drain(drain, 0, err);
+    } else {
+        // --------------------------------------------------------- epilogue
+        const int r = (warp << 5) + lane; // TMEM lane == row within the tile
+        const uint32_t lane_base = static_cast<uint32_t>(warp << 5) << 16;
+        int n_acc = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
+            const int rt = u / p.slices, sl = u % p.slices;
+            const int c_begin = sl * p.slice_codes;
+            const int c_end = min(p.codes, c_begin + p.slice_codes);
+            const int row = rt * 128 + r;
+            const bool live = row < p.rows;
+            const float xn = live ? p.xn[row] : 0.f;
+            // kVqsCand: the row's approximate best and its window edge.
+            float thr = INFINITY;
+            if (MODE == kVqsCand && live) {
+                const unsigned long long key = p.keys[row];
+                if (key != ~0ull) {
+                    const int b = static_cast<int>(key & 0xffffffffu);
+                    const float best = vqs_from_order_bits(static_cast<uint32_t>(key >> 32));
+                    const float cb = static_cast<const float *>(p.cbnorm)[b];
+                    thr = best + p.delta * (xn + cb);
+                }
+                if (!(thr < INFINITY)) // non-finite: every code is a candidate
+                    thr = INFINITY;
+            }
+            const __nv_bfloat162 x2 = __float2bfloat162_rn(xn);
+            const __nv_bfloat162 neg2 = __floats2bfloat162_rn(-2.f, -2.f);
+            float best = INFINITY;
+            int best_id = 0;
+            for (int c = c_begin; c < c_end; c += 256, ++n_acc) {
+                const int buf = n_acc & 1;
+                ok = __all_sync(0xffffffffu,
+                                mbar_wait(&acc_full[buf], (n_acc >> 1) & 1, err, kErrWaitS));
+                if (!ok)
+                    break;
+                tc_fence_after();
+#pragma unroll 1
+                for (int ch = 0; ch < 8; ++ch) {
+                    uint32_t dv[32];
+                    tmem_ld32(tmem + lane_base + buf * 256 + ch * 32, dv);
+                    const int code0 = c + ch * 32;
+                    tmem_wait_ld();
+                    if (!live || code0 >= p.codes)
+                        continue;
+                    if constexpr (MODE == kVqsBf16) {
+                        const unsigned short *cs = static_cast<const unsigned short *>(p.cbnorm);
+                        float cmin = INFINITY;
+                        float dist[32];
+#pragma unroll
+                        for (int q = 0; q < 16; ++q) {
+                            const int k0 = code0 + 2 * q;
+                            const unsigned short h0 = k0 < p.codes ? cs[k0] : 0;
+                            const unsigned short h1 = k0 + 1 < p.codes ? cs[k0 + 1] : 0;
+                            const uint32_t cw = h0 | (static_cast<uint32_t>(h1) << 16);
+                            const __nv_bfloat162 c2 = *reinterpret_cast<const __nv_bfloat162 *>(&cw);
+                            const __nv_bfloat162 dd = __floats2bfloat162_rn(__uint_as_float(dv[2 * q]),
+                                                                            __uint_as_float(dv[2 * q + 1]));
+                            const __nv_bfloat162 s2 = __hadd2(x2, c2);
+                            const __nv_bfloat162 t = __hfma2(dd, neg2, s2);
+                            dist[2 * q] = k0 < p.codes ? __bfloat162float(t.x) : INFINITY;
+                            dist[2 * q + 1] = k0 + 1 < p.codes ? __bfloat162float(t.y) : INFINITY;
+                            cmin = fminf(cmin, fminf(dist[2 * q], dist[2 * q + 1]));
+                        }
+                        if (cmin < best) {
+                            best = cmin;
+#pragma unroll
+                            for (int e = 31; e >= 0; --e)
+                                if (dist[e] == cmin)
+                                    best_id = code0 + e;
+                        }
+                    } else {
+                        const float *cn = static_cast<const float *>(p.cbnorm);
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) {
+                            const int k = code0 + e;
+                            if (k >= p.codes)
+                                break;
+                            const float cnk = cn[k];
+                            const float dist = fmaf(-2.f, __uint_as_float(dv[e]), xn + cnk);
+                            if constexpr (MODE == kVqsApprox) {
+                                if (dist < best) {
+                                    best = dist;
+                                    best_id = k;
+                                }
+                            } else {
+                                // Candidate unless provably outside the window.
+                                const float lo = dist - p.delta * (xn + cnk);
+                                if (!(lo <= thr) && isfinite(lo) && thr < INFINITY)
+                                    continue;
+                                const unsigned slot = atomicAdd(p.cand_count + row, 1u);
+                                if (slot < static_cast<unsigned>(kVqCandCap))
+                                    p.cand[static_cast<long long>(row) * kVqCandCap + slot] =
+                                        static_cast<unsigned>(k);
+                            }
+                        }
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0)
+                    mbar_arrive(&acc_empty[buf]);
+            }
+            if (MODE != kVqsCand && ok && live && best < INFINITY) {
+                const unsigned long long key =
+                    (static_cast<unsigned long long>(vqs_order_bits(best)) << 32) |
+                    static_cast<unsigned>(best_id);
+                atomicMin(p.keys + row, key);
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 5)
+        tmem_dealloc(tmem, 512);
+}
+
+// Exact fp64 re-scoring of the candidates, one warp per row; rows whose list
+// overflowed are scored against every code.  The winner is the smallest
+// (direct distance, id) with a distance below +inf (src/cpu.cpp:272-282);
+// a row without one keeps id 0.
+__global__ void vq_refine_fp64(const float *x, const float *codebook, const unsigned *cand_count,
+                               const unsigned *cand, void *ids, int rows, int dim, int codes,
+                               int ids_u16) {
+    const int warps = (gridDim.x * blockDim.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    for (int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < rows; row += warps) {
+        const unsigned n = cand_count[row];
+        const bool brute = n > static_cast<unsigned>(kVqCandCap);
+        const int count = brute ? codes : static_cast<int>(n);
+        const float *xr = x + static_cast<long long>(row) * dim;
+        double best = INFINITY;
+        unsigned best_id = 0xffffffffu;
+        for (int j = lane; j < count; j += 32) {
+            const unsigned code = brute ? static_cast<unsigned>(j)
+                                        : cand[static_cast<long long>(row) * kVqCandCap + j];
+            const float *cr = codebook + static_cast<long long>(code) * dim;
+            double direct = 0.0;
+            for (int k = 0; k < dim; ++k) {
+                const double delta = static_cast<double>(xr[k]) - static_cast<double>(cr[k]);
+                direct = __dadd_rn(direct, __dmul_rn(delta, delta));
+            }
+            if (direct < best || (direct == best && code < best_id)) {
+                best = direct;
+                best_id = code;
+            }
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const double ob = __shfl_xor_sync(0xffffffffu, best, off);
+            const unsigned oi = __shfl_xor_sync(0xffffffffu, best_id, off);
+            if (ob < best || (ob == best && oi < best_id)) {
+                best = ob;
+                best_id = oi;
+            }
+        }
+        if (lane == 0) {
+            const unsigned id = best < INFINITY ? best_id : 0u;
+            if (ids_u16)
+                static_cast<uint16_t *>(ids)[row] = static_cast<uint16_t>(id);
+            else
+                static_cast<int32_t *>(ids)[row] = static_cast<int32_t>(id);
+        }
+    }
+}
+
+__global__ void vqs_finish(const unsigned long long *keys, void *ids, int rows, int ids_u16) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < rows; i += gridDim.x * blockDim.x) {
+        const unsigned long long k = keys[i];
+        // An untouched key means every distance was NaN: the reference keeps id 0.
+        const unsigned id = k == ~0ull ? 0u : static_cast<unsigned>(k & 0xffffffffu);
+        if (ids_u16)
+            static_cast<uint16_t *>(ids)[i] = static_cast<uint16_t>(id);
+        else
+            static_cast<int32_t *>(ids)[i] = static_cast<int32_t>(id);
+    }
+}
+
+__global__ void vqs_init(unsigned long long *keys, unsigned *cand_count, int rows) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < rows; i += gridDim.x * blockDim.x) {
+        keys[i] = ~0ull;
+        if (cand_count)
+            cand_count[i] = 0u;
+    }
+}
+
+// ------------------------------------------------------------------ host side
+namespace {
+template <bool TF32, int MODE> int vqs_launch_typed(const VqsParams &p, int grid, cudaStream_t stream) {
+    using S = VqsShape<TF32>;
+    static std::once_flag once;
+    static cudaError_t attr = cudaSuccess;
+    std::call_once(once, [] {
+        attr = cudaFuncSetAttribute(vq_stream_kernel<TF32, MODE>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM_BYTES);
+    });
+    if (attr != cudaSuccess)
+        return static_cast<int>(attr);
+    vq_stream_kernel<TF32, MODE><<<grid, kVqsThreads, S::SMEM_BYTES, stream>>>(p);
+    return static_cast<int>(cudaGetLastError());
+}
+
+int sm_count() {
+    int sms = 148, dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess)
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return sms;
+}
+
+// Units = 128-row tiles x codebook slices, about 8 units per SM.
+int plan_units(VqsParams &p) {
+    const int sms = sm_count();
+    const int row_tiles = (p.rows + 127) / 128;
+    const int code_tiles = (p.codes + 255) / 256;
+    int slices = (8 * sms + row_tiles - 1) / row_tiles;
+    slices = slices < 1 ? 1 : slices > code_tiles ? code_tiles : slices;
+    const int tiles_per_slice = (code_tiles + slices - 1) / slices;
+    p.slice_codes = tiles_per_slice * 256;
+    p.slices = (code_tiles + tiles_per_slice - 1) / tiles_per_slice;
+    const long long units = static_cast<long long>(row_tiles) * p.slices;
+    return static_cast<int>(units < sms ? units : sms);
+}
+} // namespace
+
+size_t vq_stream_workspace(size_t rows, int profile_fp32) {
+    // keys (8) + xn (4) [+ candidate count (4) + candidate list] per row.
+    const size_t per_row = profile_fp32 ? 16 + 4 * static_cast<size_t>(kVqCandCap) : 12;
+    return (rows * per_row + 255) / 256 * 256;
+}
+
+int vq_stream_launch(const VqArgs &a, int profile_fp32, cudaStream_t stream) {
+    VqsParams p{};
+    const bool tf32 = profile_fp32 != 0;
+    const int kc = tf32 ? 32 : 64;
+    int rc = tf32 ? make_map_2d_f32(&p.tx, a.x, a.dim, a.rows, kc, 128)
+                  : make_map_2d(&p.tx, a.x, a.dim, a.rows, kc, 128);
+    if (rc)
+        return rc;
+    rc = tf32 ? make_map_2d_f32(&p.tc, a.codebook, a.dim, a.codes, kc, 256)
+              : make_map_2d(&p.tc, a.codebook, a.dim, a.codes, kc, 256);
+    if (rc)
+        return rc;
+    // Workspace carve: keys | xn | cand_count | cand.
+    uint8_t *ws = static_cast<uint8_t *>(a.keys);
+    const size_t rows = static_cast<size_t>(a.rows);
+    p.keys = reinterpret_cast<unsigned long long *>(ws);
+    p.xn = reinterpret_cast<float *>(ws + 8 * rows);
+    if (tf32) {
+        p.cand_count = reinterpret_cast<unsigned *>(ws + 12 * rows);
+        p.cand = reinterpret_cast<unsigned *>(ws + 16 * rows);
+    }
+    p.cbnorm = a.cbnorm;
+    p.rows = a.rows;
+    p.dim = a.dim;
+    p.codes = a.codes;
+    p.chunks = (a.dim + kc - 1) / kc;
+    p.delta = static_cast<float>((std::ldexp(1.0, -8) + (2.0 * a.dim + 8) * std::ldexp(1.0, -23)) *
+                                 1.0001);
+    p.err = a.err;
+    const int grid = plan_units(p);
+    const int threads = 256;
+    const int kb = (a.rows + threads - 1) / threads;
+    vqs_init<<<kb < 4096 ? kb : 4096, threads, 0, stream>>>(p.keys, p.cand_count, a.rows);
+    // |x|^2 per row in the profile's arithmetic (bf16 profile: the bf16 value).
+    if ((rc = squares_launch(a.x, p.xn, a.rows, a.dim, tf32 ? 0 : 1, 0, stream)))
+        return rc;
+    if (!tf32) {
+        if ((rc = vqs_launch_typed<false, kVqsBf16>(p, grid, stream)))
+            return rc;
+        vqs_finish<<<kb < 4096 ? kb : 4096, threads, 0, stream>>>(p.keys, a.ids, a.rows, a.ids_u16);
+        return static_cast<int>(cudaGetLastError());
+    }
+    if ((rc = vqs_launch_typed<true, kVqsApprox>(p, grid, stream)) ||
+        (rc = vqs_launch_typed<true, kVqsCand>(p, grid, stream)))
+        return rc;
+    const int rb = (a.rows * 32 + threads - 1) / threads;
+    vq_refine_fp64<<<rb < 8192 ? rb : 8192, threads, 0, stream>>>(
+        static_cast<const float *>(a.x), static_cast<const float *>(a.codebook), p.cand_count,
+        p.cand, a.ids, a.rows, a.dim, a.codes, a.ids_u16);
+    return static_cast<int>(cudaGetLastError());
+}
+
+} // namespace omni_b200

@@ -26,31 +26,33 @@ def ob():
     return load_package()
 
 
-def _gpu_quantize(ob, x, cb, ids_u16=True):
+def _gpu_quantize(ob, x, cb, ids_u16=True, profile=1):
+    """profile 1 = BF16 (inputs cast to bf16), 0 = F32."""
     lib = ob.library()
     rows, dim = x.shape
     codes = cb.shape[0]
-    tx = torch.from_numpy(x).to(torch.bfloat16).cuda()
-    tc = torch.from_numpy(cb).to(torch.bfloat16).cuda()
-    norms = torch.empty(codes, dtype=torch.bfloat16, device="cuda")
+    dt = torch.bfloat16 if profile == 1 else torch.float32
+    tx = torch.from_numpy(x).to(dt).cuda()
+    tc = torch.from_numpy(cb).to(dt).cuda()
+    norms = torch.empty(codes, dtype=dt, device="cuda")
     stream = torch.cuda.current_stream().cuda_stream
-    lib.check(lib.lib.omni_b200_squares(tc.data_ptr(), norms.data_ptr(), codes, dim, 1, 1, stream))
-    ws_bytes = lib.lib.omni_b200_vq_workspace(rows, dim, codes, 1)
+    lib.check(lib.lib.omni_b200_squares(tc.data_ptr(), norms.data_ptr(), codes, dim, profile, profile, stream))
+    ws_bytes = lib.lib.omni_b200_vq_workspace(rows, dim, codes, profile)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
     ids = torch.empty(rows, dtype=torch.int16 if ids_u16 else torch.int32, device="cuda")
     lib.check(lib.lib.omni_b200_vq_argmin(tx.data_ptr(), tc.data_ptr(), norms.data_ptr(), ids.data_ptr(), rows,
-                                          dim, codes, 1, int(ids_u16), ws.data_ptr(), ws_bytes, stream))
+                                          dim, codes, profile, int(ids_u16), ws.data_ptr(), ws_bytes, stream))
     lib.sync_check()
     out = ids.cpu().numpy()
     return (out.view(np.uint16).astype(np.int64) if ids_u16 else out.astype(np.int64)), norms
 
 
-def _check(x, cb, got, allowed_rounding_flips=0.002):
-    want = O.quantize(x, cb, bf16=True).astype(np.int64)
+def _check(x, cb, got, allowed_rounding_flips=0.002, bf16=True):
+    want = O.quantize(x, cb, bf16=bf16).astype(np.int64)
     mism = np.nonzero(got != want)[0]
     if len(mism) == 0:
         return 0
-    d1, d2 = O.quantize_top2(x[mism], cb, bf16=True)
+    d1, d2 = O.quantize_top2(x[mism], cb, bf16=bf16)
     near_tie = (d2 - d1) < 1e-3 * np.abs(d1)
     # Remaining rows: the chosen code must be within one bf16 ulp of the best
     # under the reference's own distance (dot rounding-order flips only).
@@ -96,3 +98,61 @@ def test_vq_int32_ids_and_normalised_image_features(ob):
     x, cb = O.round_bf16(x), O.round_bf16(cb)
     got, _ = _gpu_quantize(ob, x, cb, ids_u16=False)
     _check(x, cb, got)
+
+
+# ---------------------------------------------------------------- wide codes
+@pytest.mark.parametrize("rows,dim,codes", [(300, 1280, 2051), (130, 2048, 1024), (200, 136, 999)])
+def test_vq_bf16_wide_dims_match_oracle(ob, rows, dim, codes):
+    """Production code widths (1280 audio, 2048 image) take the K-streamed kernel."""
+    rng = np.random.default_rng(rows * 7 + dim)
+    x = O.round_bf16(rng.standard_normal((rows, dim)).astype(np.float32))
+    cb = O.round_bf16(rng.standard_normal((codes, dim)).astype(np.float32))
+    cb[min(9, codes - 1)] = x[1]
+    got, norms = _gpu_quantize(ob, x, cb)
+    assert np.array_equal(norms.float().cpu().numpy(), O.squares(cb, bf16=True))
+    assert got[1] == min(9, codes - 1) or O.quantize(x[1:2], cb, bf16=True)[0] == got[1]
+    _check(x, cb, got)
+
+
+# ---------------------------------------------------------------- fp32 profile
+@pytest.mark.parametrize("rows,dim,codes", [(777, 64, 4099), (300, 32, 16384), (129, 1280, 1500), (64, 12, 300)])
+def test_vq_fp32_matches_oracle(ob, rows, dim, codes):
+    """fp32 profile: the refined ids must equal the reference's (exact fp64 re-scoring)."""
+    rng = np.random.default_rng(rows + 3 * dim + codes)
+    x = rng.standard_normal((rows, dim)).astype(np.float32)
+    cb = rng.standard_normal((codes, dim)).astype(np.float32)
+    cb[min(11, codes - 1)] = x[2]
+    got, norms = _gpu_quantize(ob, x, cb, profile=0)
+    assert np.array_equal(norms.cpu().numpy(), O.squares(cb, bf16=False))
+    want = O.quantize(x, cb, bf16=False).astype(np.int64)
+    assert np.array_equal(got, want), f"{int((got != want).sum())} rows differ"
+
+
+def test_vq_fp32_refinement_known_answer(ob):
+    """tests/native_vq_cases.h:6-30: cancellation and fp32 overflow -> ids {1024, 3, 1026}."""
+    rows, width, codes = 3, 1280, 1027
+    x = np.full((rows, width), 1000.0, np.float32)
+    cb = np.full((codes, width), 1000.25, np.float32)
+    x[1] = 1002.0
+    x[2] = 1e20
+    cb[7] = 1000.0 + 1.0 / 1024
+    cb[1024] = x[0]
+    cb[1025] = x[0]
+    cb[3] = x[1]
+    cb[1026] = x[2]
+    got, _ = _gpu_quantize(ob, x, cb, profile=0)
+    assert got.tolist() == [1024, 3, 1026]
+
+
+def test_vq_fp32_ties_and_nan_rows(ob):
+    """Duplicates across tiles -> smallest id; a NaN row keeps id 0 (src/cpu.cpp:276)."""
+    rows, width, codes = 9, 16, 2051
+    x = np.array([(int(i * 7 % 13) - 6) * 0.25 for i in range(rows * width)], np.float32).reshape(rows, width)
+    cb = np.array([(int(i * 11 % 17) - 8) * 0.25 for i in range(codes * width)], np.float32).reshape(codes, width)
+    for index in (7, 1024, codes - 1):
+        cb[index] = x[0]
+    x[5, 3] = np.nan
+    got, _ = _gpu_quantize(ob, x, cb, profile=0, ids_u16=False)
+    want = O.quantize(x, cb, bf16=False).astype(np.int64)
+    assert got[0] == 7 and got[5] == 0
+    assert np.array_equal(got, want)
