@@ -25,8 +25,12 @@
 // whose minimum is the smallest distance and, among equal distances, the
 // smallest id -- the reference's tie rule.
 //
-// Roles: warp 4 TMA producer, warp 5 TMEM owner + tcgen05.mma issuer,
-// warps 0-3 epilogue (thread r owns TMEM lane r = row r of the tile).
+// Roles: warp 16 TMA producer, warp 17 TMEM owner + tcgen05.mma issuer,
+// warps 0-15 epilogue: warp w reads TMEM lane quarter w % 4 (rows
+// 32 (w % 4) .. +31 of the tile) and accumulator columns [64 (w / 4), +64), so
+// each sub-partition runs four epilogue warps and hides the TMEM-load and
+// norm-load latency; every warp keeps its own running best per row and ends
+// a unit with one atomicMin per row.
 // TMEM: two 256-column fp32 accumulators (512 columns).
 #include "sm100.cuh"
 #include "tma.h"
@@ -57,7 +61,10 @@ template <int DP> struct VqShape {
     static_assert(C1 == 0 || C1 == 16 || C1 == 32 || C1 == 64, "unsupported dim padding");
 };
 
-constexpr int kVqThreads = 192;
+constexpr int kVqThreads = 576;
+constexpr int kVqEpiWarps = 16;
+constexpr int kVqProducerWarp = 16;
+constexpr int kVqMmaWarp = 17;
 
 __device__ __forceinline__ uint32_t order_bits(float f) {
     const uint32_t u = __float_as_uint(f);
@@ -109,12 +116,12 @@ __global__ void __launch_bounds__(kVqThreads, 1) vq_bf16_kernel(const __grid_con
         }
         mbar_init(&acc_full[0], 1);
         mbar_init(&acc_full[1], 1);
-        mbar_init(&acc_empty[0], 128);
-        mbar_init(&acc_empty[1], 128);
+        mbar_init(&acc_empty[0], kVqEpiWarps); // one arrive per epilogue warp
+        mbar_init(&acc_empty[1], kVqEpiWarps);
         mbar_init(drain, 1);
         fence_mbarrier_init();
     }
-    if (warp == 5) {
+    if (warp == kVqMmaWarp) {
         tmem_alloc(tmem_holder, 512);
         tmem_relinquish();
     }
@@ -123,7 +130,7 @@ __global__ void __launch_bounds__(kVqThreads, 1) vq_bf16_kernel(const __grid_con
     tc_fence_after();
     const uint32_t tmem = *tmem_holder;
 
-    if (warp == 4) {
+    if (warp == kVqProducerWarp) {
         // ------------------------------------------------------ TMA producer
         if (lane == 0) {
             tma_prefetch_desc(&p.tx0);
@@ -162,7 +169,7 @@ __global__ void __launch_bounds__(kVqThreads, 1) vq_bf16_kernel(const __grid_con
                 vq_wait_drain(&c_full[j % S::STAGES], (j / S::STAGES) & 1, err);
         }
         __syncwarp();
-    } else if (warp == 5) {
+    } else if (warp == kVqMmaWarp) {
         // ------------------------------------------------------ MMA issuer
         if (lane == 0) {
             constexpr uint32_t idesc = make_idesc_f16(128, 256, true, false);
@@ -209,8 +216,9 @@ __global__ void __launch_bounds__(kVqThreads, 1) vq_bf16_kernel(const __grid_con
         __syncwarp();
     } else {
         // --------------------------------------------------------- epilogue
-        const int r = (warp << 5) + lane; // TMEM lane == row within the tile
-        const uint32_t lane_base = static_cast<uint32_t>(warp << 5) << 16;
+        const int qd = warp & 3, cg = warp >> 2;   // lane quarter, 64-column group
+        const int r = (qd << 5) + lane;            // TMEM lane == row within the tile
+        const uint32_t lane_base = static_cast<uint32_t>(qd << 5) << 16;
         const __nv_bfloat16 *x = static_cast<const __nv_bfloat16 *>(p.x);
         const uint4 *cn = static_cast<const uint4 *>(p.cbnorm);
         const __nv_bfloat162 neg2 = __floats2bfloat162_rn(-2.f, -2.f);
@@ -221,13 +229,26 @@ __global__ void __launch_bounds__(kVqThreads, 1) vq_bf16_kernel(const __grid_con
             const int c_begin = sl * p.slice_codes;
             const int c_end = min(p.codes, c_begin + p.slice_codes);
             const int row = rt * 128 + r;
-            // |x|^2 in column order (src/cpu.cpp:216-226), bf16 profile.
+            // |x|^2 in column order (src/cpu.cpp:216-226), bf16 profile: the
+            // row is fetched with independent 16-byte loads (dim % 8 == 0),
+            // then summed sequentially; padding columns add +0.
             float xn = 0.f;
             if (row < p.rows) {
-                const __nv_bfloat16 *xr = x + static_cast<long long>(row) * p.dim;
-                for (int j = 0; j < p.dim; ++j) {
-                    const float v = __bfloat162float(xr[j]);
-                    xn += __bfloat162float(__float2bfloat16_rn(v * v));
+                const uint4 *xr =
+                    reinterpret_cast<const uint4 *>(x + static_cast<long long>(row) * p.dim);
+                uint4 xw[DP / 8];
+#pragma unroll
+                for (int q = 0; q < DP / 8; ++q)
+                    xw[q] = q * 8 < p.dim ? __ldg(xr + q) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+                for (int q = 0; q < DP / 8; ++q) {
+                    const __nv_bfloat162 *h2 = reinterpret_cast<const __nv_bfloat162 *>(&xw[q]);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 v = __bfloat1622float2(h2[e]);
+                        xn = __fadd_rn(xn, __bfloat162float(__float2bfloat16_rn(__fmul_rn(v.x, v.x))));
+                        xn = __fadd_rn(xn, __bfloat162float(__float2bfloat16_rn(__fmul_rn(v.y, v.y))));
+                    }
                 }
             }
             const __nv_bfloat162 x2 = __float2bfloat162_rn(xn); // rounds: bf16(sum)
@@ -241,10 +262,13 @@ __global__ void __launch_bounds__(kVqThreads, 1) vq_bf16_kernel(const __grid_con
                     break;
                 tc_fence_after();
                 const bool partial = c + 256 > p.codes;
-#pragma unroll 1
-                for (int ch = 0; ch < 8; ++ch) {
-                    uint32_t d[32];
-                    tmem_ld32(tmem + lane_base + buf * 256 + ch * 32, d);
+                uint32_t dd2[2][32];
+                tmem_ld32(tmem + lane_base + buf * 256 + cg * 64, dd2[0]);
+                tmem_ld32(tmem + lane_base + buf * 256 + cg * 64 + 32, dd2[1]);
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int ch = cg * 2 + h;
+                    uint32_t *d = dd2[h];
                     const int code0 = c + ch * 32;
                     uint4 cnv[4];
                     if (!partial) {
@@ -254,19 +278,20 @@ __global__ void __launch_bounds__(kVqThreads, 1) vq_bf16_kernel(const __grid_con
                     } else {
                         // Last tile: read only norms that exist.
                         const unsigned short *cs = static_cast<const unsigned short *>(p.cbnorm);
-                        unsigned short h[32];
+                        unsigned short hv[32];
 #pragma unroll
                         for (int e = 0; e < 32; ++e)
-                            h[e] = code0 + e < p.codes ? cs[code0 + e] : 0;
+                            hv[e] = code0 + e < p.codes ? cs[code0 + e] : 0;
 #pragma unroll
                         for (int w = 0; w < 4; ++w) {
-                            cnv[w].x = h[8 * w] | (static_cast<uint32_t>(h[8 * w + 1]) << 16);
-                            cnv[w].y = h[8 * w + 2] | (static_cast<uint32_t>(h[8 * w + 3]) << 16);
-                            cnv[w].z = h[8 * w + 4] | (static_cast<uint32_t>(h[8 * w + 5]) << 16);
-                            cnv[w].w = h[8 * w + 6] | (static_cast<uint32_t>(h[8 * w + 7]) << 16);
+                            cnv[w].x = hv[8 * w] | (static_cast<uint32_t>(hv[8 * w + 1]) << 16);
+                            cnv[w].y = hv[8 * w + 2] | (static_cast<uint32_t>(hv[8 * w + 3]) << 16);
+                            cnv[w].z = hv[8 * w + 4] | (static_cast<uint32_t>(hv[8 * w + 5]) << 16);
+                            cnv[w].w = hv[8 * w + 6] | (static_cast<uint32_t>(hv[8 * w + 7]) << 16);
                         }
                     }
-                    tmem_wait_ld();
+                    if (h == 0)
+                        tmem_wait_ld();
                     __nv_bfloat162 dist[16];
                     __nv_bfloat162 m2 = __floats2bfloat162_rn(INFINITY, INFINITY);
 #pragma unroll
@@ -304,7 +329,9 @@ __global__ void __launch_bounds__(kVqThreads, 1) vq_bf16_kernel(const __grid_con
                     }
                 }
                 tc_fence_before();
-                mbar_arrive(&acc_empty[buf]);
+                __syncwarp();
+                if (lane == 0)
+                    mbar_arrive(&acc_empty[buf]);
             }
             if (ok && row < p.rows) {
                 const unsigned long long key =
@@ -319,7 +346,7 @@ __global__ void __launch_bounds__(kVqThreads, 1) vq_bf16_kernel(const __grid_con
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 5)
+    if (warp == kVqMmaWarp)
         tmem_dealloc(tmem, 512);
 }
 
