@@ -44,6 +44,17 @@ namespace omni_b200 {
 #ifndef OMNI_FMHA_PT
 #define OMNI_FMHA_PT 1
 #endif
+#ifndef OMNI_FMHA_SEP
+#define OMNI_FMHA_SEP 0
+#endif
+
+// Columns of one O tile in TMEM (the PV MMA's N).  Head dims <= 64 with the
+// SEP layout: exactly the head dim, so that each query tile gets P columns of
+// its own.  Otherwise one spare column past the head dim for the row-sum
+// column of ones (64 -> 80, 96 -> 112).
+__host__ __device__ constexpr int head_out_cols(int hdp) {
+    return (OMNI_FMHA_SEP && hdp <= 64) ? hdp : hdp == 64 ? 80 : hdp == 96 ? 112 : hdp;
+}
 #ifndef OMNI_FMHA_QBUF
 #define OMNI_FMHA_QBUF (HDP <= 96 ? 2 : 1)
 #endif
@@ -58,9 +69,8 @@ template <int HDP> struct FmhaShape {
     // V tiles keep chunk 1 as a full 64-column 128-byte-swizzle atom (zero
     // filled past the head dim) so that O += P V is ONE MMA of N = HDP per
     // 16-key step: its two MN atoms are LBO = 16 KB apart.
-    // PV output width: one spare column past the head dim for the row-sum
-    // column of ones (64 -> 80, 96 -> 112); O_i occupies HDPO <= 128 columns.
-    static constexpr int HDPO = HDP == 64 ? 80 : HDP == 96 ? 112 : HDP;
+    // PV output width (O_i occupies HDPO <= 128 columns), see head_out_cols.
+    static constexpr int HDPO = head_out_cols(HDP);
     static constexpr int V_BYTES = HDPO > 64 ? 2 * 128 * 128 : TILE_BYTES;
     static constexpr int V_CH0 = 128 * ROW0;
     // HDPO <= 80 (PT schedule): P gets TMEM columns of its own, the 48 free
@@ -71,6 +81,12 @@ template <int HDP> struct FmhaShape {
     // softmax's critical path.  Wider heads write P over S (no spare columns).
     static constexpr bool PT = OMNI_FMHA_PT && HDPO <= 80;
     static constexpr uint32_t kPcol0 = 256 + 80, kPcol1 = 384 + 80;
+    // SEP (head dims <= 64): TMEM = S_0 | S_1 | O_0 | O_1 | P_0 | P_1 with
+    // 64-column O and P tiles, so each tile has P columns of its own and
+    // waits only for its own previous O += P V before writing P.
+    static constexpr bool SEP = PT && OMNI_FMHA_SEP && HDP <= 64;
+    static constexpr uint32_t O_STRIDE = SEP ? 64 : 128; // O_1 - O_0 in columns
+    __host__ __device__ static constexpr uint32_t p_col(int i) { return 384 + 64 * i; }
     static constexpr int QBUF = OMNI_FMHA_QBUF; // Q buffers (2: next item prefetch)
     static constexpr int BUDGET = 226 * 1024 - 8 * 1024;
     static constexpr int STAGES_RAW = (BUDGET - QBUF * 2 * TILE_BYTES) / (TILE_BYTES + V_BYTES);
@@ -473,14 +489,16 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
             };
             // O_i += P_i V_st with P in its own TMEM columns (PT).
             auto pv_pt = [&](int i, int st, bool accumulate) {
-                const uint32_t d = tmem + 256 + i * 128;
+                const uint32_t d = tmem + 256 + i * S::O_STRIDE;
                 const uint32_t vb = sv + st * S::V_BYTES;
                 constexpr uint32_t vrow = S::HDPO >= 64 ? 128 : S::ROW0;
                 const uint64_t v0 = make_smem_desc(vb, S::V_CH0, 8 * vrow,
                                                    S::HDPO >= 64 ? kLayoutSW128 : lay0);
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk)
-                    umma_ts_if(leader, d, tmem + (kk < 4 ? S::kPcol0 : S::kPcol1) + (kk & 3) * 8,
+                    umma_ts_if(leader, d,
+                               S::SEP ? tmem + S::p_col(i) + kk * 8
+                                      : tmem + (kk < 4 ? S::kPcol0 : S::kPcol1) + (kk & 3) * 8,
                                v0 + static_cast<uint64_t>((kk * 16 * vrow) >> 4), idesc_pv,
                                (accumulate || kk > 0) ? 1u : 0u);
             };
@@ -678,7 +696,7 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
         const int r = (qd << 5) + lane; // TMEM lane == row in tile
         const uint32_t lane_base = static_cast<uint32_t>(qd << 5) << 16;
         const uint32_t tS = tmem + lane_base + i * 128;
-        const uint32_t tO = tmem + lane_base + 256 + i * 128;
+        const uint32_t tO = tmem + lane_base + 256 + i * S::O_STRIDE;
         const float sl2 = p.scale_log2;
         const bool ones = S::HDPO > 64 && p.ones_col >= 0;
         constexpr int kOch = S::HDPO / 16, kEch = HDP / 16;
@@ -717,19 +735,21 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                         if (kv0 + c >= limit)
                             s[c] = -INFINITY;
                 }
-                // Row max: four independent 3-input max chains.
-                float m0 = fmax3(s[0], s[1], s[2]), m1 = fmax3(s[3], s[4], s[5]);
-                float m2 = fmax3(s[6], s[7], s[8]), m3 = fmax3(s[9], s[10], s[11]);
+                // Row max: eight independent 3-input max chains of 16 scores
+                // (short dependency chains; the max is latency-bound).
+                float mc[8];
 #pragma unroll
-                for (int c = 12; c < 124; c += 8) {
-                    m0 = fmax3(m0, s[c], s[c + 1]);
-                    m1 = fmax3(m1, s[c + 2], s[c + 3]);
-                    m2 = fmax3(m2, s[c + 4], s[c + 5]);
-                    m3 = fmax3(m3, s[c + 6], s[c + 7]);
+                for (int q = 0; q < 8; ++q) {
+                    const float *sq = s + 16 * q;
+                    float v = fmax3(sq[0], sq[1], sq[2]);
+#pragma unroll
+                    for (int e = 3; e < 15; e += 2)
+                        v = fmax3(v, sq[e], sq[e + 1]);
+                    mc[q] = fmaxf(v, sq[15]);
                 }
-                m0 = fmax3(m0, s[124], s[125]);
-                m1 = fmax3(m1, s[126], s[127]);
-                const float mnew = fmaxf(m, fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)) * sl2);
+                const float mt = fmax3(fmax3(mc[0], mc[1], mc[2]), fmax3(mc[3], mc[4], mc[5]),
+                                       fmaxf(mc[6], mc[7]));
+                const float mnew = fmaxf(m, mt * sl2);
                 // Lazy rescale: a row keeps its stale max while P stays below 2^8.
                 const bool grow = mnew > m + 8.0f;
                 const float alpha = (grow && j > 0) ? ex2_approx(m - mnew) : 1.f;
@@ -780,7 +800,18 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                     l += (a0 + a1) + (b0 + b1);
                 if (OMNI_FMHA_TURN)
                     warp_arrive(&turn[i ^ 1]); // the other tile's turn
-                if constexpr (S::PT) {
+                if constexpr (S::SEP) {
+                    // Own P columns: P_i(g) overwrites P_i(g-1) once
+                    // O_i += P_i(g-1) V is complete (which also allows the O
+                    // rescale).
+                    if (g > 0) {
+                        ok = __all_sync(0xffffffffu,
+                                        mbar_wait(&pv_done[i], (g - 1) & 1, err, kErrWaitO));
+                        if (!ok)
+                            break;
+                        tc_fence_after();
+                    }
+                } else if constexpr (S::PT) {
                     // The P columns are shared by the two tiles: tile 0 writes
                     // P(g) once O_1 += P_1(g-1) V is complete, tile 1 once
                     // O_0 += P_0(g) V is.  Each of those MMAs was issued after
@@ -811,7 +842,12 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                     }
                 }
                 __syncwarp();
-                if constexpr (S::PT) {
+                if constexpr (S::SEP) {
+                    tmem_st32(tmem + lane_base + S::p_col(i),
+                              *reinterpret_cast<uint32_t(*)[32]>(&sraw[0]));
+                    tmem_st32(tmem + lane_base + S::p_col(i) + 32,
+                              *reinterpret_cast<uint32_t(*)[32]>(&sraw[32]));
+                } else if constexpr (S::PT) {
                     tmem_st32(tmem + lane_base + S::kPcol0,
                               *reinterpret_cast<uint32_t(*)[32]>(&sraw[0]));
                     tmem_st32(tmem + lane_base + S::kPcol1,
@@ -837,16 +873,30 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                 ++n_items;
                 tc_fence_after();
             }
+            // The whole row of O (and the ones column) in one batch of TMEM
+            // loads with a single wait.
+            uint32_t ob[kOch][16];
+            if (it.T > 0) {
+#pragma unroll
+                for (int cq = 0; cq < kOch; ++cq)
+                    tmem_ld16(tO + cq * 16, ob[cq]);
+                tmem_wait_ld();
+            } else {
+#pragma unroll
+                for (int cq = 0; cq < kOch; ++cq)
+#pragma unroll
+                    for (int e = 0; e < 16; ++e)
+                        ob[cq][e] = 0u;
+            }
             if (ones && it.T > 0) {
                 // Row sum of P = O[:, ones_col] (rescaled together with O).
-                uint32_t o[16];
-                tmem_ld16(tO + (p.ones_col & ~15), o);
-                tmem_wait_ld();
-                const int e1 = p.ones_col & 15;
-                l = 0.f;
+                float lv = 0.f;
 #pragma unroll
-                for (int e = 0; e < 16; ++e)
-                    l = e == e1 ? __uint_as_float(o[e]) : l;
+                for (int cq = 0; cq < kOch; ++cq)
+#pragma unroll
+                    for (int e = 0; e < 16; ++e)
+                        lv = cq * 16 + e == p.ones_col ? __uint_as_float(ob[cq][e]) : lv;
+                l = lv;
             }
             const float inv = (it.T > 0 && l > 0.f) ? 1.f / l : 0.f;
             if (p.o_tma && it.T > 0) {
@@ -859,9 +909,7 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
 #pragma unroll
                 for (int cq = 0; cq < kEch; ++cq) {
                     const int c = cq * 16;
-                    uint32_t o[16];
-                    tmem_ld16(tO + c, o);
-                    tmem_wait_ld();
+                    const uint32_t *o = ob[cq];
                     uint4 w0, w1;
                     w0.x = pack2(__uint_as_float(o[0]) * inv, __uint_as_float(o[1]) * inv, BF16);
                     w0.y = pack2(__uint_as_float(o[2]) * inv, __uint_as_float(o[3]) * inv, BF16);
@@ -889,15 +937,7 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
 #pragma unroll
             for (int cq = 0; cq < kEch; ++cq) {
                 const int c = cq * 16;
-                uint32_t o[16];
-                if (it.T > 0) {
-                    tmem_ld16(tO + c, o);
-                    tmem_wait_ld();
-                } else {
-#pragma unroll
-                    for (int e = 0; e < 16; ++e)
-                        o[e] = 0u;
-                }
+                const uint32_t *o = ob[cq];
                 if (!store)
                     continue;
                 float v[16];
@@ -1031,7 +1071,7 @@ int fmha_launch(const FmhaArgs &a, cudaStream_t stream) {
     }
     // Row-sum column: V column `d` (first column past the data) holds 1.0 when
     // the PV output has room for it and the data ends on a 16-byte boundary.
-    const int hdpo = hdp == 64 ? 80 : hdp == 96 ? 112 : hdp;
+    const int hdpo = head_out_cols(hdp);
     const int dv = a.v.d;
     p.ones_col = (hdpo > 64 && dv >= 64 && dv % 8 == 0 && dv < hdpo) ? dv : -1;
     // V's second chunk: TMA loads only the data columns [64, dv), 16-byte
