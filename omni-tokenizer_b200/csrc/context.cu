@@ -15,9 +15,14 @@ namespace omni_b200 {
 int ctx_fail(int code, const char *msg);
 } // namespace omni_b200
 
+// Batch chunks of the pipelined host-buffer attention call.
+constexpr int kMaxChunks = 8;
+
 struct omni_b200_context {
     int device = 0;
-    cudaStream_t stream = nullptr;
+    cudaStream_t stream = nullptr;               // copies in (and every other call)
+    cudaStream_t s_compute = nullptr, s_out = nullptr;
+    cudaEvent_t ev_in[kMaxChunks] = {}, ev_done[kMaxChunks] = {};
     void *buf[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
     size_t cap[6] = {0, 0, 0, 0, 0, 0};
     std::atomic_flag running = ATOMIC_FLAG_INIT;
@@ -82,9 +87,22 @@ int omni_b200_context_create(int device, omni_b200_context **out) {
         delete c;
         return rc;
     }
-    if (int rc = cuda_status(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking),
-                             "stream create")) {
-        delete c;
+    int rc = cuda_status(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking),
+                         "stream create");
+    if (!rc)
+        rc = cuda_status(cudaStreamCreateWithFlags(&c->s_compute, cudaStreamNonBlocking),
+                         "stream create");
+    if (!rc)
+        rc = cuda_status(cudaStreamCreateWithFlags(&c->s_out, cudaStreamNonBlocking),
+                         "stream create");
+    for (int k = 0; !rc && k < kMaxChunks; ++k) {
+        rc = cuda_status(cudaEventCreateWithFlags(&c->ev_in[k], cudaEventDisableTiming), "event");
+        if (!rc)
+            rc = cuda_status(cudaEventCreateWithFlags(&c->ev_done[k], cudaEventDisableTiming),
+                             "event");
+    }
+    if (rc) {
+        omni_b200_context_free(c);
         return rc;
     }
     *out = c;
@@ -95,13 +113,21 @@ void omni_b200_context_free(omni_b200_context *c) {
     if (!c)
         return;
     cudaSetDevice(c->device);
-    if (c->stream)
-        cudaStreamSynchronize(c->stream);
+    for (cudaStream_t st : {c->stream, c->s_compute, c->s_out})
+        if (st)
+            cudaStreamSynchronize(st);
     for (void *b : c->buf)
         if (b)
             cudaFree(b);
-    if (c->stream)
-        cudaStreamDestroy(c->stream);
+    for (int k = 0; k < kMaxChunks; ++k) {
+        if (c->ev_in[k])
+            cudaEventDestroy(c->ev_in[k]);
+        if (c->ev_done[k])
+            cudaEventDestroy(c->ev_done[k]);
+    }
+    for (cudaStream_t st : {c->stream, c->s_compute, c->s_out})
+        if (st)
+            cudaStreamDestroy(st);
     delete c;
 }
 
@@ -131,28 +157,58 @@ int omni_b200_attention_bhld_host(omni_b200_context *c, const void *q, const voi
     if (lengths)
         if (int rc = reserve(c, 4, sizeof(int32_t) * batch))
             return rc;
-    const void *src[3] = {q, k, v};
-    for (int i = 0; i < 3; ++i)
-        if (int rc = cuda_status(
-                cudaMemcpyAsync(c->buf[i], src[i], in_bytes, cudaMemcpyHostToDevice, c->stream),
-                "copy in"))
-            return rc;
+    // Pipelined over batch chunks: chunk k's inputs are copied in on `stream`
+    // while chunk k-1 runs on `s_compute` and chunk k-2's output is copied out
+    // on `s_out` (host-to-device and device-to-host copies use separate copy
+    // engines), so the call costs about one pass over the inputs at PCIe rate.
+    const int chunks = batch < kMaxChunks ? batch : kMaxChunks;
+    const size_t item_elems = static_cast<size_t>(heads) * L * head_dim;
+    const size_t in_es = elem_size(dtype), out_es = elem_size(out_dtype);
     if (lengths)
         if (int rc = cuda_status(cudaMemcpyAsync(c->buf[4], lengths, sizeof(int32_t) * batch,
                                                  cudaMemcpyHostToDevice, c->stream),
                                  "copy lengths"))
             return rc;
-    int rc = omni_b200_attention_bhld(c->buf[0], c->buf[1], c->buf[2], c->buf[3], batch, heads, L,
-                                      head_dim, dtype, out_dtype,
-                                      lengths ? static_cast<const int32_t *>(c->buf[4]) : nullptr,
-                                      block, skip_padded_queries, scale, c->stream);
+    const void *src[3] = {q, k, v};
+    int rc = 0;
+    for (int ck = 0; ck < chunks && !rc; ++ck) {
+        const int b0 = static_cast<int>(static_cast<long long>(batch) * ck / chunks);
+        const int b1 = static_cast<int>(static_cast<long long>(batch) * (ck + 1) / chunks);
+        const size_t off_in = b0 * item_elems * in_es, len_in = (b1 - b0) * item_elems * in_es;
+        const size_t off_out = b0 * item_elems * out_es, len_out = (b1 - b0) * item_elems * out_es;
+        for (int i = 0; i < 3 && !rc; ++i)
+            rc = cuda_status(cudaMemcpyAsync(static_cast<char *>(c->buf[i]) + off_in,
+                                             static_cast<const char *>(src[i]) + off_in, len_in,
+                                             cudaMemcpyHostToDevice, c->stream),
+                             "copy in");
+        if (!rc)
+            rc = cuda_status(cudaEventRecord(c->ev_in[ck], c->stream), "event record");
+        if (!rc)
+            rc = cuda_status(cudaStreamWaitEvent(c->s_compute, c->ev_in[ck], 0), "stream wait");
+        if (!rc)
+            rc = omni_b200_attention_bhld(
+                static_cast<char *>(c->buf[0]) + off_in, static_cast<char *>(c->buf[1]) + off_in,
+                static_cast<char *>(c->buf[2]) + off_in, static_cast<char *>(c->buf[3]) + off_out,
+                b1 - b0, heads, L, head_dim, dtype, out_dtype,
+                lengths ? static_cast<const int32_t *>(c->buf[4]) + b0 : nullptr, block,
+                skip_padded_queries, scale, c->s_compute);
+        if (!rc)
+            rc = cuda_status(cudaEventRecord(c->ev_done[ck], c->s_compute), "event record");
+        if (!rc)
+            rc = cuda_status(cudaStreamWaitEvent(c->s_out, c->ev_done[ck], 0), "stream wait");
+        if (!rc)
+            rc = cuda_status(cudaMemcpyAsync(static_cast<char *>(out) + off_out,
+                                             static_cast<char *>(c->buf[3]) + off_out, len_out,
+                                             cudaMemcpyDeviceToHost, c->s_out),
+                             "copy out");
+    }
+    // Drain every stream before returning (also on errors), then report.
+    const int rc_in = cuda_status(cudaStreamSynchronize(c->stream), "copy in");
+    const int rc_k = omni_b200_sync_check(c->s_compute);
+    const int rc_out = cuda_status(cudaStreamSynchronize(c->s_out), "copy out");
     if (rc)
         return rc;
-    if ((rc = cuda_status(
-             cudaMemcpyAsync(out, c->buf[3], out_bytes, cudaMemcpyDeviceToHost, c->stream),
-             "copy out")))
-        return rc;
-    return omni_b200_sync_check(c->stream);
+    return rc_in ? rc_in : rc_k ? rc_k : rc_out;
 }
 
 int omni_b200_vq_argmin_host(omni_b200_context *c, const void *x, const void *codebook,
