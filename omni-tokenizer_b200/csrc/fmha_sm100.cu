@@ -47,6 +47,11 @@ namespace omni_b200 {
 #ifndef OMNI_FMHA_SEP
 #define OMNI_FMHA_SEP 0
 #endif
+// 1: two softmax warps per query row (each owns 64 of the 128 score columns
+// and they exchange row maxima per TMEM lane quarter); 0: one thread per row.
+#ifndef OMNI_FMHA_SPLIT
+#define OMNI_FMHA_SPLIT 0
+#endif
 
 // Columns of one O tile in TMEM (the PV MMA's N).  Head dims <= 64 with the
 // SEP layout: exactly the head dim, so that each query tile gets P columns of
@@ -84,7 +89,7 @@ template <int HDP> struct FmhaShape {
     // SEP (head dims <= 64): TMEM = S_0 | S_1 | O_0 | O_1 | P_0 | P_1 with
     // 64-column O and P tiles, so each tile has P columns of its own and
     // waits only for its own previous O += P V before writing P.
-    static constexpr bool SEP = PT && OMNI_FMHA_SEP && HDP <= 64;
+    static constexpr bool SEP = PT && OMNI_FMHA_SEP && !OMNI_FMHA_SPLIT && HDP <= 64;
     static constexpr uint32_t O_STRIDE = SEP ? 64 : 128; // O_1 - O_0 in columns
     __host__ __device__ static constexpr uint32_t p_col(int i) { return 384 + 64 * i; }
     static constexpr int QBUF = OMNI_FMHA_QBUF; // Q buffers (2: next item prefetch)
@@ -92,7 +97,9 @@ template <int HDP> struct FmhaShape {
     static constexpr int STAGES_RAW = (BUDGET - QBUF * 2 * TILE_BYTES) / (TILE_BYTES + V_BYTES);
     static constexpr int STAGES = STAGES_RAW > 4 ? 4 : STAGES_RAW;
     static constexpr int KSTEPS = HDP / 16;
-    static constexpr int BAR_BYTES = 512;
+    // Barriers, TMEM handle and (two warps per row) the row-max / row-sum
+    // exchange buffers.
+    static constexpr int BAR_BYTES = 1024 + 8192;
     // At least 120 KB so that one CTA (which allocates all 512 TMEM columns)
     // occupies an SM by itself.
     static constexpr int SMEM_RAW =
@@ -110,11 +117,19 @@ template <int HDP> struct FmhaShape {
 // warpgroups grow to 208 and the control warpgroup shrinks to 72
 // (8*32*208 + 4*32*72 = 62464 <= 384*168 = 64512 per CTA; 2*208 + 72 = 488
 // <= 512 per SM sub-partition).
-constexpr int kThreads = 384;
-constexpr int kSoftmaxRegs = 208;
-constexpr int kControlRegs = 72;
-constexpr int kProducerWarp = 8;
-constexpr int kMmaWarp = 9;
+//
+// OMNI_FMHA_SPLIT = 1: 20 warps, 0-7 softmax tile 0 and 8-15 tile 1 (warp w
+// serves lane quarter w % 4 and score columns [64 ((w / 4) % 2), +64)), 16-19
+// as warps 8-11 above; launch 96 registers, softmax 104, control 64
+// (16*32*104 + 4*32*64 = 61440 = 640*96; 4*104 + 64 = 480 per sub-partition).
+constexpr int kSplit = OMNI_FMHA_SPLIT;
+constexpr int kTileWarps = 4 << kSplit;        // softmax warps per query tile
+constexpr int kSoftWarps = 2 * kTileWarps;
+constexpr int kThreads = (kSoftWarps + 4) * 32;
+constexpr int kSoftmaxRegs = kSplit ? 104 : 208;
+constexpr int kControlRegs = kSplit ? 64 : 72;
+constexpr int kProducerWarp = kSoftWarps;
+constexpr int kMmaWarp = kSoftWarps + 1;
 
 // Loads one 128-row tile (both chunks) of a (token, head, batch) tensor.
 template <int HDP>
@@ -295,7 +310,6 @@ __device__ __forceinline__ bool load_q_tiles(const FmhaParams &p, int u, int nq,
 // shared-memory and tensor-memory accesses before lane 0's release), then
 // lane 0 arrives.  256 per-thread arrives on one barrier word would serialise
 // in the shared-memory atomic unit (~2 clk each, on the softmax critical path).
-constexpr int kTileWarps = 4;
 __device__ __forceinline__ void warp_arrive(uint64_t *bar) {
     __syncwarp();
     if ((threadIdx.x & 31) == 0)
@@ -326,7 +340,12 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
     uint64_t *turn = ebar + 2;                // [2] exp-phase hand-off between the tiles
     uint64_t *s_free = turn + 2;              // [2] softmax has read S_i (PT)
     uint64_t *pv_done = s_free + 2;           // [2] O_i += P_i V complete (PT)
-    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(pv_done + 2);
+    uint64_t *xq = pv_done + 2;               // [2 tiles][4 quarters] row-max exchange (split)
+    uint64_t *lq = xq + 8;                    // [2 tiles][4 quarters] row-sum exchange (split)
+    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(lq + 8);
+    // Exchange buffers (split): [2 parity][2 tile][4 quarter][2 half][32 lanes].
+    float *xmax = reinterpret_cast<float *>(bars + 128);
+    float *xsum = xmax + 2 * 2 * 4 * 2 * 32;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int items = p.batch * p.heads * ((p.L + 255) / 256);
@@ -350,6 +369,10 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
             mbar_init(&k_empty[s], 1);
             mbar_init(&v_full[s], 1);
             mbar_init(&v_empty[s], 1);
+        }
+        for (int e = 0; e < 8; ++e) {
+            mbar_init(&xq[e], 2); // the two warps of one lane quarter
+            mbar_init(&lq[e], 2);
         }
         mbar_init(o_full, 1);
         mbar_init(drain, 1);
@@ -688,19 +711,27 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
         __syncwarp();
     } else {
         // ------------------------------------------------- softmax warpgroups
-        // Tile i = warp / 4; warp w serves TMEM lane quarter w % 4 (fixed by
-        // the hardware) and each of its threads owns one query row: all 128
-        // score columns, the running max / sum and the row of O.
+        // Tile i = warp / kTileWarps; warp w serves TMEM lane quarter w % 4
+        // (fixed by the hardware).  One thread per row (kSplit = 0): all 128
+        // score columns, the running max / sum and the row of O.  Two warps per
+        // row (kSplit = 1): half hh = (w / 4) % 2 owns score columns
+        // [64 hh, 64 hh + 64) and half of O's column chunks; the two warps of a
+        // lane quarter exchange their row maxima through shared memory.
         setmaxnreg_inc<kSoftmaxRegs>();
-        const int i = warp >> 2, qd = warp & 3;
+        constexpr int kCols = 128 >> kSplit; // score columns per thread
+        const int i = warp / kTileWarps, hh = kSplit ? (warp >> 2) & 1 : 0, qd = warp & 3;
         const int r = (qd << 5) + lane; // TMEM lane == row in tile
         const uint32_t lane_base = static_cast<uint32_t>(qd << 5) << 16;
-        const uint32_t tS = tmem + lane_base + i * 128;
+        const uint32_t tS = tmem + lane_base + i * 128 + hh * kCols;
         const uint32_t tO = tmem + lane_base + 256 + i * S::O_STRIDE;
         const float sl2 = p.scale_log2;
         const bool ones = S::HDPO > 64 && p.ones_col >= 0;
         constexpr int kOch = S::HDPO / 16, kEch = HDP / 16;
-        int g = 0, n_items = 0;
+        // O column chunks this warp rescales / stores.
+        constexpr int kOsplit = kSplit ? (kOch + 1) / 2 : kOch, kEsplit = kSplit ? (kEch + 1) / 2 : kEch;
+        const int oc_begin = hh ? kOsplit : 0, oc_end = hh ? kOch : kOsplit;
+        const int ec_begin = hh ? kEsplit : 0, ec_end = hh ? kEch : kEsplit;
+        int g = 0, n_items = 0, n_sum = 0;
         bool ok = true;
         for (int u = blockIdx.x; ok && u < items; u += gridDim.x) {
             const Item it = decode_item(p, u);
@@ -716,9 +747,9 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                 if (!ok)
                     break;
                 tc_fence_after();
-                uint32_t sraw[128];
+                uint32_t sraw[kCols];
 #pragma unroll
-                for (int c = 0; c < 4; ++c)
+                for (int c = 0; c < kCols / 32; ++c)
                     tmem_ld32(tS + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&sraw[32 * c]));
                 tmem_wait_ld();
                 if constexpr (S::PT) {
@@ -727,19 +758,19 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                     warp_arrive(&s_free[i]);
                 }
                 float *s = reinterpret_cast<float *>(sraw);
-                const int kv0 = j * 128;
-                const bool masked = kv0 + 128 > limit;
+                const int kv0 = j * 128 + hh * kCols;
+                const bool masked = kv0 + kCols > limit;
                 if (masked) {
 #pragma unroll
-                    for (int c = 0; c < 128; ++c)
+                    for (int c = 0; c < kCols; ++c)
                         if (kv0 + c >= limit)
                             s[c] = -INFINITY;
                 }
-                // Row max: eight independent 3-input max chains of 16 scores
-                // (short dependency chains; the max is latency-bound).
-                float mc[8];
+                // Row max: independent 3-input max chains of 16 scores (short
+                // dependency chains; the max is latency-bound).
+                float mc[kCols / 16];
 #pragma unroll
-                for (int q = 0; q < 8; ++q) {
+                for (int q = 0; q < kCols / 16; ++q) {
                     const float *sq = s + 16 * q;
                     float v = fmax3(sq[0], sq[1], sq[2]);
 #pragma unroll
@@ -747,8 +778,24 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                         v = fmax3(v, sq[e], sq[e + 1]);
                     mc[q] = fmaxf(v, sq[15]);
                 }
-                const float mt = fmax3(fmax3(mc[0], mc[1], mc[2]), fmax3(mc[3], mc[4], mc[5]),
-                                       fmaxf(mc[6], mc[7]));
+#pragma unroll
+                for (int w = kCols / 32; w > 0; w >>= 1)
+#pragma unroll
+                    for (int q = 0; q < w; ++q)
+                        mc[q] = fmaxf(mc[q], mc[q + w]);
+                float mt = mc[0];
+                if constexpr (kSplit) {
+                    // Exchange with the other half of the row (double-buffered
+                    // by iteration parity).  After this wait both halves have
+                    // read their scores, so P may overwrite S (P-over-S layout).
+                    float *xm = xmax + ((((g & 1) * 2 + i) * 4 + qd) * 2) * 32;
+                    xm[hh * 32 + lane] = mt;
+                    warp_arrive(&xq[i * 4 + qd]);
+                    ok = __all_sync(0xffffffffu, mbar_wait(&xq[i * 4 + qd], g & 1, err, kErrWaitP));
+                    if (!ok)
+                        break;
+                    mt = fmaxf(mt, xm[(hh ^ 1) * 32 + lane]);
+                }
                 const float mnew = fmaxf(m, mt * sl2);
                 // Lazy rescale: a row keeps its stale max while P stays below 2^8.
                 const bool grow = mnew > m + 8.0f;
@@ -768,12 +815,13 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                         break;
                 }
                 // P = 2^(s*scale - m) (packed fp32 FMA, MUFU ex2 or the FMA-pipe
-                // polynomial); P pair c (keys 2c, 2c+1) is written over sraw[c]
-                // (its inputs s[2c], s[2c+1] are consumed by then).  Rows of a
-                // masked tile use MUFU only (exact zeros for -inf).
+                // polynomial); P pair c (keys 2c, 2c+1 of this thread's columns)
+                // is written over sraw[c] (its inputs s[2c], s[2c+1] are
+                // consumed by then).  Rows of a masked tile use MUFU only (exact
+                // zeros for -inf).
                 float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
 #pragma unroll
-                for (int c = 0; c < 64; c += 2) {
+                for (int c = 0; c < kCols / 2; c += 2) {
                     float x0, x1, x2, x3;
                     ffma2(x0, x1, s[2 * c], s[2 * c + 1], sl2, sl2, neg_m, neg_m);
                     ffma2(x2, x3, s[2 * c + 2], s[2 * c + 3], sl2, sl2, neg_m, neg_m);
@@ -832,6 +880,8 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                 if (j > 0 && __any_sync(0xffffffffu, grow)) {
 #pragma unroll
                     for (int c = 0; c < kOch; ++c) {
+                        if (c < oc_begin || c >= oc_end)
+                            continue;
                         uint32_t o[16];
                         tmem_ld16(tO + c * 16, o);
                         tmem_wait_ld();
@@ -848,14 +898,23 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                     tmem_st32(tmem + lane_base + S::p_col(i) + 32,
                               *reinterpret_cast<uint32_t(*)[32]>(&sraw[32]));
                 } else if constexpr (S::PT) {
-                    tmem_st32(tmem + lane_base + S::kPcol0,
-                              *reinterpret_cast<uint32_t(*)[32]>(&sraw[0]));
-                    tmem_st32(tmem + lane_base + S::kPcol1,
-                              *reinterpret_cast<uint32_t(*)[32]>(&sraw[32]));
+                    // Keys [0, 64) at kPcol0, [64, 128) at kPcol1.
+                    if constexpr (kSplit) {
+                        tmem_st32(tmem + lane_base + (hh ? S::kPcol1 : S::kPcol0),
+                                  *reinterpret_cast<uint32_t(*)[32]>(&sraw[0]));
+                    } else {
+                        tmem_st32(tmem + lane_base + S::kPcol0,
+                                  *reinterpret_cast<uint32_t(*)[32]>(&sraw[0]));
+                        tmem_st32(tmem + lane_base + S::kPcol1,
+                                  *reinterpret_cast<uint32_t(*)[32]>(&sraw[32]));
+                    }
                 } else {
-                    // P over the first 64 columns of S_i (all of S_i was read).
-                    tmem_st32(tS, *reinterpret_cast<uint32_t(*)[32]>(&sraw[0]));
-                    tmem_st32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(&sraw[32]));
+                    // P over the first 64 columns of S_i (all of S_i was read:
+                    // by this thread, or by both halves before the exchange).
+                    const uint32_t tP = tmem + lane_base + i * 128 + hh * 32;
+                    tmem_st32(tP, *reinterpret_cast<uint32_t(*)[32]>(&sraw[0]));
+                    if constexpr (!kSplit)
+                        tmem_st32(tP + 32, *reinterpret_cast<uint32_t(*)[32]>(&sraw[32]));
                 }
                 tmem_wait_st(); // P, and the O rescale above
                 tc_fence_before();
@@ -873,30 +932,74 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                 ++n_items;
                 tc_fence_after();
             }
-            // The whole row of O (and the ones column) in one batch of TMEM
-            // loads with a single wait.
-            uint32_t ob[kOch][16];
-            if (it.T > 0) {
+            // One thread per row: the whole O row (and the ones column) in one
+            // batch of TMEM loads with a single wait.  Two warps per row (fewer
+            // registers): the ones column here, O chunk by chunk below.
+            constexpr int kOb = kSplit ? 1 : kOch;
+            uint32_t ob[kOb][16];
+            if constexpr (kSplit) {
+                if (ones && it.T > 0) {
+                    tmem_ld16(tO + (p.ones_col & ~15), ob[0]);
+                    tmem_wait_ld();
+                    float lv = 0.f;
 #pragma unroll
-                for (int cq = 0; cq < kOch; ++cq)
-                    tmem_ld16(tO + cq * 16, ob[cq]);
-                tmem_wait_ld();
+                    for (int e = 0; e < 16; ++e)
+                        lv = e == (p.ones_col & 15) ? __uint_as_float(ob[0][e]) : lv;
+                    l = lv;
+                }
             } else {
+                if (it.T > 0) {
 #pragma unroll
-                for (int cq = 0; cq < kOch; ++cq)
+                    for (int cq = 0; cq < kOb; ++cq)
+                        tmem_ld16(tO + cq * 16, ob[cq]);
+                    tmem_wait_ld();
+                } else {
 #pragma unroll
-                    for (int e = 0; e < 16; ++e)
-                        ob[cq][e] = 0u;
+                    for (int cq = 0; cq < kOb; ++cq)
+#pragma unroll
+                        for (int e = 0; e < 16; ++e)
+                            ob[cq][e] = 0u;
+                }
+                if (ones && it.T > 0) {
+                    // Row sum of P = O[:, ones_col] (rescaled together with O).
+                    float lv = 0.f;
+#pragma unroll
+                    for (int cq = 0; cq < kOb; ++cq)
+#pragma unroll
+                        for (int e = 0; e < 16; ++e)
+                            lv = cq * 16 + e == p.ones_col ? __uint_as_float(ob[cq][e]) : lv;
+                    l = lv;
+                }
             }
-            if (ones && it.T > 0) {
-                // Row sum of P = O[:, ones_col] (rescaled together with O).
-                float lv = 0.f;
+            // Chunk cq of this thread's O row.
+            auto o_chunk = [&](int cq, uint32_t (&tmp)[16]) -> const uint32_t * {
+                if constexpr (kSplit) {
+                    if (it.T > 0) {
+                        tmem_ld16(tO + cq * 16, tmp);
+                        tmem_wait_ld();
+                    } else {
 #pragma unroll
-                for (int cq = 0; cq < kOch; ++cq)
-#pragma unroll
-                    for (int e = 0; e < 16; ++e)
-                        lv = cq * 16 + e == p.ones_col ? __uint_as_float(ob[cq][e]) : lv;
-                l = lv;
+                        for (int e = 0; e < 16; ++e)
+                            tmp[e] = 0u;
+                    }
+                    return tmp;
+                } else {
+                    return ob[cq < kOb ? cq : 0];
+                }
+            };
+            if constexpr (kSplit) {
+                if (!ones && it.T > 0) {
+                    // Sum of the two halves' partial row sums (double-buffered
+                    // by exchange parity).
+                    float *xs = xsum + ((((n_sum & 1) * 2 + i) * 4 + qd) * 2) * 32;
+                    xs[hh * 32 + lane] = l;
+                    warp_arrive(&lq[i * 4 + qd]);
+                    ok = __all_sync(0xffffffffu, mbar_wait(&lq[i * 4 + qd], n_sum & 1, err, kErrWaitO));
+                    if (!ok)
+                        break;
+                    ++n_sum;
+                    l += xs[(hh ^ 1) * 32 + lane];
+                }
             }
             const float inv = (it.T > 0 && l > 0.f) ? 1.f / l : 0.f;
             if (p.o_tma && it.T > 0) {
@@ -908,8 +1011,11 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                 uint8_t *stile = sQ + (qs_out * 2 + i) * S::TILE_BYTES;
 #pragma unroll
                 for (int cq = 0; cq < kEch; ++cq) {
+                    if (cq < ec_begin || cq >= ec_end)
+                        continue;
                     const int c = cq * 16;
-                    const uint32_t *o = ob[cq];
+                    uint32_t otmp[16];
+                    const uint32_t *o = o_chunk(cq, otmp);
                     uint4 w0, w1;
                     w0.x = pack2(__uint_as_float(o[0]) * inv, __uint_as_float(o[1]) * inv, BF16);
                     w0.y = pack2(__uint_as_float(o[2]) * inv, __uint_as_float(o[3]) * inv, BF16);
@@ -936,8 +1042,11 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                 it.b * p.o_sb + it.h * p.o_sh + static_cast<long long>(t) * p.o_st;
 #pragma unroll
             for (int cq = 0; cq < kEch; ++cq) {
+                if (cq < ec_begin || cq >= ec_end)
+                    continue;
                 const int c = cq * 16;
-                const uint32_t *o = ob[cq];
+                uint32_t otmp[16];
+                const uint32_t *o = o_chunk(cq, otmp);
                 if (!store)
                     continue;
                 float v[16];
