@@ -78,7 +78,11 @@ def build(force: bool = False, verbose: bool = False) -> Path:
                 if verbose:
                     print("compiled", name)
     if force or jobs or _stale(LIB, objs):
-        cmd = [nvcc()] + ARCH + ["-shared", "-o", str(LIB)] + [str(o) for o in objs]
+        # cuBLAS (the encoder graphs' linears) is linked dynamically from the CUDA
+        # toolkit the library was built with.
+        cuda_lib = Path(nvcc()).resolve().parent.parent / "lib64"
+        cmd = [nvcc()] + ARCH + ["-shared", "-o", str(LIB)] + [str(o) for o in objs] + [
+            "-L", str(cuda_lib), "-lcublas", "-Xlinker", f"-rpath={cuda_lib}"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stderr}")

@@ -345,7 +345,7 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
     uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(lq + 8);
     // Exchange buffers (split): [2 parity][2 tile][4 quarter][2 half][32 lanes].
     float *xmax = reinterpret_cast<float *>(bars + 128);
-    float *xsum = xmax + 2 * 2 * 4 * 2 * 32;
+    [[maybe_unused]] float *xsum = xmax + 2 * 2 * 4 * 2 * 32;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int items = p.batch * p.heads * ((p.L + 255) / 256);
@@ -731,7 +731,8 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
         constexpr int kOsplit = kSplit ? (kOch + 1) / 2 : kOch, kEsplit = kSplit ? (kEch + 1) / 2 : kEch;
         const int oc_begin = hh ? kOsplit : 0, oc_end = hh ? kOch : kOsplit;
         const int ec_begin = hh ? kEsplit : 0, ec_end = hh ? kEch : kEsplit;
-        int g = 0, n_items = 0, n_sum = 0;
+        int g = 0, n_items = 0;
+        [[maybe_unused]] int n_sum = 0;
         bool ok = true;
         for (int u = blockIdx.x; ok && u < items; u += gridDim.x) {
             const Item it = decode_item(p, u);

@@ -1,0 +1,312 @@
+// graph_kernels.cu -- the non-hot operators of the encoder graphs.
+//
+// Each kernel restates one operator of omni-tokenizer's CPU backend
+// (src/cpu.cpp) with the same rounding points: in the bf16 profile a result is
+// rounded to bf16 exactly once, where Cpu applies r(x, true).  Products and
+// sums use __fmul_rn / __fadd_rn where the reference's order matters, so that
+// the compiler does not contract them into FMAs the reference does not use.
+#include "graph_kernels.h"
+
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+namespace omni_b200 {
+namespace graph {
+namespace {
+
+__device__ __forceinline__ float ld(const void *p, size_t i, bool bf16) {
+    return bf16 ? __bfloat162float(static_cast<const __nv_bfloat16 *>(p)[i])
+                : static_cast<const float *>(p)[i];
+}
+__device__ __forceinline__ void st(void *p, size_t i, float v, bool bf16) {
+    if (bf16)
+        static_cast<__nv_bfloat16 *>(p)[i] = __float2bfloat16_rn(v);
+    else
+        static_cast<float *>(p)[i] = v;
+}
+// The value a bf16-profile result holds after rounding (fp32 otherwise).
+__device__ __forceinline__ float rnd(float v, bool bf16) {
+    return bf16 ? __bfloat162float(__float2bfloat16_rn(v)) : v;
+}
+
+unsigned blocks_for(size_t n, unsigned threads) {
+    size_t b = (n + threads - 1) / threads;
+    return static_cast<unsigned>(b < 148 * 32 ? (b < 1 ? 1 : b) : 148 * 32);
+}
+int status() { return static_cast<int>(cudaGetLastError()); }
+
+#define GRID_STRIDE(i, n)                                                                          \
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < (n);         \
+         i += static_cast<size_t>(gridDim.x) * blockDim.x)
+
+__global__ void k_linear_epilogue(const float *acc, const void *b, bool bbf16, void *y, bool bf16,
+                                  size_t rows, size_t cols) {
+    GRID_STRIDE(i, rows * cols) {
+        const float bv = b ? ld(b, i % cols, bbf16) : 0.f;
+        st(y, i, __fadd_rn(acc[i], bv), bf16);
+    }
+}
+
+// One block per row; the two reductions follow the row in column order per
+// thread (stride blockDim) and combine in a fixed tree.
+__global__ void k_layer_norm(const void *x, const void *w, const void *b, void *y, bool bf16,
+                             size_t cols, float eps) {
+    __shared__ float red[32];
+    const size_t row = blockIdx.x;
+    const size_t base = row * cols;
+    auto block_sum = [&](float v) {
+        for (int o = 16; o > 0; o >>= 1)
+            v += __shfl_xor_sync(0xffffffffu, v, o);
+        if ((threadIdx.x & 31) == 0)
+            red[threadIdx.x >> 5] = v;
+        __syncthreads();
+        float t = 0.f;
+        if (threadIdx.x < 32) {
+            t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+            for (int o = 16; o > 0; o >>= 1)
+                t += __shfl_xor_sync(0xffffffffu, t, o);
+            if (threadIdx.x == 0)
+                red[0] = t;
+        }
+        __syncthreads();
+        t = red[0];
+        __syncthreads();
+        return t;
+    };
+    float s = 0.f;
+    for (size_t j = threadIdx.x; j < cols; j += blockDim.x)
+        s = __fadd_rn(s, ld(x, base + j, bf16));
+    const float mean = block_sum(s) / static_cast<float>(cols);
+    float v = 0.f;
+    for (size_t j = threadIdx.x; j < cols; j += blockDim.x) {
+        const float z = __fsub_rn(ld(x, base + j, bf16), mean);
+        v = __fadd_rn(v, __fmul_rn(z, z));
+    }
+    const float var = block_sum(v);
+    const float inv = 1.f / sqrtf(var / static_cast<float>(cols) + eps);
+    for (size_t j = threadIdx.x; j < cols; j += blockDim.x) {
+        const float z = __fmul_rn(__fmul_rn(__fsub_rn(ld(x, base + j, bf16), mean), inv), ld(w, j, bf16));
+        st(y, base + j, __fadd_rn(z, ld(b, j, bf16)), bf16);
+    }
+}
+
+__global__ void k_gelu(void *x, bool bf16, size_t n) {
+    GRID_STRIDE(i, n) {
+        const float z = ld(x, i, bf16);
+        st(x, i, __fmul_rn(__fmul_rn(0.5f, z), __fadd_rn(1.f, erff(__fmul_rn(z, 0.7071067811865475244f)))),
+           bf16);
+    }
+}
+
+__global__ void k_add(void *x, const void *y, bool bf16, size_t n) {
+    GRID_STRIDE(i, n) { st(x, i, __fadd_rn(ld(x, i, bf16), ld(y, i, bf16)), bf16); }
+}
+
+__global__ void k_bias(void *x, const void *b, bool bf16, size_t rows, size_t cols) {
+    GRID_STRIDE(i, rows * cols) { st(x, i, __fadd_rn(ld(x, i, bf16), ld(b, i % cols, bf16)), bf16); }
+}
+
+__global__ void k_conv_gather(const void *x, void *y, bool bf16, size_t rows, size_t cols,
+                              size_t stride, size_t out_rows) {
+    GRID_STRIDE(i, out_rows * cols * 3) {
+        const size_t t = i / (cols * 3), rem = i % (cols * 3), c = rem / 3, k = rem % 3;
+        const long long s = static_cast<long long>(t * stride + k) - 2;
+        const float v = s >= 0 && s < static_cast<long long>(rows) ? ld(x, s * cols + c, bf16) : 0.f;
+        st(y, i, v, bf16);
+    }
+}
+
+__global__ void k_pool(const void *x, void *y, bool bf16, size_t rows, size_t cols, size_t factor,
+                       size_t out_rows) {
+    GRID_STRIDE(i, out_rows * cols) {
+        const size_t t = i / cols, j = i % cols;
+        float sum = 0.f;
+        for (size_t k = 0; k < factor && t * factor + k < rows; ++k)
+            sum = __fadd_rn(sum, ld(x, (t * factor + k) * cols + j, bf16));
+        st(y, i, sum / static_cast<float>(factor), bf16);
+    }
+}
+
+__global__ void k_interpolate(const void *x, void *y, bool bf16, size_t source, size_t height,
+                              size_t width, size_t cols) {
+    GRID_STRIDE(idx, height * width * cols) {
+        const size_t c = idx % cols, ij = idx / cols, i = ij / width, j = ij % width;
+        const float sy = fmaxf(0.f, __fsub_rn(__fmul_rn(static_cast<float>(i) + .5f,
+                                                       static_cast<float>(source) / static_cast<float>(height)),
+                                             .5f));
+        const float sx = fmaxf(0.f, __fsub_rn(__fmul_rn(static_cast<float>(j) + .5f,
+                                                       static_cast<float>(source) / static_cast<float>(width)),
+                                             .5f));
+        const size_t y0 = static_cast<size_t>(sy), x0 = static_cast<size_t>(sx);
+        const size_t y1 = y0 + 1 < source ? y0 + 1 : source - 1, x1 = x0 + 1 < source ? x0 + 1 : source - 1;
+        const float fy = sy - static_cast<float>(y0), fx = sx - static_cast<float>(x0);
+        const float a = fmaf(1.f - fx, ld(x, (y0 * source + x0) * cols + c, bf16),
+                             __fmul_rn(fx, ld(x, (y0 * source + x1) * cols + c, bf16)));
+        const float b = fmaf(1.f - fx, ld(x, (y1 * source + x0) * cols + c, bf16),
+                             __fmul_rn(fx, ld(x, (y1 * source + x1) * cols + c, bf16)));
+        st(y, idx, fmaf(1.f - fy, a, __fmul_rn(fy, b)), bf16);
+    }
+}
+
+// One thread per row (column order as the reference).
+__global__ void k_normalize(const void *x, void *y, bool bf16, size_t rows, size_t cols) {
+    GRID_STRIDE(r, rows) {
+        float n = 0.f;
+        for (size_t j = 0; j < cols; ++j) {
+            const float v = ld(x, r * cols + j, bf16);
+            n = __fadd_rn(n, __fmul_rn(v, v));
+        }
+        n = fmaxf(rnd(sqrtf(n), bf16), rnd(1e-12f, bf16));
+        for (size_t j = 0; j < cols; ++j)
+            st(y, r * cols + j, ld(x, r * cols + j, bf16) / n, bf16);
+    }
+}
+
+__global__ void k_image_patches(const float *px, __nv_bfloat16 *y, size_t height, size_t width,
+                                size_t patch) {
+    const size_t gw = width / patch, pd = 8 * patch * patch, n = (height / patch) * gw * pd;
+    GRID_STRIDE(i, n) {
+        const size_t cell = i / pd, rem = i % pd, pix = rem / 8, ch = rem % 8;
+        float v = 0.f;
+        if (ch < 3) {
+            const size_t gy = cell / gw, gx = cell % gw, dy = pix / patch, dx = pix % patch;
+            v = px[ch * height * width + (gy * patch + dy) * width + gx * patch + dx];
+        }
+        y[i] = __float2bfloat16_rn(v);
+    }
+}
+
+__global__ void k_convert(const float *x, void *y, bool bf16, size_t n) {
+    GRID_STRIDE(i, n) { st(y, i, x[i], bf16); }
+}
+__global__ void k_to_float(const void *x, float *y, bool bf16, size_t n) {
+    GRID_STRIDE(i, n) { y[i] = ld(x, i, bf16); }
+}
+
+// One warp per (query t, head h): pass 1 keeps the scores of keys < limit(t)
+// in shared memory and their maximum, pass 2 their exponentials and sum, pass
+// 3 accumulates the output in key order, each lane owning head-dim columns.
+__global__ void k_attention_f32(const float *q, const float *k, const float *v, float *y, size_t n,
+                                size_t heads, size_t hd, size_t block, size_t valid) {
+    extern __shared__ float sm[];
+    const int wib = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float *scores = sm + static_cast<size_t>(wib) * n;
+    const size_t task = static_cast<size_t>(blockIdx.x) * (blockDim.x >> 5) + wib;
+    if (task >= n * heads)
+        return;
+    const size_t t = task / heads, h = task % heads, d = heads * hd;
+    size_t limit = n < valid ? n : valid;
+    if (block)
+        limit = limit < (t / block + 1) * block ? limit : (t / block + 1) * block;
+    const float scale = 1.f / sqrtf(static_cast<float>(hd));
+    const float *qr = q + t * d + h * hd;
+    float mx = -INFINITY;
+    for (size_t s = lane; s < limit; s += 32) {
+        const float *kr = k + s * d + h * hd;
+        float z = 0.f;
+        for (size_t j = 0; j < hd; ++j)
+            z = __fadd_rn(z, __fmul_rn(__fmul_rn(qr[j], scale), kr[j]));
+        scores[s] = z;
+        mx = fmaxf(mx, z);
+    }
+    for (int o = 16; o > 0; o >>= 1)
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float total = 0.f;
+    for (size_t s = lane; s < limit; s += 32) {
+        const float e = expf(scores[s] - mx);
+        scores[s] = e;
+        total += e;
+    }
+    for (int o = 16; o > 0; o >>= 1)
+        total += __shfl_xor_sync(0xffffffffu, total, o);
+    __syncwarp();
+    for (size_t j = lane; j < hd; j += 32) {
+        float acc = 0.f;
+        for (size_t s = 0; s < limit; ++s)
+            acc = __fadd_rn(acc, __fmul_rn(scores[s] / total, v[s * d + h * hd + j]));
+        y[t * d + h * hd + j] = acc;
+    }
+}
+
+} // namespace
+
+int linear_epilogue(const float *acc, const void *b, bool bbf16, void *y, bool bf16, size_t rows,
+                    size_t cols, cudaStream_t s) {
+    k_linear_epilogue<<<blocks_for(rows * cols, 256), 256, 0, s>>>(acc, b, bbf16, y, bf16, rows, cols);
+    return status();
+}
+int layer_norm(const void *x, const void *w, const void *b, void *y, bool bf16, size_t rows,
+               size_t cols, float eps, cudaStream_t s) {
+    if (rows)
+        k_layer_norm<<<static_cast<unsigned>(rows), 256, 0, s>>>(x, w, b, y, bf16, cols, eps);
+    return status();
+}
+int gelu(void *x, bool bf16, size_t n, cudaStream_t s) {
+    k_gelu<<<blocks_for(n, 256), 256, 0, s>>>(x, bf16, n);
+    return status();
+}
+int add(void *x, const void *y, bool bf16, size_t n, cudaStream_t s) {
+    k_add<<<blocks_for(n, 256), 256, 0, s>>>(x, y, bf16, n);
+    return status();
+}
+int bias(void *x, const void *b, bool bf16, size_t rows, size_t cols, cudaStream_t s) {
+    k_bias<<<blocks_for(rows * cols, 256), 256, 0, s>>>(x, b, bf16, rows, cols);
+    return status();
+}
+int conv_gather(const void *x, void *y, bool bf16, size_t rows, size_t cols, size_t stride,
+                cudaStream_t s) {
+    const size_t out_rows = (rows + stride - 1) / stride;
+    k_conv_gather<<<blocks_for(out_rows * cols * 3, 256), 256, 0, s>>>(x, y, bf16, rows, cols, stride,
+                                                                        out_rows);
+    return status();
+}
+int pool(const void *x, void *y, bool bf16, size_t rows, size_t cols, size_t factor,
+         cudaStream_t s) {
+    const size_t out_rows = (rows + factor - 1) / factor;
+    k_pool<<<blocks_for(out_rows * cols, 256), 256, 0, s>>>(x, y, bf16, rows, cols, factor, out_rows);
+    return status();
+}
+int interpolate(const void *x, void *y, bool bf16, size_t source, size_t height, size_t width,
+                size_t cols, cudaStream_t s) {
+    k_interpolate<<<blocks_for(height * width * cols, 256), 256, 0, s>>>(x, y, bf16, source, height,
+                                                                          width, cols);
+    return status();
+}
+int normalize(const void *x, void *y, bool bf16, size_t rows, size_t cols, cudaStream_t s) {
+    k_normalize<<<blocks_for(rows, 128), 128, 0, s>>>(x, y, bf16, rows, cols);
+    return status();
+}
+int image_patches(const float *pixels, void *y, size_t height, size_t width, size_t patch,
+                  cudaStream_t s) {
+    const size_t n = (height / patch) * (width / patch) * 8 * patch * patch;
+    k_image_patches<<<blocks_for(n, 256), 256, 0, s>>>(pixels, static_cast<__nv_bfloat16 *>(y), height,
+                                                        width, patch);
+    return status();
+}
+int convert(const float *x, void *y, bool bf16, size_t n, cudaStream_t s) {
+    k_convert<<<blocks_for(n, 256), 256, 0, s>>>(x, y, bf16, n);
+    return status();
+}
+int to_float(const void *x, float *y, bool bf16, size_t n, cudaStream_t s) {
+    k_to_float<<<blocks_for(n, 256), 256, 0, s>>>(x, y, bf16, n);
+    return status();
+}
+int attention_f32(const float *q, const float *k, const float *v, float *y, size_t n, size_t heads,
+                  size_t hd, size_t block, size_t valid, cudaStream_t s) {
+    constexpr int kWarps = 4;
+    const size_t smem = static_cast<size_t>(kWarps) * n * sizeof(float);
+    if (smem > 200 * 1024)
+        return -2; // sequences longer than 12800 keys are not supported here
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(k_attention_f32, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        attr = true;
+    }
+    const size_t tasks = n * heads;
+    k_attention_f32<<<static_cast<unsigned>((tasks + kWarps - 1) / kWarps), kWarps * 32, smem, s>>>(
+        q, k, v, y, n, heads, hd, block, valid);
+    return status();
+}
+
+} // namespace graph
+} // namespace omni_b200

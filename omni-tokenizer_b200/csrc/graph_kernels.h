@@ -1,0 +1,52 @@
+// graph_kernels.h -- the non-hot operators of the encoder graphs (CUDA).
+//
+// Semantics follow the reference's CPU backend, omni-tokenizer
+// src/cpu.cpp:20-221 (Cpu::upload / linear epilogue / norm / gelu / add / bias /
+// conv_gather / pool / interpolate / normalize) and the patch layout of
+// src/internal.h:57-70 (Ops::image_patches).  A tensor is either fp32 or, in
+// the bf16 profile, bf16 in memory: every bf16-profile result is rounded to
+// bf16 once, exactly where the reference applies round_bf16.
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+
+namespace omni_b200 {
+namespace graph {
+
+// y = r(acc + bias) (bias may be null); acc fp32 [rows, cols]; y fp32 or bf16.
+int linear_epilogue(const float *acc, const void *bias, bool bias_bf16, void *y, bool bf16,
+                    size_t rows, size_t cols, cudaStream_t s);
+// Layer norm over each row: r((x - mean) * inv * w + b), inv = 1/sqrt(var + eps).
+int layer_norm(const void *x, const void *w, const void *b, void *y, bool bf16, size_t rows,
+               size_t cols, float eps, cudaStream_t s);
+// In place: x = r(0.5 x (1 + erf(x / sqrt 2))).
+int gelu(void *x, bool bf16, size_t n, cudaStream_t s);
+// In place: x = r(x + y) over the first n elements.
+int add(void *x, const void *y, bool bf16, size_t n, cudaStream_t s);
+// In place: x[r, c] = r(x[r, c] + b[c]).
+int bias(void *x, const void *b, bool bf16, size_t rows, size_t cols, cudaStream_t s);
+// Kernel-3 causal conv input (left pad 2): y[t, 3c + k] = x[t*stride + k - 2, c].
+int conv_gather(const void *x, void *y, bool bf16, size_t rows, size_t cols, size_t stride,
+                cudaStream_t s);
+// Mean of `factor` consecutive rows (the last group may be short; divisor stays factor).
+int pool(const void *x, void *y, bool bf16, size_t rows, size_t cols, size_t factor,
+         cudaStream_t s);
+// Bilinear resize of a [source*source, cols] grid to [height*width, cols].
+int interpolate(const void *x, void *y, bool bf16, size_t source, size_t height, size_t width,
+                size_t cols, cudaStream_t s);
+// Row-wise L2 normalisation with the reference's max(r(sqrt(n)), r(1e-12)) guard.
+int normalize(const void *x, void *y, bool bf16, size_t rows, size_t cols, cudaStream_t s);
+// CHW fp32 pixels -> bf16 patches [gh*gw, 8*p*p] (channel-padded to 8 per pixel).
+int image_patches(const float *pixels, void *y, size_t height, size_t width, size_t patch,
+                  cudaStream_t s);
+// fp32 -> bf16 (round to nearest even, NaN quieted) or a copy for fp32.
+int convert(const float *x, void *y, bool bf16, size_t n, cudaStream_t s);
+// bf16/fp32 -> fp32.
+int to_float(const void *x, float *y, bool bf16, size_t n, cudaStream_t s);
+// fp32 multi-head attention on [n, heads*hd] rows (the fp32 audio profile):
+// scores (q*scale).k, softmax over keys < limit(t), output in fp32.
+int attention_f32(const float *q, const float *k, const float *v, float *y, size_t n, size_t heads,
+                  size_t hd, size_t block, size_t valid, cudaStream_t s);
+
+} // namespace graph
+} // namespace omni_b200

@@ -1,0 +1,812 @@
+// omni_runtime.cu -- the reference's outer C ABI (include/omni_abi.h) on B200:
+// OMNIVQ01 model loading, the audio and image encoder graphs, and the 15
+// omni_* entry points, so that omni-tokenizer's Python Tokenizer and C callers
+// can load this library through OMNI_LIBRARY.
+//
+// Graph semantics follow omni-tokenizer src/runtime.cpp:30-130 (audio, image),
+// the loader src/model.cpp:96-205, the operator semantics src/cpu.cpp and the
+// C API behaviour src/runtime.cpp:131-288.  Hot operators run on this
+// library's sm_100a kernels (attention: fmha_sm100.cu; VQ argmin:
+// vq_sm100.cu / vq_stream_sm100.cu; norms: norms.cu); linears are cuBLAS
+// GEMMs (fp32 in the audio profile, bf16 x bf16 -> fp32 in the image profile)
+// followed by the bias / bf16-rounding epilogue; the remaining operators are
+// graph_kernels.cu.  Audio-profile attention runs in fp32 on the CUDA cores
+// (the reference's audio kernels are fp32-accurate 3xTF32); setting
+// OMNI_B200_AUDIO_BF16=1 routes it through the tcgen05 kernel instead.
+#include "graph_kernels.h"
+#include "omni_abi.h"
+#include "omni_b200.h"
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <cublas_v2.h>
+#include <cuda_runtime.h>
+#include <fstream>
+#include <limits>
+#include <memory>
+#include <set>
+#include <stdexcept>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+namespace omni_b200 {
+namespace rt {
+
+struct Fail : std::runtime_error {
+    int code;
+    Fail(int c, const std::string &m) : std::runtime_error(m), code(c) {}
+};
+void require(bool ok, const std::string &msg, int code = OMNI_INVALID_ARGUMENT) {
+    if (!ok)
+        throw Fail(code, msg);
+}
+void cuda_ok(cudaError_t e, const char *what) {
+    if (e != cudaSuccess)
+        throw Fail(e == cudaErrorMemoryAllocation ? OMNI_OUT_OF_MEMORY : OMNI_INTERNAL_ERROR,
+                   std::string(what) + ": " + cudaGetErrorString(e));
+}
+void op_ok(int rc, const char *what) {
+    if (rc == 0)
+        return;
+    const char *msg = omni_b200_last_error();
+    throw Fail(rc > 0 && rc <= 7 ? rc : OMNI_INTERNAL_ERROR,
+               std::string(what) + ": " + (msg && *msg ? msg : "device error " + std::to_string(rc)));
+}
+void blas_ok(cublasStatus_t st, const char *what) {
+    if (st != CUBLAS_STATUS_SUCCESS)
+        throw Fail(st == CUBLAS_STATUS_ALLOC_FAILED ? OMNI_OUT_OF_MEMORY : OMNI_INTERNAL_ERROR,
+                   std::string(what) + ": cuBLAS status " + std::to_string(static_cast<int>(st)));
+}
+
+// Device bytes a context holds (activations, scratch); the peak is reported
+// by omni_context_peak_workspace.
+struct Memory {
+    std::atomic<uint64_t> live{0}, peak{0};
+    void add(uint64_t n) {
+        const uint64_t v = live.fetch_add(n) + n;
+        uint64_t p = peak.load();
+        while (v > p && !peak.compare_exchange_weak(p, v)) {
+        }
+    }
+};
+
+// A row-major device matrix of fp32 or bf16 values.
+struct Tensor {
+    std::shared_ptr<void> mem;
+    size_t rows = 0, cols = 0;
+    bool bf16 = false;
+    void *data() const { return mem.get(); }
+    size_t size() const { return rows * cols; }
+    size_t bytes() const { return size() * (bf16 ? 2 : 4); }
+};
+
+Tensor weight_tensor(size_t rows, size_t cols, bool bf16) {
+    Tensor t;
+    t.rows = rows;
+    t.cols = cols;
+    t.bf16 = bf16;
+    void *p = nullptr;
+    cuda_ok(cudaMalloc(&p, t.bytes() ? t.bytes() : 1), "weight allocation");
+    t.mem = std::shared_ptr<void>(p, [](void *q) { cudaFree(q); });
+    return t;
+}
+
+struct Config {
+    uint32_t kind = 0, layers = 0, width = 0, heads = 0, ffn = 0, input_channels = 0,
+             patch_size = 0, pool_size = 0, block_size = 0, pos_height = 0, pos_width = 0,
+             code_dim = 0, vocab_size = 0;
+};
+
+struct Model {
+    Config cfg;
+    int backend = OMNI_CUDA, device = 0;
+    uint64_t weight_bytes = 0;
+    std::unordered_map<std::string, Tensor> w;
+    std::unordered_map<std::string, std::vector<uint64_t>> shapes;
+    Tensor cbnorm;
+    const Tensor &get(const std::string &name) const {
+        auto it = w.find(name);
+        require(it != w.end(), "Missing tensor: " + name, OMNI_INVALID_MODEL);
+        return it->second;
+    }
+    const Tensor *opt(const std::string &name) const {
+        auto it = w.find(name);
+        return it == w.end() ? nullptr : &it->second;
+    }
+};
+
+// ------------------------------------------------------------------ loader
+namespace {
+uint32_t rd32(std::istream &f) {
+    unsigned char b[4];
+    f.read(reinterpret_cast<char *>(b), 4);
+    require(static_cast<bool>(f), "Truncated model index", OMNI_INVALID_MODEL);
+    return uint32_t(b[0]) | uint32_t(b[1]) << 8 | uint32_t(b[2]) << 16 | uint32_t(b[3]) << 24;
+}
+uint64_t rd64(std::istream &f) {
+    const uint64_t lo = rd32(f);
+    return lo | uint64_t(rd32(f)) << 32;
+}
+struct Entry {
+    std::string name;
+    uint32_t dtype = 0;
+    uint64_t offset = 0, bytes = 0;
+    std::vector<uint64_t> shape;
+};
+
+void expect_shape(const Model &m, const std::string &name, std::vector<uint64_t> s) {
+    auto it = m.shapes.find(name);
+    require(it != m.shapes.end(), "Missing tensor: " + name, OMNI_INVALID_MODEL);
+    require(it->second == s, "Incorrect shape for " + name, OMNI_INVALID_MODEL);
+}
+
+// The fixed tensor set of each model kind (src/model.cpp:33-94).
+void check_layout(const Model &m) {
+    const Config &c = m.cfg;
+    const uint64_t W = c.width, F = c.ffn;
+    if (c.kind == OMNI_AUDIO) {
+        expect_shape(m, "conv1.weight", {W, c.input_channels, 3});
+        expect_shape(m, "conv1.bias", {W});
+        expect_shape(m, "conv2.weight", {W, W, 3});
+        expect_shape(m, "conv2.bias", {W});
+        expect_shape(m, "embed_positions.weight", {c.pos_height, W});
+        expect_shape(m, "codebook.weight", {c.vocab_size, W});
+        require(c.pool_size == 4 && c.patch_size == 0 && c.code_dim == c.width && c.block_size > 0,
+                "Invalid audio configuration", OMNI_INVALID_MODEL);
+        for (uint32_t l = 0; l < c.layers; ++l) {
+            const std::string p = "layers." + std::to_string(l) + ".";
+            for (const char *n : {"self_attn_layer_norm", "final_layer_norm"}) {
+                expect_shape(m, p + n + ".weight", {W});
+                expect_shape(m, p + n + ".bias", {W});
+            }
+            for (const char *n : {"q_proj", "k_proj", "v_proj", "out_proj"})
+                expect_shape(m, p + "self_attn." + n + ".weight", {W, W});
+            for (const char *n : {"q_proj", "v_proj", "out_proj"})
+                expect_shape(m, p + "self_attn." + n + ".bias", {W});
+            expect_shape(m, p + "fc1.weight", {F, W});
+            expect_shape(m, p + "fc1.bias", {F});
+            expect_shape(m, p + "fc2.weight", {W, F});
+            expect_shape(m, p + "fc2.bias", {W});
+        }
+    } else {
+        require(c.input_channels == 3 && c.patch_size > 0 && c.patch_size <= 64 &&
+                    c.pos_height == c.pos_width,
+                "Invalid image configuration", OMNI_INVALID_MODEL);
+        const uint64_t P = c.patch_size;
+        expect_shape(m, "patch_embed.proj.weight", {W, 3, P, P});
+        expect_shape(m, "patch_embed.proj.bias", {W});
+        expect_shape(m, "pos_embed", {1, uint64_t(c.pos_height) * c.pos_width, W});
+        expect_shape(m, "quant_conv.weight", {c.code_dim, W, 1, 1});
+        expect_shape(m, "quant_conv.bias", {c.code_dim});
+        expect_shape(m, "quantize.embedding.weight", {c.vocab_size, c.code_dim});
+        for (uint32_t l = 0; l < c.layers; ++l) {
+            const std::string p = "blocks." + std::to_string(l) + ".";
+            for (const char *n : {"norm1", "norm2"}) {
+                expect_shape(m, p + n + ".weight", {W});
+                expect_shape(m, p + n + ".bias", {W});
+            }
+            expect_shape(m, p + "attn.qkv.weight", {3 * W, W});
+            expect_shape(m, p + "attn.qkv.bias", {3 * W});
+            expect_shape(m, p + "attn.proj.weight", {W, W});
+            expect_shape(m, p + "attn.proj.bias", {W});
+            expect_shape(m, p + "mlp.fc1.weight", {F, W});
+            expect_shape(m, p + "mlp.fc1.bias", {F});
+            expect_shape(m, p + "mlp.fc2.weight", {W, F});
+            expect_shape(m, p + "mlp.fc2.bias", {W});
+        }
+    }
+}
+} // namespace
+
+std::shared_ptr<Model> load_model(const char *path, int backend, int device) {
+    require(path && *path, "Model path must not be empty");
+    require(backend == OMNI_CUDA,
+            "This library implements the CUDA backend only (OMNI_CPU is unsupported)",
+            OMNI_UNSUPPORTED);
+    int devices = 0;
+    require(cudaGetDeviceCount(&devices) == cudaSuccess && device >= 0 && device < devices,
+            "Requested CUDA device is unavailable", OMNI_UNSUPPORTED);
+    cuda_ok(cudaSetDevice(device), "set device");
+    std::ifstream f(path, std::ios::binary | std::ios::ate);
+    require(static_cast<bool>(f), "Cannot open model file", OMNI_IO_ERROR);
+    const uint64_t file_bytes = static_cast<uint64_t>(f.tellg());
+    require(file_bytes >= 68, "Model file is too short", OMNI_INVALID_MODEL);
+    f.seekg(0);
+    char magic[8];
+    f.read(magic, 8);
+    require(static_cast<bool>(f) && std::memcmp(magic, "OMNIVQ01", 8) == 0, "Invalid model magic",
+            OMNI_INVALID_MODEL);
+    require(rd32(f) == 1, "Unsupported model version", OMNI_INVALID_MODEL);
+    auto m = std::make_shared<Model>();
+    m->backend = backend;
+    m->device = device;
+    Config &c = m->cfg;
+    c.kind = rd32(f);
+    for (uint32_t *fld : {&c.layers, &c.width, &c.heads, &c.ffn, &c.input_channels, &c.patch_size,
+                          &c.pool_size, &c.block_size, &c.pos_height, &c.pos_width, &c.code_dim,
+                          &c.vocab_size})
+        *fld = rd32(f);
+    require((c.kind == OMNI_AUDIO || c.kind == OMNI_IMAGE) && c.layers > 0 && c.layers <= 80 &&
+                c.width > 0 && c.width <= 8192 && c.heads > 0 && c.width % c.heads == 0 &&
+                c.ffn > 0 && c.ffn <= 32768 && c.code_dim > 0 && c.code_dim <= 8192 &&
+                c.vocab_size > 0 && c.vocab_size <= 16384 && c.input_channels > 0 &&
+                c.input_channels <= 512 && c.pos_height > 0 && c.pos_height <= 16384 &&
+                c.pos_width <= 16384,
+            "Model configuration exceeds supported bounds", OMNI_INVALID_MODEL);
+    const uint32_t count = rd32(f);
+    require(count == 6 + c.layers * (c.kind == OMNI_AUDIO ? 15u : 12u),
+            "Unexpected tensor count for the fixed model", OMNI_INVALID_MODEL);
+    std::vector<Entry> entries;
+    std::set<std::string> names;
+    const uint32_t want_dtype = c.kind == OMNI_AUDIO ? 1u : 2u; // 1 = fp32, 2 = bf16
+    for (uint32_t i = 0; i < count; ++i) {
+        const uint32_t len = rd32(f), dtype = rd32(f), rank = rd32(f), reserved = rd32(f);
+        Entry e;
+        e.dtype = dtype;
+        e.offset = rd64(f);
+        e.bytes = rd64(f);
+        require(len > 0 && len <= 1024 && dtype == want_dtype && rank > 0 && rank <= 4 &&
+                    reserved == 0,
+                "Invalid tensor record or precision profile", OMNI_INVALID_MODEL);
+        uint64_t elements = 1;
+        for (uint32_t r = 0; r < rank; ++r) {
+            const uint64_t d = rd64(f);
+            require(d > 0 && d <= (uint64_t(1) << 24) &&
+                        elements <= std::numeric_limits<uint64_t>::max() / d,
+                    "Tensor dimensions overflow", OMNI_INVALID_MODEL);
+            elements *= d;
+            e.shape.push_back(d);
+        }
+        require(elements <= std::numeric_limits<uint64_t>::max() / 4 &&
+                    e.bytes == elements * (dtype == 1 ? 4 : 2) && e.offset % 64 == 0 &&
+                    e.offset <= file_bytes && e.bytes <= file_bytes - e.offset,
+                "Invalid tensor data bounds", OMNI_INVALID_MODEL);
+        e.name.resize(len);
+        f.read(&e.name[0], len);
+        require(static_cast<bool>(f) && e.name.find('\0') == std::string::npos &&
+                    names.insert(e.name).second,
+                "Invalid or duplicate tensor name", OMNI_INVALID_MODEL);
+        entries.push_back(std::move(e));
+    }
+    // Tensor data must not overlap each other or the index.
+    {
+        std::vector<std::pair<uint64_t, uint64_t>> spans;
+        for (const Entry &e : entries)
+            spans.emplace_back(e.offset, e.bytes);
+        std::sort(spans.begin(), spans.end());
+        uint64_t end = static_cast<uint64_t>(f.tellg());
+        for (auto &s : spans) {
+            require(s.first >= end, "Overlapping model tensors/index", OMNI_INVALID_MODEL);
+            end = s.first + s.second;
+        }
+    }
+    for (const Entry &e : entries)
+        m->shapes[e.name] = e.shape;
+    check_layout(*m);
+    const bool bf16 = c.kind == OMNI_IMAGE;
+    for (const Entry &e : entries) {
+        std::vector<unsigned char> raw(static_cast<size_t>(e.bytes));
+        f.seekg(static_cast<std::streamoff>(e.offset));
+        f.read(reinterpret_cast<char *>(raw.data()), static_cast<std::streamsize>(e.bytes));
+        require(static_cast<bool>(f), "Truncated tensor data", OMNI_IO_ERROR);
+        size_t rows = static_cast<size_t>(e.shape[0]), cols = 1;
+        for (size_t r = 1; r < e.shape.size(); ++r)
+            cols *= static_cast<size_t>(e.shape[r]);
+        if (e.name == "pos_embed") {
+            rows = static_cast<size_t>(e.shape[1]);
+            cols = static_cast<size_t>(e.shape[2]);
+        }
+        if (c.kind == OMNI_IMAGE && e.name == "patch_embed.proj.weight") {
+            // [width, 3, p, p] -> [width, p*p*8]: pixel-major, channels padded
+            // to 8, matching the patch layout the graph builds.
+            const size_t px = size_t(c.patch_size) * c.patch_size;
+            std::vector<unsigned char> packed(rows * px * 8 * 2, 0);
+            for (size_t o = 0; o < rows; ++o)
+                for (size_t q = 0; q < px; ++q)
+                    for (size_t ch = 0; ch < 3; ++ch)
+                        std::memcpy(&packed[(o * px * 8 + q * 8 + ch) * 2],
+                                    &raw[(o * 3 * px + ch * px + q) * 2], 2);
+            raw.swap(packed);
+            cols = px * 8;
+        }
+        Tensor t = weight_tensor(rows, cols, bf16);
+        cuda_ok(cudaMemcpy(t.data(), raw.data(), t.bytes(), cudaMemcpyHostToDevice), "weight upload");
+        m->weight_bytes += t.bytes();
+        m->w.emplace(e.name, std::move(t));
+    }
+    const char *cb_name = c.kind == OMNI_AUDIO ? "codebook.weight" : "quantize.embedding.weight";
+    Tensor &cb = m->w.at(cb_name);
+    if (c.kind == OMNI_IMAGE) {
+        // The image codebook is L2-normalised once at load (src/model.cpp:203-204).
+        Tensor n = weight_tensor(cb.rows, cb.cols, true);
+        cuda_ok(static_cast<cudaError_t>(graph::normalize(cb.data(), n.data(), true, cb.rows, cb.cols, 0)),
+                "codebook normalise");
+        cb = std::move(n);
+    }
+    m->cbnorm = weight_tensor(cb.rows, 1, bf16);
+    op_ok(omni_b200_squares(cb.data(), m->cbnorm.data(), cb.rows, cb.cols, bf16 ? OMNI_B200_BF16 : OMNI_B200_F32,
+                            bf16 ? OMNI_B200_BF16 : OMNI_B200_F32, nullptr),
+          "codebook norms");
+    cuda_ok(cudaDeviceSynchronize(), "model load");
+    return m;
+}
+
+// ------------------------------------------------------------------ context
+struct Context {
+    std::shared_ptr<Model> model;
+    cudaStream_t stream = nullptr;
+    cublasHandle_t blas = nullptr;
+    std::shared_ptr<Memory> memory = std::make_shared<Memory>();
+    std::atomic<bool> cancelled{false};
+    std::atomic_flag running = ATOMIC_FLAG_INIT;
+    Tensor features;
+    omni_trace_callback trace = nullptr;
+    void *trace_user = nullptr;
+    bool audio_bf16 = false;
+
+    ~Context() {
+        features = {};
+        if (stream) {
+            cudaSetDevice(model ? model->device : 0);
+            cudaStreamSynchronize(stream);
+        }
+        if (blas)
+            cublasDestroy(blas);
+        if (stream)
+            cudaStreamDestroy(stream);
+    }
+    void check() const {
+        if (cancelled.load())
+            throw Fail(OMNI_CANCELLED, "Inference cancelled");
+    }
+    // Stream-ordered activation memory, counted in the workspace peak.
+    Tensor make(size_t rows, size_t cols, bool bf16) {
+        Tensor t;
+        t.rows = rows;
+        t.cols = cols;
+        t.bf16 = bf16;
+        const size_t bytes = t.bytes() ? t.bytes() : 1;
+        void *p = nullptr;
+        cuda_ok(cudaMallocAsync(&p, bytes, stream), "activation allocation");
+        memory->add(bytes);
+        auto mem = memory;
+        cudaStream_t s = stream;
+        t.mem = std::shared_ptr<void>(p, [mem, s, bytes](void *q) {
+            cudaFreeAsync(q, s);
+            mem->live.fetch_sub(bytes);
+        });
+        return t;
+    }
+    void *scratch(size_t bytes, Tensor &holder) {
+        holder = make((bytes + 3) / 4, 1, false);
+        return holder.data();
+    }
+};
+
+namespace {
+// y = x W^T (+ b): cuBLAS GEMM into fp32, then the bias / rounding epilogue.
+// bias_after_round: the reference's image_conv -- r(r(x W^T) + b).
+Tensor linear(Context &c, const Tensor &x, const Tensor &w, const Tensor *b,
+              bool bias_after_round = false) {
+    require(x.cols == w.cols, "Linear dimensions disagree", OMNI_INVALID_MODEL);
+    const size_t m = x.rows, n = w.rows, k = x.cols;
+    Tensor y = c.make(m, n, x.bf16);
+    if (m == 0)
+        return y;
+    Tensor acc_holder;
+    float *acc = x.bf16 ? static_cast<float *>(c.scratch(m * n * 4, acc_holder))
+                        : static_cast<float *>(y.data());
+    const float one = 1.f, zero = 0.f;
+    blas_ok(cublasGemmEx(c.blas, CUBLAS_OP_T, CUBLAS_OP_N, static_cast<int>(n), static_cast<int>(m),
+                         static_cast<int>(k), &one, w.data(), x.bf16 ? CUDA_R_16BF : CUDA_R_32F,
+                         static_cast<int>(k), x.data(), x.bf16 ? CUDA_R_16BF : CUDA_R_32F,
+                         static_cast<int>(k), &zero, acc, CUDA_R_32F, static_cast<int>(n),
+                         x.bf16 ? CUBLAS_COMPUTE_32F : CUBLAS_COMPUTE_32F_PEDANTIC,
+                         CUBLAS_GEMM_DEFAULT),
+            "linear");
+    const bool fused_bias = b && !bias_after_round;
+    cuda_ok(static_cast<cudaError_t>(graph::linear_epilogue(acc, fused_bias ? b->data() : nullptr,
+                                                            b ? b->bf16 : false, y.data(), y.bf16, m,
+                                                            n, c.stream)),
+            "linear epilogue");
+    if (b && bias_after_round)
+        cuda_ok(static_cast<cudaError_t>(graph::bias(y.data(), b->data(), y.bf16, m, n, c.stream)),
+                "bias");
+    return y;
+}
+
+Tensor layer_norm(Context &c, const Tensor &x, const Tensor &w, const Tensor &b, float eps) {
+    Tensor y = c.make(x.rows, x.cols, x.bf16);
+    cuda_ok(static_cast<cudaError_t>(graph::layer_norm(x.data(), w.data(), b.data(), y.data(), x.bf16,
+                                                       x.rows, x.cols, eps, c.stream)),
+            "layer norm");
+    return y;
+}
+
+void add_in_place(Context &c, Tensor &x, const Tensor &y) {
+    require(x.cols == y.cols && y.rows >= x.rows && x.bf16 == y.bf16, "Residual dimensions disagree",
+            OMNI_INTERNAL_ERROR);
+    cuda_ok(static_cast<cudaError_t>(graph::add(x.data(), y.data(), x.bf16, x.size(), c.stream)), "add");
+}
+
+void gelu_in_place(Context &c, Tensor &x) {
+    cuda_ok(static_cast<cudaError_t>(graph::gelu(x.data(), x.bf16, x.size(), c.stream)), "gelu");
+}
+
+// Ops::attention on [n, heads*hd] (fused: [n, 3*heads*hd]) rows.
+Tensor attention(Context &c, const Tensor &q, const Tensor *k, const Tensor *v, size_t heads,
+                 size_t block, size_t valid, bool fused) {
+    const size_t n = q.rows, d = fused ? q.cols / 3 : q.cols, hd = d / heads;
+    Tensor y = c.make(n, d, q.bf16);
+    if (!q.bf16 && !c.audio_bf16) {
+        require(!fused, "fp32 fused attention is not used by the graphs", OMNI_INTERNAL_ERROR);
+        cuda_ok(static_cast<cudaError_t>(graph::attention_f32(
+                    static_cast<const float *>(q.data()), static_cast<const float *>(k->data()),
+                    static_cast<const float *>(v->data()), static_cast<float *>(y.data()), n, heads,
+                    hd, block, valid, c.stream)),
+                "attention");
+        return y;
+    }
+    const int dt = q.bf16 ? OMNI_B200_BF16 : OMNI_B200_F32;
+    const size_t ws_bytes = omni_b200_attention_rows_workspace(n, static_cast<int>(heads),
+                                                               static_cast<int>(hd), dt, fused ? 1 : 0);
+    Tensor ws_holder;
+    void *ws = ws_bytes ? c.scratch(ws_bytes, ws_holder) : nullptr;
+    op_ok(omni_b200_attention_rows(q.data(), fused ? nullptr : k->data(), fused ? nullptr : v->data(),
+                                   y.data(), n, static_cast<int>(heads), static_cast<int>(hd), block,
+                                   valid, fused ? 1 : 0, dt, dt, ws, ws_bytes, c.stream),
+          "attention");
+    return y;
+}
+
+std::vector<uint16_t> quantize(Context &c, const Tensor &x, const Tensor &cb, const Tensor &cbnorm) {
+    c.check();
+    const int profile = x.bf16 ? OMNI_B200_BF16 : OMNI_B200_F32;
+    const size_t ws_bytes = omni_b200_vq_workspace(x.rows, x.cols, cb.rows, profile);
+    Tensor ws_holder, ids_holder;
+    void *ws = c.scratch(ws_bytes, ws_holder);
+    void *ids = c.scratch(x.rows * 2, ids_holder);
+    op_ok(omni_b200_vq_argmin(x.data(), cb.data(), cbnorm.data(), ids, x.rows, x.cols, cb.rows, profile,
+                              1, ws, ws_bytes, c.stream),
+          "quantize");
+    std::vector<uint16_t> out(x.rows);
+    cuda_ok(cudaMemcpyAsync(out.data(), ids, x.rows * 2, cudaMemcpyDeviceToHost, c.stream), "ids");
+    cuda_ok(cudaStreamSynchronize(c.stream), "quantize");
+    op_ok(omni_b200_sync_check(c.stream), "quantize");
+    return out;
+}
+
+std::vector<float> download(Context &c, const Tensor &t) {
+    std::vector<float> out(t.size());
+    if (t.size() == 0)
+        return out;
+    Tensor tmp;
+    const float *src = static_cast<const float *>(t.data());
+    if (t.bf16) {
+        tmp = c.make(t.rows, t.cols, false);
+        cuda_ok(static_cast<cudaError_t>(graph::to_float(t.data(), static_cast<float *>(tmp.data()), true,
+                                                         t.size(), c.stream)),
+                "download");
+        src = static_cast<const float *>(tmp.data());
+    }
+    cuda_ok(cudaMemcpyAsync(out.data(), src, t.size() * 4, cudaMemcpyDeviceToHost, c.stream), "download");
+    cuda_ok(cudaStreamSynchronize(c.stream), "download");
+    return out;
+}
+
+void trace(Context &c, const Tensor &x, const std::string &stage) {
+    if (c.trace) {
+        const std::vector<float> v = download(c, x);
+        c.trace(c.trace_user, stage.c_str(), v.data(), x.rows, x.cols);
+    }
+}
+
+void finite_input(const float *p, size_t n) {
+    for (size_t i = 0; i < n; ++i)
+        require(std::isfinite(p[i]), "Input contains a non-finite value");
+}
+
+Tensor upload(Context &c, const float *host, size_t rows, size_t cols, bool bf16) {
+    Tensor staged = c.make(rows, cols, false);
+    cuda_ok(cudaMemcpyAsync(staged.data(), host, rows * cols * 4, cudaMemcpyHostToDevice, c.stream),
+            "upload");
+    if (!bf16)
+        return staged;
+    Tensor t = c.make(rows, cols, true);
+    cuda_ok(static_cast<cudaError_t>(graph::convert(static_cast<const float *>(staged.data()), t.data(),
+                                                    true, rows * cols, c.stream)),
+            "upload");
+    return t;
+}
+} // namespace
+
+// Audio graph (src/runtime.cpp:30-75): causal conv stem, pre-norm encoder
+// layers with block-causal attention, mean-pool by 4, fp32 VQ.
+std::vector<uint16_t> encode_audio(Context &c, const float *mel, uint32_t frames, uint32_t valid) {
+    const Model &m = *c.model;
+    const Config &cfg = m.cfg;
+    c.check();
+    finite_input(mel, size_t(frames) * cfg.input_channels);
+    std::vector<float> tr(size_t(frames) * cfg.input_channels);
+    for (size_t t = 0; t < frames; ++t)
+        for (size_t j = 0; j < cfg.input_channels; ++j)
+            tr[t * cfg.input_channels + j] = mel[j * size_t(frames) + t];
+    Tensor x = upload(c, tr.data(), frames, cfg.input_channels, false);
+    auto conv = [&](const Tensor &in, size_t stride, const char *name) {
+        Tensor g = c.make((in.rows + stride - 1) / stride, in.cols * 3, in.bf16);
+        cuda_ok(static_cast<cudaError_t>(graph::conv_gather(in.data(), g.data(), in.bf16, in.rows, in.cols,
+                                                            stride, c.stream)),
+                "conv gather");
+        Tensor y = linear(c, g, m.get(std::string(name) + ".weight"), m.opt(std::string(name) + ".bias"));
+        gelu_in_place(c, y);
+        return y;
+    };
+    x = conv(x, 1, "conv1");
+    x = conv(x, 2, "conv2");
+    add_in_place(c, x, m.get("embed_positions.weight"));
+    trace(c, x, "embedding");
+    for (uint32_t i = 0; i < cfg.layers; ++i) {
+        c.check();
+        const std::string p = "layers." + std::to_string(i) + ".";
+        Tensor z = layer_norm(c, x, m.get(p + "self_attn_layer_norm.weight"),
+                              m.get(p + "self_attn_layer_norm.bias"), 1e-5f);
+        auto proj = [&](const Tensor &in, const std::string &name) {
+            return linear(c, in, m.get(name + ".weight"), m.opt(name + ".bias"));
+        };
+        Tensor q = proj(z, p + "self_attn.q_proj"), k = proj(z, p + "self_attn.k_proj"),
+               v = proj(z, p + "self_attn.v_proj");
+        z = attention(c, q, &k, &v, cfg.heads, cfg.block_size, (valid + 1) / 2, false);
+        z = proj(z, p + "self_attn.out_proj");
+        add_in_place(c, x, z);
+        z = layer_norm(c, x, m.get(p + "final_layer_norm.weight"), m.get(p + "final_layer_norm.bias"), 1e-5f);
+        z = proj(z, p + "fc1");
+        gelu_in_place(c, z);
+        z = proj(z, p + "fc2");
+        add_in_place(c, x, z);
+        trace(c, x, "layer." + std::to_string(i));
+    }
+    c.check();
+    Tensor pooled = c.make((x.rows + cfg.pool_size - 1) / cfg.pool_size, x.cols, x.bf16);
+    cuda_ok(static_cast<cudaError_t>(graph::pool(x.data(), pooled.data(), x.bf16, x.rows, x.cols,
+                                                 cfg.pool_size, c.stream)),
+            "pool");
+    pooled.rows = (valid + 7) / 8;
+    c.features = pooled;
+    return quantize(c, c.features, m.get("codebook.weight"), m.cbnorm);
+}
+
+// Image graph (src/runtime.cpp:76-130): patch embedding, interpolated
+// positions, pre-norm blocks with fused-QKV attention, 1x1 projection, L2
+// normalisation, bf16 VQ.
+std::vector<uint16_t> encode_image(Context &c, const float *pixels, uint32_t height, uint32_t width) {
+    const Model &m = *c.model;
+    const Config &cfg = m.cfg;
+    c.check();
+    finite_input(pixels, size_t(height) * width * 3);
+    const size_t P = cfg.patch_size, gh = height / P, gw = width / P, n = gh * gw;
+    Tensor px = upload(c, pixels, 3, size_t(height) * width, false);
+    Tensor patches = c.make(n, 8 * P * P, true);
+    cuda_ok(static_cast<cudaError_t>(graph::image_patches(static_cast<const float *>(px.data()),
+                                                          patches.data(), height, width, P, c.stream)),
+            "patches");
+    px = {};
+    Tensor x = linear(c, patches, m.get("patch_embed.proj.weight"), &m.get("patch_embed.proj.bias"), true);
+    patches = {};
+    trace(c, x, "patch");
+    Tensor pos = c.make(n, cfg.width, true);
+    cuda_ok(static_cast<cudaError_t>(graph::interpolate(m.get("pos_embed").data(), pos.data(), true,
+                                                        cfg.pos_height, gh, gw, cfg.width, c.stream)),
+            "interpolate");
+    trace(c, pos, "position");
+    add_in_place(c, x, pos);
+    pos = {};
+    trace(c, x, "embedding");
+    for (uint32_t i = 0; i < cfg.layers; ++i) {
+        c.check();
+        const std::string p = "blocks." + std::to_string(i) + ".";
+        auto proj = [&](const Tensor &in, const std::string &name) {
+            return linear(c, in, m.get(name + ".weight"), m.opt(name + ".bias"));
+        };
+        Tensor z = layer_norm(c, x, m.get(p + "norm1.weight"), m.get(p + "norm1.bias"), 1e-6f);
+        if (i == 0)
+            trace(c, z, "norm1.0");
+        z = proj(z, p + "attn.qkv");
+        if (i == 0)
+            trace(c, z, "qkv.0");
+        z = attention(c, z, nullptr, nullptr, cfg.heads, 0, n, true);
+        if (i == 0)
+            trace(c, z, "attention.0");
+        z = proj(z, p + "attn.proj");
+        add_in_place(c, x, z);
+        if (i == 0)
+            trace(c, x, "residual1.0");
+        z = layer_norm(c, x, m.get(p + "norm2.weight"), m.get(p + "norm2.bias"), 1e-6f);
+        z = proj(z, p + "mlp.fc1");
+        if (i == 0)
+            trace(c, z, "fc1.0");
+        gelu_in_place(c, z);
+        if (i == 0)
+            trace(c, z, "gelu.0");
+        z = proj(z, p + "mlp.fc2");
+        if (i == 0)
+            trace(c, z, "fc2.0");
+        add_in_place(c, x, z);
+        trace(c, x, "layer." + std::to_string(i));
+    }
+    c.check();
+    x = linear(c, x, m.get("quant_conv.weight"), &m.get("quant_conv.bias"), true);
+    trace(c, x, "projected");
+    Tensor f = c.make(x.rows, x.cols, true);
+    cuda_ok(static_cast<cudaError_t>(graph::normalize(x.data(), f.data(), true, x.rows, x.cols, c.stream)),
+            "normalize");
+    c.features = f;
+    return quantize(c, c.features, m.get("quantize.embedding.weight"), m.cbnorm);
+}
+
+} // namespace rt
+} // namespace omni_b200
+
+// --------------------------------------------------------------- C ABI
+struct omni_model {
+    std::shared_ptr<omni_b200::rt::Model> impl;
+};
+struct omni_context {
+    omni_b200::rt::Context impl;
+};
+
+namespace {
+thread_local std::string g_abi_error;
+template <class F> int guarded(F f) {
+    try {
+        g_abi_error.clear();
+        f();
+        return OMNI_OK;
+    } catch (const omni_b200::rt::Fail &e) {
+        g_abi_error = e.what();
+        return e.code;
+    } catch (const std::bad_alloc &) {
+        g_abi_error = "Allocation failed";
+        return OMNI_OUT_OF_MEMORY;
+    } catch (const std::exception &e) {
+        g_abi_error = e.what();
+        return OMNI_INTERNAL_ERROR;
+    } catch (...) {
+        g_abi_error = "Unknown native failure";
+        return OMNI_INTERNAL_ERROR;
+    }
+}
+struct Running {
+    omni_b200::rt::Context &c;
+    explicit Running(omni_b200::rt::Context &ctx) : c(ctx) {
+        omni_b200::rt::require(!c.running.test_and_set(), "Context is already executing");
+    }
+    ~Running() { c.running.clear(); }
+};
+} // namespace
+
+using omni_b200::rt::require;
+
+extern "C" {
+const char *omni_last_error(void) { return g_abi_error.c_str(); }
+const char *omni_version(void) { return "0.1.0+b200"; }
+int omni_has_cuda(void) {
+    int n = 0;
+    return cudaGetDeviceCount(&n) == cudaSuccess && n > 0 ? 1 : 0;
+}
+int omni_model_load(const char *path, int backend, int device, omni_model **out) {
+    if (out)
+        *out = nullptr;
+    return guarded([&] {
+        require(out != nullptr, "Output handle is null");
+        auto m = omni_b200::rt::load_model(path, backend, device);
+        *out = new omni_model{std::move(m)};
+    });
+}
+void omni_model_free(omni_model *m) { delete m; }
+int omni_model_get_info(const omni_model *m, omni_model_info *out) {
+    return guarded([&] {
+        require(m && out && out->struct_size >= sizeof(omni_model_info), "Invalid model info arguments");
+        const auto &c = m->impl->cfg;
+        *out = {sizeof(omni_model_info), c.kind, c.layers, c.width, c.heads, c.code_dim, c.vocab_size,
+                uint32_t(m->impl->backend), m->impl->weight_bytes};
+    });
+}
+int omni_context_create(omni_model *m, omni_context **out) {
+    if (out)
+        *out = nullptr;
+    return guarded([&] {
+        require(m && out, "Invalid context arguments");
+        auto c = std::make_unique<omni_context>();
+        c->impl.model = m->impl;
+        omni_b200::rt::cuda_ok(cudaSetDevice(m->impl->device), "set device");
+        omni_b200::rt::cuda_ok(cudaStreamCreateWithFlags(&c->impl.stream, cudaStreamNonBlocking),
+                               "stream create");
+        omni_b200::rt::blas_ok(cublasCreate(&c->impl.blas), "cuBLAS handle");
+        omni_b200::rt::blas_ok(cublasSetStream(c->impl.blas, c->impl.stream), "cuBLAS stream");
+        const char *fast = std::getenv("OMNI_B200_AUDIO_BF16");
+        c->impl.audio_bf16 = fast && *fast && *fast != '0';
+        *out = c.release();
+    });
+}
+void omni_context_free(omni_context *c) { delete c; }
+void omni_context_cancel(omni_context *c) {
+    if (c)
+        c->impl.cancelled.store(true);
+}
+void omni_context_reset_cancel(omni_context *c) {
+    if (c)
+        c->impl.cancelled.store(false);
+}
+int omni_context_set_trace(omni_context *c, omni_trace_callback callback, void *user) {
+    return guarded([&] {
+        require(c != nullptr, "Invalid context");
+        Running guard(c->impl);
+        c->impl.trace = callback;
+        c->impl.trace_user = user;
+    });
+}
+int omni_encode_audio(omni_context *c, const float *mel, uint32_t frames, uint32_t valid,
+                      uint16_t *codes, size_t capacity, size_t *count) {
+    return guarded([&] {
+        require(c && mel && count, "Invalid audio pointers");
+        const auto &cfg = c->impl.model->cfg;
+        require(cfg.kind == OMNI_AUDIO, "Model is not an audio tokenizer");
+        require(frames > 0 && frames % 8 == 0 && frames <= 3000 && frames / 2 <= cfg.pos_height &&
+                    valid > 0 && valid <= frames,
+                "Invalid audio frame lengths");
+        *count = (valid + 7) / 8;
+        require(codes && capacity >= *count, "Output capacity is too small");
+        Running guard(c->impl);
+        omni_b200::rt::cuda_ok(cudaSetDevice(c->impl.model->device), "set device");
+        c->impl.features = {};
+        const auto ids = omni_b200::rt::encode_audio(c->impl, mel, frames, valid);
+        std::copy(ids.begin(), ids.end(), codes);
+    });
+}
+int omni_encode_image(omni_context *c, const float *pixels, uint32_t height, uint32_t width,
+                      uint16_t *codes, size_t capacity, size_t *count) {
+    return guarded([&] {
+        require(c && pixels && count, "Invalid image pointers");
+        const auto &cfg = c->impl.model->cfg;
+        require(cfg.kind == OMNI_IMAGE, "Model is not an image tokenizer");
+        require(height > 0 && width > 0 && height % cfg.patch_size == 0 && width % cfg.patch_size == 0,
+                "Invalid image dimensions");
+        const uint64_t patches = uint64_t(height / cfg.patch_size) * (width / cfg.patch_size);
+        // Activation, patch, attention and VQ buffers stay within int-indexed BLAS
+        // dimensions (the reference's capacity rule, src/runtime.cpp:253-262).
+        const uint64_t columns = std::max({uint64_t(8) * cfg.patch_size * cfg.patch_size,
+                                          uint64_t(3) * cfg.width, uint64_t(cfg.ffn),
+                                          uint64_t(cfg.code_dim), uint64_t(256) * cfg.heads,
+                                          uint64_t(1024)});
+        const uint64_t elements = std::min(uint64_t(std::numeric_limits<int>::max()),
+                                          uint64_t(std::numeric_limits<size_t>::max() / sizeof(float)));
+        require(patches <= elements / columns, "Image dimensions exceed native tensor indexing capacity");
+        *count = static_cast<size_t>(patches);
+        require(codes && capacity >= *count, "Output capacity is too small");
+        Running guard(c->impl);
+        omni_b200::rt::cuda_ok(cudaSetDevice(c->impl.model->device), "set device");
+        c->impl.features = {};
+        const auto ids = omni_b200::rt::encode_image(c->impl, pixels, height, width);
+        std::copy(ids.begin(), ids.end(), codes);
+    });
+}
+int omni_context_copy_features(omni_context *c, float *out, size_t capacity, size_t *count) {
+    return guarded([&] {
+        require(c && count, "Invalid feature pointers");
+        Running guard(c->impl);
+        *count = c->impl.features.size();
+        require(*count > 0, "No completed feature tensor");
+        require(out && capacity >= *count, "Feature output capacity is too small");
+        omni_b200::rt::cuda_ok(cudaSetDevice(c->impl.model->device), "set device");
+        const auto v = omni_b200::rt::download(c->impl, c->impl.features);
+        std::copy(v.begin(), v.end(), out);
+    });
+}
+uint64_t omni_context_peak_workspace(const omni_context *c) {
+    return c ? c->impl.memory->peak.load() : 0;
+}
+} // extern "C"

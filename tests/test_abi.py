@@ -55,3 +55,65 @@ def test_workspace_queries():
     assert lib.lib.omni_b200_attention_rows_workspace(729, 16, 72, 1, 0) == 0
     assert lib.lib.omni_b200_attention_rows_workspace(1500, 20, 64, 0, 0) >= 3 * 20 * 1500 * 64 * 2
     assert lib.lib.omni_b200_vq_workspace(1000, 64, 16384, 1) >= 8000
+
+
+# ------------------------------------------------ the reference's outer C ABI
+ABI_HEADER = ROOT / "include" / "omni_abi.h"
+
+
+def abi_symbols():
+    return sorted(set(re.findall(r"OMNI_ABI_API\s+[\w\s\*]+?\b(omni_\w+)\s*\(", ABI_HEADER.read_text())))
+
+
+def test_outer_abi_declares_and_exports_the_15_entry_points():
+    load_package()
+    import omni_tokenizer_b200.abi as abi
+
+    names = abi_symbols()
+    assert names == sorted(abi.SYMBOLS) and len(names) == 15
+    lib = abi.OmniLib(ROOT / "omni-tokenizer_b200" / "libomni_b200.so")  # binds all 15
+    assert lib.lib.omni_version().startswith(b"0.1.0")
+
+
+def test_outer_abi_errors_without_a_device(tmp_path):
+    load_package()
+    import omni_tokenizer_b200.abi as abi
+    import omni_tokenizer_b200.omnivq as ov
+
+    lib = abi.OmniLib(ROOT / "omni-tokenizer_b200" / "libomni_b200.so")
+    path = tmp_path / "tiny.omni"
+    ov.write_random_model(path, ov.image_config(layers=1, width=16, heads=2, ffn=32, patch=4, grid=2,
+                                                code_dim=8, vocab=16), seed=3)
+    with pytest.raises(abi.OmniError) as e:  # only the CUDA backend exists here
+        lib.load(path, backend=abi.CPU)
+    assert e.value.status == 4
+    handle = C.c_void_p()
+    assert lib.lib.omni_model_load(str(path).encode(), abi.CUDA, 0, None) == 1
+    assert lib.lib.omni_model_get_info(None, None) == 1
+    assert lib.lib.omni_context_create(None, C.byref(handle)) == 1 and not handle
+    assert lib.lib.omni_context_peak_workspace(None) == 0
+    lib.lib.omni_context_cancel(None)  # no-ops on NULL, like the reference
+    lib.lib.omni_model_free(None)
+    if not lib.lib.omni_has_cuda():
+        with pytest.raises(abi.OmniError) as e:
+            lib.load(path)
+        assert e.value.status == 4
+
+
+def test_model_writer_round_trips_through_the_reference_loader(tmp_path):
+    """omnivq.write_model output is accepted by the reference's own loader (when built)."""
+    ref = ROOT / "oracle" / "_ref" / "libomni_ref_full.so"
+    if not ref.is_file():
+        pytest.skip("reference CPU library not built")
+    load_package()
+    import omni_tokenizer_b200.abi as abi
+    import omni_tokenizer_b200.omnivq as ov
+
+    lib = abi.OmniLib(ref)
+    for cfg in (ov.audio_config(layers=1, width=16, heads=2, ffn=32, mel=8, positions=16, block=8, vocab=32),
+                ov.image_config(layers=1, width=16, heads=2, ffn=32, patch=4, grid=2, code_dim=8, vocab=32)):
+        path = tmp_path / f"m{cfg.kind}.omni"
+        ov.write_random_model(path, cfg, seed=cfg.kind)
+        with lib.load(path, backend=abi.CPU) as m:
+            info = m.info()
+            assert (info.kind, info.layers, info.width, info.code_dim) == (cfg.kind, 1, 16, cfg.code_dim)

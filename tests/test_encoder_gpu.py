@@ -1,0 +1,188 @@
+"""The reference's outer C ABI on B200 (libomni_b200.so, include/omni_abi.h):
+whole audio and image encoder graphs against the reference's own CPU library
+(golden fixtures from tests/golden/encoder/make_encoder_golden.py; a live
+check when oracle/_ref/libomni_ref_full.so is present), plus the C API
+behaviours of omni-tokenizer src/runtime.cpp:131-288 that need a device.
+
+Tolerances: audio (fp32 profile) features within 1e-4 of the reference's fp32
+values, image (bf16 profile) features within 1/128 (the reference's own
+CUDA-vs-fixture tolerance, tests/test_native.py:55-58).  Codes: (1) this
+library's codes are exactly the oracle VQ of this library's features (ties
+aside: the BASELINE top-2 rule); (2) a code that differs from the reference's
+is one whose distance to the reference's features is within the bound the
+measured feature difference allows (|d(f, c) - d(f', c)| <= 2 |f - f'| |c| +
+| |f|^2 - |f'|^2 |), plus bf16 rounding of the distance.
+"""
+
+import ctypes as C
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from tests.conftest import ROOT, load_package
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).resolve().parent / "golden" / "encoder"
+
+
+@pytest.fixture(scope="module")
+def abi():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    load_package()
+    import omni_tokenizer_b200.abi as abi
+
+    return abi
+
+
+@pytest.fixture(scope="module")
+def ours(abi):
+    import os
+
+    path = os.environ.get("OMNI_B200_LIBRARY") or str(ROOT / "omni-tokenizer_b200" / "libomni_b200.so")
+    return abi.OmniLib(path)
+
+
+@pytest.fixture(scope="module")
+def golden():
+    return dict(np.load(GOLDEN / "golden.npz"))
+
+
+def _codebook(kind):
+    load_package()
+    import omni_tokenizer_b200.omnivq as ov
+    from tests.golden.encoder.make_encoder_golden import AUDIO_CFG, IMAGE_CFG
+
+    if kind == "audio":
+        cfg = ov.audio_config(**AUDIO_CFG)
+        cb = ov.random_tensors(cfg, seed=11)["codebook.weight"]
+    else:
+        cfg = ov.image_config(**IMAGE_CFG)
+        cb = O.round_bf16(ov.random_tensors(cfg, seed=12)["quantize.embedding.weight"])
+        cb = cb / np.maximum(O.round_bf16(np.sqrt((cb * cb).sum(1, keepdims=True))), O.round_bf16(np.float32(1e-12)))
+        cb = O.round_bf16(cb)
+    return cb
+
+
+def _check_codes(got, want, ours, ref, cb, bf16):
+    # (1) Our codes are the oracle VQ of our own features.
+    own = O.quantize(ours, cb, bf16=bf16).astype(np.int64)
+    mism = np.nonzero(got != own)[0]
+    if len(mism):
+        d1, d2 = O.quantize_top2(ours[mism], cb, bf16=bf16)
+        assert np.all((d2 - d1) < 1e-3 * np.abs(d1)), f"VQ of our features differs at rows {mism}"
+    # (2) Differences from the reference stay within the feature-difference bound.
+    mism = np.nonzero(got != want)[0]
+    f, g = ref.astype(np.float64), ours.astype(np.float64)
+    c = cb.astype(np.float64)
+    cmax = np.sqrt((c * c).sum(1)).max()
+    for r in mism:
+        d_want = ((f[r] - c[want[r]]) ** 2).sum()
+        d_got = ((f[r] - c[got[r]]) ** 2).sum()
+        delta = np.sqrt(((f[r] - g[r]) ** 2).sum())
+        slack = 2 * (2 * delta * cmax + abs((f[r] ** 2).sum() - (g[r] ** 2).sum()))
+        slack += (2.0 ** -6) * (abs(d_want) + 1.0) if bf16 else 1e-6 * (abs(d_want) + 1.0)
+        assert d_got - d_want <= slack, (r, d_got, d_want, slack)
+
+
+def test_audio_encoder_matches_reference(abi, ours, golden):
+    cb = _codebook("audio")
+    with ours.load(GOLDEN / "audio.omni", backend=abi.CUDA) as m:
+        info = m.info()
+        assert (info.kind, info.layers, info.width, info.backend) == (1, 2, 32, 1)
+        s = m.context()
+        for i in range(3):
+            mel, valid = golden[f"audio{i}_mel"], int(golden[f"audio{i}_valid"])
+            codes = s.encode_audio(mel, valid)
+            feats = s.features(len(codes))
+            want = golden[f"audio{i}_features"]
+            assert feats.shape == want.shape
+            np.testing.assert_allclose(feats, want, rtol=1e-4, atol=1e-4)
+            _check_codes(codes.astype(np.int64), golden[f"audio{i}_codes"].astype(np.int64), feats, want, cb, False)
+        assert s.peak_workspace > 0
+        s.close()
+
+
+def test_image_encoder_matches_reference(abi, ours, golden):
+    cb = _codebook("image")
+    with ours.load(GOLDEN / "image.omni", backend=abi.CUDA) as m:
+        s = m.context()
+        for i in range(3):
+            px = golden[f"image{i}_pixels"]
+            codes = s.encode_image(px)
+            feats = s.features(len(codes))
+            want = golden[f"image{i}_features"]
+            assert feats.shape == want.shape
+            assert np.abs(feats - want).max() <= 1 / 128
+            _check_codes(codes.astype(np.int64), golden[f"image{i}_codes"].astype(np.int64), feats, want, cb, True)
+        s.close()
+
+
+def test_live_reference_cross_check(abi, ours):
+    """Same inputs through the reference CPU library (when built) and this library."""
+    ref_path = ROOT / "oracle" / "_ref" / "libomni_ref_full.so"
+    if not ref_path.is_file():
+        pytest.skip("reference CPU library not built")
+    ref = abi.OmniLib(ref_path)
+    rng = np.random.default_rng(77)
+    px = rng.uniform(-1, 1, (3, 40, 24)).astype(np.float32)
+    with ref.load(GOLDEN / "image.omni", backend=abi.CPU) as rm, ours.load(GOLDEN / "image.omni") as om:
+        rs, os_ = rm.context(), om.context()
+        want, got = rs.encode_image(px), os_.encode_image(px)
+        wf, gf = rs.features(len(want)), os_.features(len(got))
+        assert np.abs(wf - gf).max() <= 1 / 128
+        _check_codes(got.astype(np.int64), want.astype(np.int64), gf, wf, _codebook("image"), True)
+        rs.close(), os_.close()
+
+
+def test_api_behaviour(abi, ours, golden):
+    lib = ours.lib
+    with ours.load(GOLDEN / "image.omni") as m:
+        s = m.context()
+        # No features before the first encode.
+        count = C.c_size_t()
+        buf = np.zeros(4, np.float32)
+        assert lib.omni_context_copy_features(s.handle, buf.ctypes.data_as(C.POINTER(C.c_float)), 4, C.byref(count)) == 1
+        # Size query: NULL codes, zero capacity -> INVALID_ARGUMENT with the count.
+        px = golden["image1_pixels"]
+        assert lib.omni_encode_image(s.handle, px.ctypes.data_as(C.POINTER(C.c_float)), 48, 32, None, 0,
+                                     C.byref(count)) == 1
+        assert count.value == 24
+        assert b"capacity is too small" in lib.omni_last_error()
+        # Cancel -> CANCELLED; reset -> works again.
+        s.cancel()
+        with pytest.raises(abi.OmniError) as e:
+            s.encode_image(px)
+        assert e.value.status == 6
+        s.reset_cancel()
+        assert s.encode_image(px).size == 24
+        # Trace callback: the reference's image stage names.
+        stages = []
+
+        def cb(user, stage, values, rows, cols):
+            stages.append((stage.decode(), rows, cols))
+
+        fn = abi.TRACE(cb)
+        assert lib.omni_context_set_trace(s.handle, fn, None) == 0
+        s.encode_image(golden["image0_pixels"])
+        names = [n for n, _, _ in stages]
+        assert names == ["patch", "position", "embedding", "norm1.0", "qkv.0", "attention.0", "residual1.0",
+                         "fc1.0", "gelu.0", "fc2.0", "layer.0", "layer.1", "projected"]
+        assert stages[4][1:] == (16, 96)
+        # Non-finite input -> INVALID_ARGUMENT.
+        bad = golden["image0_pixels"].copy()
+        bad[0, 0, 0] = np.nan
+        with pytest.raises(abi.OmniError) as e:
+            s.encode_image(bad)
+        assert e.value.status == 1
+        s.close()
+    # Invalid model files.
+    with pytest.raises(abi.OmniError) as e:
+        ours.load(GOLDEN / "no_such_model.omni")
+    assert e.value.status == 2
+    with pytest.raises(abi.OmniError) as e:
+        ours.load(GOLDEN / "golden.npz")
+    assert e.value.status == 3
