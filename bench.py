@@ -54,6 +54,22 @@ CONFIGS = {
                      workload="VQ argmin op, audio-shaped (x 24000x64 vs codebook 16384x64, bf16)"),
     "vq_image": dict(kind="vq", N=373248, K=16384, dim=32, seed=1011,
                      workload="VQ argmin op, image-shaped (x 373248x32 vs codebook 16384x32, bf16)"),
+    # Whole encoders through the reference's omni_* C ABI (libomni_b200.so), on
+    # randomly initialised OMNIVQ01 models of production shape.
+    "c4": dict(kind="encoder", modality="audio", items=16, mel=80, frames=3000, width=1024, layers=24, heads=16,
+               ffn=4096, positions=1500, block=1500, vocab=16384, seed=1004, audio_bf16=False,
+               workload="full audio encoder (BASELINE config 4 body: 24 layers, d 1024, 16 heads, ffn 4096, "
+                        "80 mel x 3000 frames; reference head: pool 4, fp32 VQ over 16384x1024)"),
+    "c4_bf16": dict(kind="encoder", modality="audio", items=16, mel=80, frames=3000, width=1024, layers=24,
+                    heads=16, ffn=4096, positions=1500, block=1500, vocab=16384, seed=1004, audio_bf16=True,
+                    workload="config 4 with OMNI_B200_AUDIO_BF16=1 (attention on the bf16 tcgen05 kernel)"),
+    # 378 = 27 x 14: the 27x27 patch grid a stride-14 conv takes from a 384x384
+    # image; the reference ABI wants sides that are multiples of the patch.
+    "c5": dict(kind="encoder", modality="image", items=512, size=378, patch=14, grid=27, width=1152, layers=27,
+               heads=16, ffn=4304, code_dim=32, vocab=16384, seed=1005,
+               workload="full image encoder (BASELINE config 5: 27 layers, d 1152, 16 heads of 72, ffn 4304, "
+                        "729 patches of 14x14 (384x384 cropped to 378x378), 32-dim L2-normalised bf16 VQ "
+                        "over 16384 codes)"),
 }
 METRIC = "attn TFLOP/s vs B200 BF16 peak"
 L2_BYTES = 126 * 1024 * 1024
@@ -230,6 +246,266 @@ def cpu_reference_sample(cfg, budget_s, items=None):
         done += rows
         chunks += 1
     return work, t_total, threads, kind, f"{done} rows x {K} codes, bf16 profile, src/cpu.cpp Ops::quantize"
+
+
+# ------------------------------------------------------------------ whole encoders
+def encoder_model_config(cfg, layers=None):
+    load_package()
+    import omni_tokenizer_b200.omnivq as ov
+
+    n = cfg["layers"] if layers is None else layers
+    if cfg["modality"] == "audio":
+        return ov, ov.audio_config(layers=n, width=cfg["width"], heads=cfg["heads"], ffn=cfg["ffn"],
+                                   mel=cfg["mel"], positions=cfg["positions"], block=cfg["block"],
+                                   vocab=cfg["vocab"])
+    return ov, ov.image_config(layers=n, width=cfg["width"], heads=cfg["heads"], ffn=cfg["ffn"],
+                               patch=cfg["patch"], grid=cfg["grid"], code_dim=cfg["code_dim"], vocab=cfg["vocab"])
+
+
+def encoder_flops(cfg, layers=None):
+    """Algorithmic FLOPs of one item (one 30 s segment or one image): GEMM
+    multiply-adds x 2 over the reference graph, attention 4 L^2 d per layer."""
+    W, F = cfg["width"], cfg["ffn"]
+    n = cfg["layers"] if layers is None else layers
+    if cfg["modality"] == "audio":
+        T = cfg["frames"]
+        L = (T + 1) // 2
+        stem = 2.0 * T * 3 * cfg["mel"] * W + 2.0 * L * 3 * W * W
+        body = n * (2.0 * L * (4 * W * W + 2 * W * F) + 4.0 * L * L * W)
+        vq = 2.0 * ((L + 3) // 4) * cfg["vocab"] * W
+        return stem + body + vq
+    g = cfg["size"] // cfg["patch"]
+    L = g * g
+    stem = 2.0 * L * 3 * cfg["patch"] ** 2 * W
+    body = n * (2.0 * L * (4 * W * W + 2 * W * F) + 4.0 * L * L * W)
+    head = 2.0 * L * W * cfg["code_dim"] + 2.0 * L * cfg["vocab"] * cfg["code_dim"]
+    return stem + body + head
+
+
+def encoder_inputs(cfg, count, seed):
+    """U(-1, 1) log-mel segments [mel, frames] or images [3, size, size]."""
+    rng = np.random.default_rng(seed)
+    if cfg["modality"] == "audio":
+        shape = (cfg["mel"], cfg["frames"])
+    else:
+        shape = (3, cfg["size"], cfg["size"])
+    return [rng.uniform(-1.0, 1.0, shape).astype(np.float32) for _ in range(count)]
+
+
+def encode_item(session, cfg, x):
+    if cfg["modality"] == "audio":
+        return session.encode_audio(x, cfg["frames"])
+    return session.encode_image(x)
+
+
+def encoder_unit(cfg):
+    return ("audio-s/s", 30.0 * cfg["frames"] / 3000) if cfg["modality"] == "audio" else ("images/s", 1.0)
+
+
+def cpu_encoder_sample(cfg, tmpdir, repeats=1):
+    """The reference's own CPU library (oracle/_ref/libomni_ref_full.so, all host
+    threads) on 1- and 2-layer models of the workload's width, one item each;
+    the per-item time of the full depth is extrapolated linearly in layers.
+    Returns (seconds_per_item, threads, sample_text) or None without the library."""
+    from oracle import oracle as O
+
+    lib_path = ROOT / "oracle" / "_ref" / "libomni_ref_full.so"
+    if not lib_path.is_file():
+        return None
+    load_package()
+    import omni_tokenizer_b200.abi as abi
+
+    ref = abi.OmniLib(lib_path)
+    x = encoder_inputs(cfg, 1, cfg["seed"] + 99)[0]
+    times = {}
+    for n in (1, 2):
+        ov, mc = encoder_model_config(cfg, layers=n)
+        path = os.path.join(tmpdir, f"cpu_{cfg['modality']}_{n}.omni")
+        ov.write_random_model(path, mc, seed=cfg["seed"] + n)
+        with ref.load(path, backend=abi.CPU) as m:
+            s = m.context()
+            best = None
+            for _ in range(repeats):
+                t0 = time.perf_counter()
+                encode_item(s, cfg, x)
+                dt = time.perf_counter() - t0
+                best = dt if best is None else min(best, dt)
+            s.close()
+        times[n] = best
+        os.remove(path)
+    per_layer = max(times[2] - times[1], 0.0)
+    per_item = times[1] + (cfg["layers"] - 1) * per_layer
+    sample = (f"1 item through 1- and 2-layer models of the same width on the reference CPU backend "
+              f"({times[1]:.2f} s, {times[2]:.2f} s); per-item time extrapolated to {cfg['layers']} layers")
+    return per_item, O.cpu_threads(), sample
+
+
+def run_encoder(args, cfg, reference=False):
+    import tempfile
+
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    unit_name, unit_per_item = encoder_unit(cfg)
+    flops_item = encoder_flops(cfg)
+    tmpdir = tempfile.mkdtemp(prefix="omni_bench_")
+    if reference:
+        if rank != 0:
+            return 0
+        # Each step is one item per model depth; the best of `steps` repeats counts.
+        got = cpu_encoder_sample(cfg, tmpdir, repeats=max(1, min(args.steps, 3)))
+        if got is None:
+            print(json.dumps({"impl": "reference", "unavailable": "reference CPU library oracle/_ref/"
+                              "libomni_ref_full.so not built"}), flush=True)
+            return 0
+        per_item, threads, sample = got
+        value = unit_per_item / per_item
+        line = {
+            "impl": "reference", "metric": f"{unit_name} (full encoder)", "value": value, "unit": unit_name,
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 * per_item * cfg["items"], "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32" if cfg["modality"] == "audio" else "bf16",
+            "data": "synthetic (seeded U(-1,1) inputs, random-init weights)",
+            "config": {"workload": cfg["workload"], "config": args.config, "items_per_step": cfg["items"],
+                       "extrapolated": True},
+            "cpu_baseline": {"value": value, "unit": unit_name, "cores": threads, "kind": "reference",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": unit_name, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }
+        print(json.dumps(line), flush=True)
+        return 0
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    if cfg.get("audio_bf16"):
+        os.environ["OMNI_B200_AUDIO_BF16"] = "1"
+    load_package()
+    import omni_tokenizer_b200.abi as abi
+
+    lib = abi.OmniLib(ROOT / "omni-tokenizer_b200" / "libomni_b200.so")
+    # Every rank writes the same seeded model into its own temporary directory
+    # (no shared filesystem is assumed between ranks).
+    ov, mc = encoder_model_config(cfg)
+    model_path = os.path.join(tmpdir, f"{args.config}.omni")
+    t_write = time.perf_counter()
+    ov.write_random_model(model_path, mc, seed=cfg["seed"])
+    t_write = time.perf_counter() - t_write
+    # Strong scaling: the step's items split evenly across ranks.
+    share = [len(r) for r in np.array_split(np.arange(cfg["items"]), world)]
+    mine = share[rank]
+    inputs = encoder_inputs(cfg, mine, cfg["seed"] + 7919 * rank)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    with lib.load(model_path, backend=abi.CUDA, device=local) as model:
+        session = model.context()
+        for i in range(max(args.warmup, 3)):
+            encode_item(session, cfg, inputs[i % len(inputs)])
+        # Kernel launches of one item, by name, through the profiler (untimed).
+        launches_item, library_launches = None, None
+        try:
+            from torch.profiler import ProfilerActivity, profile
+
+            with profile(activities=[ProfilerActivity.CUDA]) as prof:
+                encode_item(session, cfg, inputs[0])
+                torch.cuda.synchronize()
+            names = [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA
+                     and "memcpy" not in e.name.lower() and "memset" not in e.name.lower()]
+            lib_like = ("gemm", "cutlass", "cublas", "nvjet", "xmma", "splitk", "reduce_1block")
+            library_launches = sum(1 for n in names if any(k in n.lower() for k in lib_like))
+            launches_item = len(names) - library_launches
+        except Exception:
+            pass
+        sampler = ClockSampler(local)
+        sampler.start()
+        barrier()
+        t0 = time.perf_counter()
+        codes_bytes = 0
+        for _ in range(args.steps):
+            for x in inputs:
+                codes_bytes += encode_item(session, cfg, x).nbytes
+        torch.cuda.synchronize()
+        elapsed = time.perf_counter() - t0
+        barrier()
+        t1 = time.perf_counter()
+        sampler.stop()
+        peak_ws = session.peak_workspace
+        session.close()
+    clocks = sampler.summary(t0, t1)
+    os.remove(model_path)
+    if dist is not None:
+        t = torch.tensor([elapsed], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed = t.item()
+
+    items_total = cfg["items"] * args.steps
+    value = items_total * unit_per_item / elapsed
+    tflops = items_total * flops_item / elapsed / 1e12
+    pk, pk_kind = peaks()
+    peak = float(pk.get("bf16_tflops_sustained", pk.get("bf16_tflops", 1400.0)))
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        got = cpu_encoder_sample(cfg, tmpdir)
+        if got is not None:
+            per_item, threads, sample = got
+            cpu = {"value": unit_per_item / per_item, "unit": unit_name, "cores": threads, "kind": "reference",
+                   "sample": sample}
+    in_item = int(np.prod(inputs[0].shape)) * 4
+    if rank == 0:
+        line = {
+            "metric": f"{unit_name} (full encoder)",
+            "value": value,
+            "unit": unit_name,
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": max(args.warmup, 3),
+            "ms_per_step": 1e3 * elapsed / args.steps,
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "f32" if (cfg["modality"] == "audio" and not cfg.get("audio_bf16")) else "bf16",
+            "data": "synthetic (seeded U(-1,1) inputs, random-init weights of the named shape)",
+            "config": {
+                "workload": cfg["workload"],
+                "config": args.config,
+                "items_per_step": cfg["items"],
+                "items_per_rank": share,
+                "flops_per_item": flops_item,
+                "parallelism": f"item-sharded replicas x{world}" if world > 1 else "single GPU",
+                "timing": "wall clock around synchronous omni_encode_* calls on host buffers, "
+                          "synchronize + barrier on both sides, max over ranks; value and e2e are "
+                          "the same measurement (the reference ABI takes host buffers only)",
+                "l2": "per-item weights above L2 size (streamed each layer); no flush",
+                "model_write_s": round(t_write, 1),
+                "peak_workspace_bytes": peak_ws,
+            },
+            "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak, "unit": "TFLOP/s",
+                         "frac": tflops / peak, "traffic": None,
+                         "peak_source": f"{pk_kind} bf16_tflops_sustained (whole-encoder FLOPs / wall time)"},
+            "e2e": {"value": value, "unit": unit_name, "h2d_bytes_per_step": in_item * cfg["items"],
+                    "d2h_bytes_per_step": codes_bytes // max(args.steps, 1) * world},
+            "cpu_baseline": cpu,
+            "gpu_launches": None if launches_item is None else launches_item * items_total,
+            "library_launches": None if library_launches is None else library_launches * items_total,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
 
 
 # ------------------------------------------------------------------ arms
@@ -466,6 +742,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     cfg = CONFIGS[args.config]
+    if cfg["kind"] == "encoder":
+        return run_encoder(args, cfg, reference=args.impl == "reference")
     if args.impl == "reference":
         return run_reference(args, cfg)
     return run_ours(args, cfg)

@@ -97,56 +97,63 @@ def tensor_shapes(cfg: Config) -> Dict[str, tuple]:
     return out
 
 
-def random_tensors(cfg: Config, seed: int = 0, std: float = 0.02) -> Dict[str, np.ndarray]:
-    """Seeded weights: N(0, std) matrices, N(1, 0.05) norm scales, N(0, 0.02) biases,
-    N(0, 1) codebook rows and positions of unit scale."""
+def _random_tensor(rng, name, shape) -> np.ndarray:
+    if name.endswith("norm.weight") or ".norm1.weight" in name or ".norm2.weight" in name \
+            or name.endswith("_layer_norm.weight"):
+        a = 1.0 + 0.05 * rng.standard_normal(shape)
+    elif name.endswith(".bias"):
+        a = 0.02 * rng.standard_normal(shape)
+    elif name in ("codebook.weight", "quantize.embedding.weight"):
+        a = rng.standard_normal(shape)
+    elif name in ("embed_positions.weight", "pos_embed"):
+        a = 0.1 * rng.standard_normal(shape)
+    else:
+        fan_in = int(np.prod(shape[1:]))
+        a = rng.standard_normal(shape) / np.sqrt(max(fan_in, 1))
+    return a.astype(np.float32)
+
+
+def random_tensors(cfg: Config, seed: int = 0) -> Dict[str, np.ndarray]:
+    """Seeded weights: N(0, 1/fan_in) matrices, N(1, 0.05) norm scales, N(0, 0.02)
+    biases, N(0, 1) codebook rows, positions with standard deviation 0.1."""
     rng = np.random.default_rng(seed)
-    out = {}
-    for name, shape in tensor_shapes(cfg).items():
-        if name.endswith("norm.weight") or ".norm1.weight" in name or ".norm2.weight" in name \
-                or name.endswith("_layer_norm.weight"):
-            a = 1.0 + 0.05 * rng.standard_normal(shape)
-        elif name.endswith(".bias"):
-            a = 0.02 * rng.standard_normal(shape)
-        elif name in ("codebook.weight", "quantize.embedding.weight"):
-            a = rng.standard_normal(shape)
-        elif name in ("embed_positions.weight", "pos_embed"):
-            a = 0.1 * rng.standard_normal(shape)
-        else:
-            fan_in = int(np.prod(shape[1:]))
-            a = rng.standard_normal(shape) / np.sqrt(max(fan_in, 1))
-        out[name] = a.astype(np.float32)
-    return out
+    return {name: _random_tensor(rng, name, shape) for name, shape in tensor_shapes(cfg).items()}
 
 
-def write_model(path, cfg: Config, tensors: Dict[str, np.ndarray]) -> None:
+def write_model(path, cfg: Config, tensors) -> None:
+    """tensors: a dict name -> array, or a callable name -> array (called once per
+    tensor, in index order, so that large models never sit in memory whole)."""
+    get = tensors if callable(tensors) else tensors.__getitem__
     names = list(tensor_shapes(cfg))
+    shapes = tensor_shapes(cfg)
     dtype = 1 if cfg.kind == AUDIO else 2
     esize = 4 if dtype == 1 else 2
     head = b"OMNIVQ01" + struct.pack("<II", 1, cfg.kind)
     head += struct.pack("<12I", *[getattr(cfg, f) for f in _FIELDS])
     head += struct.pack("<I", len(names))
-    index_len = sum(4 * 4 + 8 * 2 + 8 * len(tensors[n].shape) + len(n.encode()) for n in names)
+    index_len = sum(4 * 4 + 8 * 2 + 8 * len(shapes[n]) + len(n.encode()) for n in names)
     offset = (len(head) + index_len + 63) // 64 * 64
-    records, blobs = [], []
+    records, offsets = [], []
     for n in names:
-        a = np.ascontiguousarray(tensors[n], np.float32)
-        assert a.shape == tensor_shapes(cfg)[n], n
-        raw = a.tobytes() if dtype == 1 else _bf16_bits(a).tobytes()
+        size = int(np.prod(shapes[n]))
         nb = n.encode()
-        records.append(struct.pack("<IIIIQQ", len(nb), dtype, a.ndim, 0, offset, a.size * esize)
-                       + struct.pack(f"<{a.ndim}Q", *a.shape) + nb)
-        blobs.append((offset, raw))
-        offset = (offset + len(raw) + 63) // 64 * 64
+        records.append(struct.pack("<IIIIQQ", len(nb), dtype, len(shapes[n]), 0, offset, size * esize)
+                       + struct.pack(f"<{len(shapes[n])}Q", *shapes[n]) + nb)
+        offsets.append(offset)
+        offset = (offset + size * esize + 63) // 64 * 64
     with open(path, "wb") as f:
         f.write(head)
         f.write(b"".join(records))
-        for off, raw in blobs:
+        for n, off in zip(names, offsets):
+            a = np.ascontiguousarray(get(n), np.float32)
+            assert a.shape == shapes[n], n
             f.seek(off)
-            f.write(raw)
+            f.write(a.tobytes() if dtype == 1 else _bf16_bits(a).tobytes())
 
 
-def write_random_model(path, cfg: Config, seed: int = 0) -> Dict[str, np.ndarray]:
-    t = random_tensors(cfg, seed)
-    write_model(path, cfg, t)
-    return t
+def write_random_model(path, cfg: Config, seed: int = 0) -> None:
+    """Same weights as random_tensors(cfg, seed), generated and written one tensor
+    at a time."""
+    rng = np.random.default_rng(seed)
+    shapes = tensor_shapes(cfg)
+    write_model(path, cfg, lambda name: _random_tensor(rng, name, shapes[name]))
