@@ -87,6 +87,25 @@ OMNI_ABI_API int omni_context_copy_features(omni_context *context, float *output
 /* Peak device workspace of the context (activations and scratch; not weights). */
 OMNI_ABI_API uint64_t omni_context_peak_workspace(const omni_context *context);
 
+/* Batched extension of this library (not part of the reference's omni.h):
+ * `items` inputs of one shape per call, stacked into large GEMMs and one
+ * attention launch per layer; results equal the per-item calls'.  Inputs may be
+ * host or device memory (device memory of the model's device is read in
+ * place).  Codes are each item's codes concatenated in item order (*count =
+ * their total); omni_context_copy_features then returns all items' features
+ * stacked the same way.  Non-finite input fails with OMNI_INVALID_ARGUMENT.
+ *
+ * mel: [items, mel_channels, frames] fp32; valid_frames[items], each in
+ * (0, frames]; item i has ceil(valid_frames[i] / 8) codes. */
+OMNI_ABI_API int omni_b200_encode_audio_batch(omni_context *context, const float *mel, uint32_t items,
+                                              uint32_t frames, const uint32_t *valid_frames,
+                                              uint16_t *codes, size_t capacity, size_t *count);
+/* pixels: [items, 3, height, width] fp32; (height / patch) * (width / patch)
+ * codes per image. */
+OMNI_ABI_API int omni_b200_encode_images(omni_context *context, const float *pixels, uint32_t items,
+                                         uint32_t height, uint32_t width, uint16_t *codes,
+                                         size_t capacity, size_t *count);
+
 #ifdef __cplusplus
 }
 #endif

@@ -50,6 +50,15 @@ _SIGS = {
     "omni_context_peak_workspace": (C.c_uint64, [C.c_void_p]),
 }
 SYMBOLS = tuple(_SIGS)
+# Batched extension of libomni_b200.so (absent from the reference's library).
+_EXT_SIGS = {
+    "omni_b200_encode_audio_batch": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32,
+                                               C.POINTER(C.c_uint32), C.POINTER(C.c_uint16), C.c_size_t,
+                                               C.POINTER(C.c_size_t)]),
+    "omni_b200_encode_images": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32,
+                                          C.POINTER(C.c_uint16), C.c_size_t, C.POINTER(C.c_size_t)]),
+}
+EXTENSION_SYMBOLS = tuple(_EXT_SIGS)
 
 
 class OmniLib:
@@ -59,6 +68,11 @@ class OmniLib:
         for name, (res, args) in _SIGS.items():
             fn = getattr(self.lib, name)
             fn.restype, fn.argtypes = res, args
+        self.batched = all(hasattr(self.lib, n) for n in _EXT_SIGS)
+        if self.batched:
+            for name, (res, args) in _EXT_SIGS.items():
+                fn = getattr(self.lib, name)
+                fn.restype, fn.argtypes = res, args
 
     def check(self, status):
         if status:
@@ -123,6 +137,39 @@ class Session:
             self.handle, pixels.ctypes.data_as(C.POINTER(C.c_float)), h, w,
             codes.ctypes.data_as(C.POINTER(C.c_uint16)), codes.size, C.byref(count)))
         return codes
+
+    def encode_audio_batch(self, mel, valid_frames, device_ptr=None):
+        """mel [items, mel, frames] fp32 (or device_ptr to the same layout on the
+        model's device); returns the concatenated codes."""
+        items, _, frames = mel.shape if device_ptr is None else mel
+        valid = np.ascontiguousarray(valid_frames, np.uint32)
+        codes = np.zeros(int(((valid.astype(np.int64) + 7) // 8).sum()), np.uint16)
+        if device_ptr is None:
+            mel = np.ascontiguousarray(mel, np.float32)
+            ptr = mel.ctypes.data
+        else:
+            ptr = device_ptr
+        count = C.c_size_t()
+        self.lib.check(self.lib.lib.omni_b200_encode_audio_batch(
+            self.handle, C.c_void_p(ptr), items, frames, valid.ctypes.data_as(C.POINTER(C.c_uint32)),
+            codes.ctypes.data_as(C.POINTER(C.c_uint16)), codes.size, C.byref(count)))
+        return codes[: count.value]
+
+    def encode_images(self, pixels, patch, device_ptr=None):
+        """pixels [items, 3, h, w] fp32 (or, with device_ptr, its shape tuple and
+        the device address); returns the codes, image after image."""
+        items, _, h, w = pixels.shape if device_ptr is None else pixels
+        codes = np.zeros(items * (h // patch) * (w // patch), np.uint16)
+        if device_ptr is None:
+            pixels = np.ascontiguousarray(pixels, np.float32)
+            ptr = pixels.ctypes.data
+        else:
+            ptr = device_ptr
+        count = C.c_size_t()
+        self.lib.check(self.lib.lib.omni_b200_encode_images(
+            self.handle, C.c_void_p(ptr), items, h, w, codes.ctypes.data_as(C.POINTER(C.c_uint16)), codes.size,
+            C.byref(count)))
+        return codes[: count.value]
 
     def features(self, rows_hint=0):
         count = C.c_size_t()

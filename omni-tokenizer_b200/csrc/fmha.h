@@ -53,6 +53,16 @@ struct FmhaArgs {
 // Returns 0 on success, a CUDA error code, or a negative/1000+ code for an
 // unsupported shape / tensor-map failure.
 int fmha_launch(const FmhaArgs &args, cudaStream_t stream);
+
+// Attention on row-major [batch*n, heads*hd] (fused: [batch*n, 3*heads*hd])
+// rows: `batch` sequences of n tokens, keys of sequence b limited to
+// lengths[b] (device int32, or nullptr: `valid` for all) and to the block
+// window.  Same codes and error text as omni_b200_attention_rows.
+size_t attention_rows_workspace(size_t rows, int heads, int head_dim, int dtype, int fused);
+int attention_rows(const void *q, const void *k, const void *v, void *out, size_t n, int batch,
+                   int heads, int head_dim, size_t block, size_t valid, const int *lengths,
+                   int fused, int dtype, int out_dtype, void *workspace, size_t workspace_bytes,
+                   cudaStream_t stream);
 bool tma_view_ok(const void *base, const TensorView &v);
 int padded_head_dim(int hd);
 

@@ -106,13 +106,48 @@ __global__ void k_bias(void *x, const void *b, bool bf16, size_t rows, size_t co
     GRID_STRIDE(i, rows * cols) { st(x, i, __fadd_rn(ld(x, i, bf16), ld(b, i % cols, bf16)), bf16); }
 }
 
-__global__ void k_conv_gather(const void *x, void *y, bool bf16, size_t rows, size_t cols,
-                              size_t stride, size_t out_rows) {
-    GRID_STRIDE(i, out_rows * cols * 3) {
-        const size_t t = i / (cols * 3), rem = i % (cols * 3), c = rem / 3, k = rem % 3;
+// Segments of `rows` input rows each; every segment has its own left padding.
+__global__ void k_conv_gather(const void *x, void *y, bool bf16, size_t segments, size_t rows,
+                              size_t cols, size_t stride, size_t out_rows) {
+    GRID_STRIDE(i, segments * out_rows * cols * 3) {
+        const size_t seg = i / (out_rows * cols * 3), ti = i % (out_rows * cols * 3);
+        const size_t t = ti / (cols * 3), rem = ti % (cols * 3), c = rem / 3, k = rem % 3;
         const long long s = static_cast<long long>(t * stride + k) - 2;
-        const float v = s >= 0 && s < static_cast<long long>(rows) ? ld(x, s * cols + c, bf16) : 0.f;
+        const float v = s >= 0 && s < static_cast<long long>(rows)
+                            ? ld(x, (seg * rows + static_cast<size_t>(s)) * cols + c, bf16)
+                            : 0.f;
         st(y, i, v, bf16);
+    }
+}
+
+__global__ void k_add_periodic(void *x, const void *y, bool bf16, size_t n, size_t period) {
+    GRID_STRIDE(i, n) { st(x, i, __fadd_rn(ld(x, i, bf16), ld(y, i % period, bf16)), bf16); }
+}
+
+__global__ void k_finite(const float *x, size_t n, int *flag) {
+    bool bad = false;
+    GRID_STRIDE(i, n) { bad |= !isfinite(x[i]); }
+    if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0)
+        atomicOr(flag, 1);
+}
+
+// [count, channels, frames] -> [count * frames, channels], 32x32 tiles through shared memory.
+__global__ void k_frames_major(const float *x, float *y, size_t channels, size_t frames) {
+    __shared__ float tile[32][33];
+    const size_t item = blockIdx.z;
+    const size_t t0 = static_cast<size_t>(blockIdx.x) * 32, c0 = static_cast<size_t>(blockIdx.y) * 32;
+    const float *src = x + item * channels * frames;
+    float *dst = y + item * channels * frames;
+    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+        const size_t c = c0 + r, t = t0 + threadIdx.x;
+        if (c < channels && t < frames)
+            tile[r][threadIdx.x] = src[c * frames + t];
+    }
+    __syncthreads();
+    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+        const size_t t = t0 + r, c = c0 + threadIdx.x;
+        if (c < channels && t < frames)
+            dst[t * channels + c] = tile[threadIdx.x][r];
     }
 }
 
@@ -162,15 +197,16 @@ __global__ void k_normalize(const void *x, void *y, bool bf16, size_t rows, size
     }
 }
 
-__global__ void k_image_patches(const float *px, __nv_bfloat16 *y, size_t height, size_t width,
-                                size_t patch) {
-    const size_t gw = width / patch, pd = 8 * patch * patch, n = (height / patch) * gw * pd;
-    GRID_STRIDE(i, n) {
-        const size_t cell = i / pd, rem = i % pd, pix = rem / 8, ch = rem % 8;
+__global__ void k_image_patches(const float *px, __nv_bfloat16 *y, size_t count, size_t height,
+                                size_t width, size_t patch) {
+    const size_t gw = width / patch, pd = 8 * patch * patch, cells = (height / patch) * gw;
+    GRID_STRIDE(i, count * cells * pd) {
+        const size_t item = i / (cells * pd), cell = (i / pd) % cells, rem = i % pd, pix = rem / 8,
+                     ch = rem % 8;
         float v = 0.f;
         if (ch < 3) {
             const size_t gy = cell / gw, gx = cell % gw, dy = pix / patch, dx = pix % patch;
-            v = px[ch * height * width + (gy * patch + dy) * width + gx * patch + dx];
+            v = px[(item * 3 + ch) * height * width + (gy * patch + dy) * width + gx * patch + dx];
         }
         y[i] = __float2bfloat16_rn(v);
     }
@@ -253,11 +289,28 @@ int bias(void *x, const void *b, bool bf16, size_t rows, size_t cols, cudaStream
     k_bias<<<blocks_for(rows * cols, 256), 256, 0, s>>>(x, b, bf16, rows, cols);
     return status();
 }
-int conv_gather(const void *x, void *y, bool bf16, size_t rows, size_t cols, size_t stride,
-                cudaStream_t s) {
+int conv_gather(const void *x, void *y, bool bf16, size_t segments, size_t rows, size_t cols,
+                size_t stride, cudaStream_t s) {
     const size_t out_rows = (rows + stride - 1) / stride;
-    k_conv_gather<<<blocks_for(out_rows * cols * 3, 256), 256, 0, s>>>(x, y, bf16, rows, cols, stride,
-                                                                        out_rows);
+    k_conv_gather<<<blocks_for(segments * out_rows * cols * 3, 256), 256, 0, s>>>(x, y, bf16, segments, rows,
+                                                                                   cols, stride, out_rows);
+    return status();
+}
+int add_periodic(void *x, const void *y, bool bf16, size_t n, size_t period, cudaStream_t s) {
+    k_add_periodic<<<blocks_for(n, 256), 256, 0, s>>>(x, y, bf16, n, period);
+    return status();
+}
+int finite_check(const float *x, size_t n, int *flag, cudaStream_t s) {
+    if (n)
+        k_finite<<<blocks_for(n, 256), 256, 0, s>>>(x, n, flag);
+    return status();
+}
+int frames_major(const float *x, float *y, size_t count, size_t channels, size_t frames, cudaStream_t s) {
+    if (count && channels && frames) {
+        const dim3 grid(static_cast<unsigned>((frames + 31) / 32), static_cast<unsigned>((channels + 31) / 32),
+                        static_cast<unsigned>(count));
+        k_frames_major<<<grid, dim3(32, 8), 0, s>>>(x, y, channels, frames);
+    }
     return status();
 }
 int pool(const void *x, void *y, bool bf16, size_t rows, size_t cols, size_t factor,
@@ -276,10 +329,10 @@ int normalize(const void *x, void *y, bool bf16, size_t rows, size_t cols, cudaS
     k_normalize<<<blocks_for(rows, 128), 128, 0, s>>>(x, y, bf16, rows, cols);
     return status();
 }
-int image_patches(const float *pixels, void *y, size_t height, size_t width, size_t patch,
+int image_patches(const float *pixels, void *y, size_t count, size_t height, size_t width, size_t patch,
                   cudaStream_t s) {
-    const size_t n = (height / patch) * (width / patch) * 8 * patch * patch;
-    k_image_patches<<<blocks_for(n, 256), 256, 0, s>>>(pixels, static_cast<__nv_bfloat16 *>(y), height,
+    const size_t n = count * (height / patch) * (width / patch) * 8 * patch * patch;
+    k_image_patches<<<blocks_for(n, 256), 256, 0, s>>>(pixels, static_cast<__nv_bfloat16 *>(y), count, height,
                                                         width, patch);
     return status();
 }
@@ -297,11 +350,8 @@ int attention_f32(const float *q, const float *k, const float *v, float *y, size
     const size_t smem = static_cast<size_t>(kWarps) * n * sizeof(float);
     if (smem > 200 * 1024)
         return -2; // sequences longer than 12800 keys are not supported here
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(k_attention_f32, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        attr = true;
-    }
+    // Per device: the attribute belongs to the current device's copy of the kernel.
+    cudaFuncSetAttribute(k_attention_f32, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     const size_t tasks = n * heads;
     k_attention_f32<<<static_cast<unsigned>((tasks + kWarps - 1) / kWarps), kWarps * 32, smem, s>>>(
         q, k, v, y, n, heads, hd, block, valid);

@@ -25,9 +25,16 @@ int gelu(void *x, bool bf16, size_t n, cudaStream_t s);
 int add(void *x, const void *y, bool bf16, size_t n, cudaStream_t s);
 // In place: x[r, c] = r(x[r, c] + b[c]).
 int bias(void *x, const void *b, bool bf16, size_t rows, size_t cols, cudaStream_t s);
-// Kernel-3 causal conv input (left pad 2): y[t, 3c + k] = x[t*stride + k - 2, c].
-int conv_gather(const void *x, void *y, bool bf16, size_t rows, size_t cols, size_t stride,
-                cudaStream_t s);
+// Kernel-3 causal conv input (left pad 2): y[t, 3c + k] = x[t*stride + k - 2, c],
+// for `segments` stacked inputs of `rows` rows each (each padded on its own).
+int conv_gather(const void *x, void *y, bool bf16, size_t segments, size_t rows, size_t cols,
+                size_t stride, cudaStream_t s);
+// In place: x[i] = r(x[i] + y[i mod period]) (positions added to stacked items).
+int add_periodic(void *x, const void *y, bool bf16, size_t n, size_t period, cudaStream_t s);
+// *flag |= 1 when any of x[0..n) is NaN or infinite.
+int finite_check(const float *x, size_t n, int *flag, cudaStream_t s);
+// [count, channels, frames] -> [count * frames, channels] (log-mel to frame rows).
+int frames_major(const float *x, float *y, size_t count, size_t channels, size_t frames, cudaStream_t s);
 // Mean of `factor` consecutive rows (the last group may be short; divisor stays factor).
 int pool(const void *x, void *y, bool bf16, size_t rows, size_t cols, size_t factor,
          cudaStream_t s);
@@ -36,8 +43,9 @@ int interpolate(const void *x, void *y, bool bf16, size_t source, size_t height,
                 size_t cols, cudaStream_t s);
 // Row-wise L2 normalisation with the reference's max(r(sqrt(n)), r(1e-12)) guard.
 int normalize(const void *x, void *y, bool bf16, size_t rows, size_t cols, cudaStream_t s);
-// CHW fp32 pixels -> bf16 patches [gh*gw, 8*p*p] (channel-padded to 8 per pixel).
-int image_patches(const float *pixels, void *y, size_t height, size_t width, size_t patch,
+// `count` CHW fp32 images -> bf16 patches [count*gh*gw, 8*p*p] (channel-padded to 8
+// per pixel).
+int image_patches(const float *pixels, void *y, size_t count, size_t height, size_t width, size_t patch,
                   cudaStream_t s);
 // fp32 -> bf16 (round to nearest even, NaN quieted) or a copy for fp32.
 int convert(const float *x, void *y, bool bf16, size_t n, cudaStream_t s);

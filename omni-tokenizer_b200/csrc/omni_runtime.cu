@@ -13,6 +13,7 @@
 // graph_kernels.cu.  Audio-profile attention runs in fp32 on the CUDA cores
 // (the reference's audio kernels are fp32-accurate 3xTF32); setting
 // OMNI_B200_AUDIO_BF16=1 routes it through the tcgen05 kernel instead.
+#include "fmha.h"
 #include "graph_kernels.h"
 #include "omni_abi.h"
 #include "omni_b200.h"
@@ -347,6 +348,10 @@ struct Context {
     omni_trace_callback trace = nullptr;
     void *trace_user = nullptr;
     bool audio_bf16 = false;
+    // Host inputs are copied on `copy` into two staging buffers (events
+    // ready[i] / done[i]), overlapping the graph of the previous chunk.
+    cudaStream_t copy = nullptr;
+    cudaEvent_t ready[2] = {}, done[2] = {}, start = nullptr;
 
     ~Context() {
         features = {};
@@ -354,8 +359,15 @@ struct Context {
             cudaSetDevice(model ? model->device : 0);
             cudaStreamSynchronize(stream);
         }
+        if (copy)
+            cudaStreamSynchronize(copy);
+        for (cudaEvent_t e : {ready[0], ready[1], done[0], done[1], start})
+            if (e)
+                cudaEventDestroy(e);
         if (blas)
             cublasDestroy(blas);
+        if (copy)
+            cudaStreamDestroy(copy);
         if (stream)
             cudaStreamDestroy(stream);
     }
@@ -437,28 +449,35 @@ void gelu_in_place(Context &c, Tensor &x) {
     cuda_ok(static_cast<cudaError_t>(graph::gelu(x.data(), x.bf16, x.size(), c.stream)), "gelu");
 }
 
-// Ops::attention on [n, heads*hd] (fused: [n, 3*heads*hd]) rows.
+// Ops::attention on `batch` stacked sequences of [n, heads*hd] rows (fused:
+// [n, 3*heads*hd]); keys of sequence b limited to valid[b] (valid_dev: the
+// same counts as device int32, or null when every count is n).
 Tensor attention(Context &c, const Tensor &q, const Tensor *k, const Tensor *v, size_t heads,
-                 size_t block, size_t valid, bool fused) {
-    const size_t n = q.rows, d = fused ? q.cols / 3 : q.cols, hd = d / heads;
-    Tensor y = c.make(n, d, q.bf16);
+                 size_t block, bool fused, size_t batch, const std::vector<int> &valid,
+                 const int *valid_dev) {
+    const size_t rows = q.rows, n = rows / batch, d = fused ? q.cols / 3 : q.cols, hd = d / heads;
+    Tensor y = c.make(rows, d, q.bf16);
     if (!q.bf16 && !c.audio_bf16) {
         require(!fused, "fp32 fused attention is not used by the graphs", OMNI_INTERNAL_ERROR);
-        cuda_ok(static_cast<cudaError_t>(graph::attention_f32(
-                    static_cast<const float *>(q.data()), static_cast<const float *>(k->data()),
-                    static_cast<const float *>(v->data()), static_cast<float *>(y.data()), n, heads,
-                    hd, block, valid, c.stream)),
-                "attention");
+        for (size_t b = 0; b < batch; ++b) {
+            const size_t off = b * n * d;
+            cuda_ok(static_cast<cudaError_t>(graph::attention_f32(
+                        static_cast<const float *>(q.data()) + off, static_cast<const float *>(k->data()) + off,
+                        static_cast<const float *>(v->data()) + off, static_cast<float *>(y.data()) + off, n,
+                        heads, hd, block, static_cast<size_t>(valid[b]), c.stream)),
+                    "attention");
+        }
         return y;
     }
     const int dt = q.bf16 ? OMNI_B200_BF16 : OMNI_B200_F32;
-    const size_t ws_bytes = omni_b200_attention_rows_workspace(n, static_cast<int>(heads),
-                                                               static_cast<int>(hd), dt, fused ? 1 : 0);
+    const size_t ws_bytes = attention_rows_workspace(rows, static_cast<int>(heads), static_cast<int>(hd), dt,
+                                                     fused ? 1 : 0);
     Tensor ws_holder;
     void *ws = ws_bytes ? c.scratch(ws_bytes, ws_holder) : nullptr;
-    op_ok(omni_b200_attention_rows(q.data(), fused ? nullptr : k->data(), fused ? nullptr : v->data(),
-                                   y.data(), n, static_cast<int>(heads), static_cast<int>(hd), block,
-                                   valid, fused ? 1 : 0, dt, dt, ws, ws_bytes, c.stream),
+    op_ok(attention_rows(q.data(), fused ? nullptr : k->data(), fused ? nullptr : v->data(), y.data(), n,
+                         static_cast<int>(batch), static_cast<int>(heads), static_cast<int>(hd), block,
+                         valid_dev ? 0 : static_cast<size_t>(valid[0]), valid_dev, fused ? 1 : 0, dt, dt, ws,
+                         ws_bytes, c.stream),
           "attention");
     return y;
 }
@@ -505,146 +524,259 @@ void trace(Context &c, const Tensor &x, const std::string &stage) {
     }
 }
 
-void finite_input(const float *p, size_t n) {
-    for (size_t i = 0; i < n; ++i)
-        require(std::isfinite(p[i]), "Input contains a non-finite value");
+// True when `p` is device (or managed) memory; such inputs are read in place.
+bool device_input(const void *p, int device) {
+    cudaPointerAttributes at{};
+    if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    if (at.type == cudaMemoryTypeManaged)
+        return true;
+    if (at.type == cudaMemoryTypeDevice) {
+        require(at.device == device, "Input is in another device's memory");
+        return true;
+    }
+    return false;
 }
 
-Tensor upload(Context &c, const float *host, size_t rows, size_t cols, bool bf16) {
-    Tensor staged = c.make(rows, cols, false);
-    cuda_ok(cudaMemcpyAsync(staged.data(), host, rows * cols * 4, cudaMemcpyHostToDevice, c.stream),
-            "upload");
-    if (!bf16)
-        return staged;
-    Tensor t = c.make(rows, cols, true);
-    cuda_ok(static_cast<cudaError_t>(graph::convert(static_cast<const float *>(staged.data()), t.data(),
-                                                    true, rows * cols, c.stream)),
-            "upload");
-    return t;
+// Activation rows one chunk of a batched call holds at most.
+constexpr size_t kChunkRows = 98304;
+
+// Runs body(first_item, items, device_input) over chunks of `chunk` items.
+// Host input goes through two device staging buffers: the copy of chunk i+1
+// (on c.copy) overlaps the graph of chunk i (on c.stream).
+template <class Body>
+void for_chunks(Context &c, const float *input, size_t count, size_t item_floats, size_t chunk,
+                Body body) {
+    const bool on_device = device_input(input, c.model->device);
+    const size_t chunks = (count + chunk - 1) / chunk;
+    Tensor stage[2];
+    auto upload = [&](size_t ci) {
+        const int slot = static_cast<int>(ci & 1);
+        const size_t i0 = ci * chunk, items = std::min(chunk, count - i0);
+        if (ci >= 2)
+            cuda_ok(cudaStreamWaitEvent(c.copy, c.done[slot], 0), "copy order");
+        cuda_ok(cudaMemcpyAsync(stage[slot].data(), input + i0 * item_floats, items * item_floats * 4,
+                                cudaMemcpyHostToDevice, c.copy),
+                "upload");
+        cuda_ok(cudaEventRecord(c.ready[slot], c.copy), "copy order");
+    };
+    if (!on_device) {
+        for (int i = 0; i < (chunks > 1 ? 2 : 1); ++i)
+            stage[i] = c.make(chunk * item_floats, 1, false);
+        cuda_ok(cudaEventRecord(c.start, c.stream), "copy order"); // the staging allocations
+        cuda_ok(cudaStreamWaitEvent(c.copy, c.start, 0), "copy order");
+        upload(0);
+    }
+    for (size_t ci = 0; ci < chunks; ++ci) {
+        c.check();
+        const int slot = static_cast<int>(ci & 1);
+        const size_t i0 = ci * chunk, items = std::min(chunk, count - i0);
+        const float *src = input + i0 * item_floats;
+        if (!on_device) {
+            cuda_ok(cudaStreamWaitEvent(c.stream, c.ready[slot], 0), "copy order");
+            src = static_cast<const float *>(stage[slot].data());
+        }
+        body(i0, items, src);
+        if (!on_device) {
+            cuda_ok(cudaEventRecord(c.done[slot], c.stream), "copy order");
+            if (ci + 1 < chunks)
+                upload(ci + 1);
+        }
+    }
+}
+
+size_t chunk_items(size_t count, size_t rows_per_item) {
+    const size_t per = std::max<size_t>(1, kChunkRows / std::max<size_t>(rows_per_item, 1));
+    const size_t chunks = (count + per - 1) / per;
+    return (count + chunks - 1) / chunks;
+}
+
+// Reads the non-finite flag the graph raised (after the stream has drained).
+void finite_or_fail(Context &c, const Tensor &flag) {
+    int v = 0;
+    cuda_ok(cudaMemcpyAsync(&v, flag.data(), sizeof v, cudaMemcpyDeviceToHost, c.stream), "input check");
+    cuda_ok(cudaStreamSynchronize(c.stream), "input check");
+    require(v == 0, "Input contains a non-finite value");
 }
 } // namespace
 
-// Audio graph (src/runtime.cpp:30-75): causal conv stem, pre-norm encoder
-// layers with block-causal attention, mean-pool by 4, fp32 VQ.
-std::vector<uint16_t> encode_audio(Context &c, const float *mel, uint32_t frames, uint32_t valid) {
+// Audio graph (src/runtime.cpp:30-75) over `count` log-mel segments
+// [count, mel, frames] (host or device memory) with valid[i] frames each:
+// causal conv stem, pre-norm encoder layers with block-causal attention,
+// mean-pool by 4, fp32 VQ.  Segments stack as rows; each keeps its own conv
+// padding, positions and key limit.  Codes of segment i are its first
+// ceil(valid[i] / 8), concatenated in segment order.
+std::vector<uint16_t> encode_audio_batch(Context &c, const float *mel, size_t count, uint32_t frames,
+                                         const uint32_t *valid) {
     const Model &m = *c.model;
     const Config &cfg = m.cfg;
     c.check();
-    finite_input(mel, size_t(frames) * cfg.input_channels);
-    std::vector<float> tr(size_t(frames) * cfg.input_channels);
-    for (size_t t = 0; t < frames; ++t)
-        for (size_t j = 0; j < cfg.input_channels; ++j)
-            tr[t * cfg.input_channels + j] = mel[j * size_t(frames) + t];
-    Tensor x = upload(c, tr.data(), frames, cfg.input_channels, false);
-    auto conv = [&](const Tensor &in, size_t stride, const char *name) {
-        Tensor g = c.make((in.rows + stride - 1) / stride, in.cols * 3, in.bf16);
-        cuda_ok(static_cast<cudaError_t>(graph::conv_gather(in.data(), g.data(), in.bf16, in.rows, in.cols,
-                                                            stride, c.stream)),
-                "conv gather");
-        Tensor y = linear(c, g, m.get(std::string(name) + ".weight"), m.opt(std::string(name) + ".bias"));
-        gelu_in_place(c, y);
-        return y;
-    };
-    x = conv(x, 1, "conv1");
-    x = conv(x, 2, "conv2");
-    add_in_place(c, x, m.get("embed_positions.weight"));
-    trace(c, x, "embedding");
-    for (uint32_t i = 0; i < cfg.layers; ++i) {
-        c.check();
-        const std::string p = "layers." + std::to_string(i) + ".";
-        Tensor z = layer_norm(c, x, m.get(p + "self_attn_layer_norm.weight"),
-                              m.get(p + "self_attn_layer_norm.bias"), 1e-5f);
-        auto proj = [&](const Tensor &in, const std::string &name) {
-            return linear(c, in, m.get(name + ".weight"), m.opt(name + ".bias"));
+    const size_t C = cfg.input_channels, T = frames, L = (T + 1) / 2, W = cfg.width;
+    std::vector<size_t> offset(count + 1, 0);
+    for (size_t i = 0; i < count; ++i)
+        offset[i + 1] = offset[i] + (valid[i] + 7) / 8;
+    Tensor flag = c.make(1, 1, false);
+    cuda_ok(cudaMemsetAsync(flag.data(), 0, 4, c.stream), "input check");
+    Tensor features = c.make(offset[count], W, false);
+    std::vector<int> keys(count);
+    for (size_t i = 0; i < count; ++i)
+        keys[i] = static_cast<int>((valid[i] + 1) / 2);
+    const size_t chunk = chunk_items(count, T);
+    for_chunks(c, mel, count, C * T, chunk, [&](size_t i0, size_t items, const float *src) {
+        cuda_ok(static_cast<cudaError_t>(graph::finite_check(src, items * C * T, static_cast<int *>(flag.data()),
+                                                             c.stream)),
+                "input check");
+        Tensor x = c.make(items * T, C, false);
+        cuda_ok(static_cast<cudaError_t>(graph::frames_major(src, static_cast<float *>(x.data()), items, C, T,
+                                                             c.stream)),
+                "frames");
+        auto conv = [&](const Tensor &in, size_t rows, size_t stride, const char *name) {
+            const size_t out_rows = (rows + stride - 1) / stride;
+            Tensor g = c.make(items * out_rows, in.cols * 3, in.bf16);
+            cuda_ok(static_cast<cudaError_t>(graph::conv_gather(in.data(), g.data(), in.bf16, items, rows,
+                                                                in.cols, stride, c.stream)),
+                    "conv gather");
+            Tensor y = linear(c, g, m.get(std::string(name) + ".weight"), m.opt(std::string(name) + ".bias"));
+            gelu_in_place(c, y);
+            return y;
         };
-        Tensor q = proj(z, p + "self_attn.q_proj"), k = proj(z, p + "self_attn.k_proj"),
-               v = proj(z, p + "self_attn.v_proj");
-        z = attention(c, q, &k, &v, cfg.heads, cfg.block_size, (valid + 1) / 2, false);
-        z = proj(z, p + "self_attn.out_proj");
-        add_in_place(c, x, z);
-        z = layer_norm(c, x, m.get(p + "final_layer_norm.weight"), m.get(p + "final_layer_norm.bias"), 1e-5f);
-        z = proj(z, p + "fc1");
-        gelu_in_place(c, z);
-        z = proj(z, p + "fc2");
-        add_in_place(c, x, z);
-        trace(c, x, "layer." + std::to_string(i));
-    }
-    c.check();
-    Tensor pooled = c.make((x.rows + cfg.pool_size - 1) / cfg.pool_size, x.cols, x.bf16);
-    cuda_ok(static_cast<cudaError_t>(graph::pool(x.data(), pooled.data(), x.bf16, x.rows, x.cols,
-                                                 cfg.pool_size, c.stream)),
-            "pool");
-    pooled.rows = (valid + 7) / 8;
-    c.features = pooled;
-    return quantize(c, c.features, m.get("codebook.weight"), m.cbnorm);
+        x = conv(x, T, 1, "conv1");
+        x = conv(x, T, 2, "conv2");
+        const Tensor &pos = m.get("embed_positions.weight");
+        cuda_ok(static_cast<cudaError_t>(graph::add_periodic(x.data(), pos.data(), x.bf16, x.size(), L * W,
+                                                             c.stream)),
+                "positions");
+        trace(c, x, "embedding");
+        const std::vector<int> chunk_keys(keys.begin() + i0, keys.begin() + i0 + items);
+        Tensor keys_dev = c.make(items, 1, false);
+        cuda_ok(cudaMemcpyAsync(keys_dev.data(), chunk_keys.data(), items * 4, cudaMemcpyHostToDevice, c.stream),
+                "key counts");
+        for (uint32_t i = 0; i < cfg.layers; ++i) {
+            c.check();
+            const std::string p = "layers." + std::to_string(i) + ".";
+            Tensor z = layer_norm(c, x, m.get(p + "self_attn_layer_norm.weight"),
+                                  m.get(p + "self_attn_layer_norm.bias"), 1e-5f);
+            auto proj = [&](const Tensor &in, const std::string &name) {
+                return linear(c, in, m.get(name + ".weight"), m.opt(name + ".bias"));
+            };
+            Tensor q = proj(z, p + "self_attn.q_proj"), k = proj(z, p + "self_attn.k_proj"),
+                   v = proj(z, p + "self_attn.v_proj");
+            z = attention(c, q, &k, &v, cfg.heads, cfg.block_size, false, items, chunk_keys,
+                          static_cast<const int *>(keys_dev.data()));
+            z = proj(z, p + "self_attn.out_proj");
+            add_in_place(c, x, z);
+            z = layer_norm(c, x, m.get(p + "final_layer_norm.weight"), m.get(p + "final_layer_norm.bias"), 1e-5f);
+            z = proj(z, p + "fc1");
+            gelu_in_place(c, z);
+            z = proj(z, p + "fc2");
+            add_in_place(c, x, z);
+            trace(c, x, "layer." + std::to_string(i));
+        }
+        c.check();
+        const size_t pooled_rows = (L + cfg.pool_size - 1) / cfg.pool_size;
+        Tensor pooled = c.make(items * pooled_rows, W, x.bf16);
+        cuda_ok(static_cast<cudaError_t>(graph::pool(x.data(), pooled.data(), x.bf16, x.rows, W, cfg.pool_size,
+                                                     c.stream)),
+                "pool");
+        // pool over the stacked rows equals pool per segment: L is a multiple of
+        // the pool size (frames % 8 == 0), so no group straddles two segments.
+        for (size_t b = 0; b < items; ++b) {
+            const size_t rows = offset[i0 + b + 1] - offset[i0 + b];
+            cuda_ok(cudaMemcpyAsync(static_cast<float *>(features.data()) + offset[i0 + b] * W,
+                                    static_cast<const float *>(pooled.data()) + b * pooled_rows * W,
+                                    rows * W * 4, cudaMemcpyDeviceToDevice, c.stream),
+                    "features");
+        }
+    });
+    auto ids = quantize(c, features, m.get("codebook.weight"), m.cbnorm);
+    finite_or_fail(c, flag);
+    c.features = features;
+    return ids;
 }
 
-// Image graph (src/runtime.cpp:76-130): patch embedding, interpolated
-// positions, pre-norm blocks with fused-QKV attention, 1x1 projection, L2
-// normalisation, bf16 VQ.
-std::vector<uint16_t> encode_image(Context &c, const float *pixels, uint32_t height, uint32_t width) {
+// Image graph (src/runtime.cpp:76-130) over `count` CHW images of one size
+// (host or device memory): patch embedding, interpolated positions, pre-norm
+// blocks with fused-QKV attention, 1x1 projection, L2 normalisation, bf16 VQ.
+// Images stack as rows; attention runs per image.  Codes in image order.
+std::vector<uint16_t> encode_images(Context &c, const float *pixels, size_t count, uint32_t height,
+                                    uint32_t width) {
     const Model &m = *c.model;
     const Config &cfg = m.cfg;
     c.check();
-    finite_input(pixels, size_t(height) * width * 3);
     const size_t P = cfg.patch_size, gh = height / P, gw = width / P, n = gh * gw;
-    Tensor px = upload(c, pixels, 3, size_t(height) * width, false);
-    Tensor patches = c.make(n, 8 * P * P, true);
-    cuda_ok(static_cast<cudaError_t>(graph::image_patches(static_cast<const float *>(px.data()),
-                                                          patches.data(), height, width, P, c.stream)),
-            "patches");
-    px = {};
-    Tensor x = linear(c, patches, m.get("patch_embed.proj.weight"), &m.get("patch_embed.proj.bias"), true);
-    patches = {};
-    trace(c, x, "patch");
+    const size_t item_floats = size_t(3) * height * width;
+    Tensor flag = c.make(1, 1, false);
+    cuda_ok(cudaMemsetAsync(flag.data(), 0, 4, c.stream), "input check");
     Tensor pos = c.make(n, cfg.width, true);
     cuda_ok(static_cast<cudaError_t>(graph::interpolate(m.get("pos_embed").data(), pos.data(), true,
                                                         cfg.pos_height, gh, gw, cfg.width, c.stream)),
             "interpolate");
-    trace(c, pos, "position");
-    add_in_place(c, x, pos);
-    pos = {};
-    trace(c, x, "embedding");
-    for (uint32_t i = 0; i < cfg.layers; ++i) {
+    Tensor features = c.make(count * n, cfg.code_dim, true);
+    const std::vector<int> all_keys(1, static_cast<int>(n));
+    const size_t chunk = chunk_items(count, n);
+    for_chunks(c, pixels, count, item_floats, chunk, [&](size_t i0, size_t items, const float *src) {
+        cuda_ok(static_cast<cudaError_t>(graph::finite_check(src, items * item_floats,
+                                                             static_cast<int *>(flag.data()), c.stream)),
+                "input check");
+        Tensor patches = c.make(items * n, 8 * P * P, true);
+        cuda_ok(static_cast<cudaError_t>(graph::image_patches(src, patches.data(), items, height, width, P,
+                                                              c.stream)),
+                "patches");
+        Tensor x = linear(c, patches, m.get("patch_embed.proj.weight"), &m.get("patch_embed.proj.bias"), true);
+        patches = {};
+        trace(c, x, "patch");
+        if (i0 == 0)
+            trace(c, pos, "position");
+        cuda_ok(static_cast<cudaError_t>(graph::add_periodic(x.data(), pos.data(), true, x.size(), pos.size(),
+                                                             c.stream)),
+                "positions");
+        trace(c, x, "embedding");
+        for (uint32_t i = 0; i < cfg.layers; ++i) {
+            c.check();
+            const std::string p = "blocks." + std::to_string(i) + ".";
+            auto proj = [&](const Tensor &in, const std::string &name) {
+                return linear(c, in, m.get(name + ".weight"), m.opt(name + ".bias"));
+            };
+            Tensor z = layer_norm(c, x, m.get(p + "norm1.weight"), m.get(p + "norm1.bias"), 1e-6f);
+            if (i == 0)
+                trace(c, z, "norm1.0");
+            z = proj(z, p + "attn.qkv");
+            if (i == 0)
+                trace(c, z, "qkv.0");
+            z = attention(c, z, nullptr, nullptr, cfg.heads, 0, true, items, all_keys, nullptr);
+            if (i == 0)
+                trace(c, z, "attention.0");
+            z = proj(z, p + "attn.proj");
+            add_in_place(c, x, z);
+            if (i == 0)
+                trace(c, x, "residual1.0");
+            z = layer_norm(c, x, m.get(p + "norm2.weight"), m.get(p + "norm2.bias"), 1e-6f);
+            z = proj(z, p + "mlp.fc1");
+            if (i == 0)
+                trace(c, z, "fc1.0");
+            gelu_in_place(c, z);
+            if (i == 0)
+                trace(c, z, "gelu.0");
+            z = proj(z, p + "mlp.fc2");
+            if (i == 0)
+                trace(c, z, "fc2.0");
+            add_in_place(c, x, z);
+            trace(c, x, "layer." + std::to_string(i));
+        }
         c.check();
-        const std::string p = "blocks." + std::to_string(i) + ".";
-        auto proj = [&](const Tensor &in, const std::string &name) {
-            return linear(c, in, m.get(name + ".weight"), m.opt(name + ".bias"));
-        };
-        Tensor z = layer_norm(c, x, m.get(p + "norm1.weight"), m.get(p + "norm1.bias"), 1e-6f);
-        if (i == 0)
-            trace(c, z, "norm1.0");
-        z = proj(z, p + "attn.qkv");
-        if (i == 0)
-            trace(c, z, "qkv.0");
-        z = attention(c, z, nullptr, nullptr, cfg.heads, 0, n, true);
-        if (i == 0)
-            trace(c, z, "attention.0");
-        z = proj(z, p + "attn.proj");
-        add_in_place(c, x, z);
-        if (i == 0)
-            trace(c, x, "residual1.0");
-        z = layer_norm(c, x, m.get(p + "norm2.weight"), m.get(p + "norm2.bias"), 1e-6f);
-        z = proj(z, p + "mlp.fc1");
-        if (i == 0)
-            trace(c, z, "fc1.0");
-        gelu_in_place(c, z);
-        if (i == 0)
-            trace(c, z, "gelu.0");
-        z = proj(z, p + "mlp.fc2");
-        if (i == 0)
-            trace(c, z, "fc2.0");
-        add_in_place(c, x, z);
-        trace(c, x, "layer." + std::to_string(i));
-    }
-    c.check();
-    x = linear(c, x, m.get("quant_conv.weight"), &m.get("quant_conv.bias"), true);
-    trace(c, x, "projected");
-    Tensor f = c.make(x.rows, x.cols, true);
-    cuda_ok(static_cast<cudaError_t>(graph::normalize(x.data(), f.data(), true, x.rows, x.cols, c.stream)),
-            "normalize");
-    c.features = f;
-    return quantize(c, c.features, m.get("quantize.embedding.weight"), m.cbnorm);
+        x = linear(c, x, m.get("quant_conv.weight"), &m.get("quant_conv.bias"), true);
+        trace(c, x, "projected");
+        cuda_ok(static_cast<cudaError_t>(graph::normalize(
+                    x.data(), static_cast<__nv_bfloat16 *>(features.data()) + i0 * n * cfg.code_dim, true, x.rows,
+                    x.cols, c.stream)),
+                "normalize");
+    });
+    auto ids = quantize(c, features, m.get("quantize.embedding.weight"), m.cbnorm);
+    finite_or_fail(c, flag);
+    c.features = features;
+    return ids;
 }
 
 } // namespace rt
@@ -727,6 +859,10 @@ int omni_context_create(omni_model *m, omni_context **out) {
                                "stream create");
         omni_b200::rt::blas_ok(cublasCreate(&c->impl.blas), "cuBLAS handle");
         omni_b200::rt::blas_ok(cublasSetStream(c->impl.blas, c->impl.stream), "cuBLAS stream");
+        omni_b200::rt::cuda_ok(cudaStreamCreateWithFlags(&c->impl.copy, cudaStreamNonBlocking), "stream create");
+        for (cudaEvent_t *e : {&c->impl.ready[0], &c->impl.ready[1], &c->impl.done[0], &c->impl.done[1],
+                               &c->impl.start})
+            omni_b200::rt::cuda_ok(cudaEventCreateWithFlags(e, cudaEventDisableTiming), "event create");
         const char *fast = std::getenv("OMNI_B200_AUDIO_BF16");
         c->impl.audio_bf16 = fast && *fast && *fast != '0';
         *out = c.release();
@@ -751,33 +887,48 @@ int omni_context_set_trace(omni_context *c, omni_trace_callback callback, void *
 }
 int omni_encode_audio(omni_context *c, const float *mel, uint32_t frames, uint32_t valid,
                       uint16_t *codes, size_t capacity, size_t *count) {
+    return omni_b200_encode_audio_batch(c, mel, 1, frames, &valid, codes, capacity, count);
+}
+int omni_encode_image(omni_context *c, const float *pixels, uint32_t height, uint32_t width,
+                      uint16_t *codes, size_t capacity, size_t *count) {
+    return omni_b200_encode_images(c, pixels, 1, height, width, codes, capacity, count);
+}
+int omni_b200_encode_audio_batch(omni_context *c, const float *mel, uint32_t items, uint32_t frames,
+                                 const uint32_t *valid, uint16_t *codes, size_t capacity, size_t *count) {
     return guarded([&] {
-        require(c && mel && count, "Invalid audio pointers");
+        require(c && mel && valid && count, "Invalid audio pointers");
         const auto &cfg = c->impl.model->cfg;
         require(cfg.kind == OMNI_AUDIO, "Model is not an audio tokenizer");
-        require(frames > 0 && frames % 8 == 0 && frames <= 3000 && frames / 2 <= cfg.pos_height &&
-                    valid > 0 && valid <= frames,
+        require(items > 0, "Invalid audio batch size");
+        require(frames > 0 && frames % 8 == 0 && frames <= 3000 && frames / 2 <= cfg.pos_height,
                 "Invalid audio frame lengths");
-        *count = (valid + 7) / 8;
+        size_t total = 0;
+        for (uint32_t i = 0; i < items; ++i) {
+            require(valid[i] > 0 && valid[i] <= frames, "Invalid audio frame lengths");
+            total += (valid[i] + 7) / 8;
+        }
+        *count = total;
         require(codes && capacity >= *count, "Output capacity is too small");
         Running guard(c->impl);
         omni_b200::rt::cuda_ok(cudaSetDevice(c->impl.model->device), "set device");
         c->impl.features = {};
-        const auto ids = omni_b200::rt::encode_audio(c->impl, mel, frames, valid);
+        const auto ids = omni_b200::rt::encode_audio_batch(c->impl, mel, items, frames, valid);
         std::copy(ids.begin(), ids.end(), codes);
     });
 }
-int omni_encode_image(omni_context *c, const float *pixels, uint32_t height, uint32_t width,
-                      uint16_t *codes, size_t capacity, size_t *count) {
+int omni_b200_encode_images(omni_context *c, const float *pixels, uint32_t items, uint32_t height,
+                            uint32_t width, uint16_t *codes, size_t capacity, size_t *count) {
     return guarded([&] {
         require(c && pixels && count, "Invalid image pointers");
         const auto &cfg = c->impl.model->cfg;
         require(cfg.kind == OMNI_IMAGE, "Model is not an image tokenizer");
+        require(items > 0, "Invalid image batch size");
         require(height > 0 && width > 0 && height % cfg.patch_size == 0 && width % cfg.patch_size == 0,
                 "Invalid image dimensions");
         const uint64_t patches = uint64_t(height / cfg.patch_size) * (width / cfg.patch_size);
         // Activation, patch, attention and VQ buffers stay within int-indexed BLAS
-        // dimensions (the reference's capacity rule, src/runtime.cpp:253-262).
+        // dimensions (the reference's capacity rule, src/runtime.cpp:253-262); a
+        // batch is processed in chunks of whole images, so the rule is per image.
         const uint64_t columns = std::max({uint64_t(8) * cfg.patch_size * cfg.patch_size,
                                           uint64_t(3) * cfg.width, uint64_t(cfg.ffn),
                                           uint64_t(cfg.code_dim), uint64_t(256) * cfg.heads,
@@ -785,12 +936,13 @@ int omni_encode_image(omni_context *c, const float *pixels, uint32_t height, uin
         const uint64_t elements = std::min(uint64_t(std::numeric_limits<int>::max()),
                                           uint64_t(std::numeric_limits<size_t>::max() / sizeof(float)));
         require(patches <= elements / columns, "Image dimensions exceed native tensor indexing capacity");
-        *count = static_cast<size_t>(patches);
+        require(patches * items <= uint64_t(std::numeric_limits<int>::max()), "Image batch is too large");
+        *count = static_cast<size_t>(patches * items);
         require(codes && capacity >= *count, "Output capacity is too small");
         Running guard(c->impl);
         omni_b200::rt::cuda_ok(cudaSetDevice(c->impl.model->device), "set device");
         c->impl.features = {};
-        const auto ids = omni_b200::rt::encode_image(c->impl, pixels, height, width);
+        const auto ids = omni_b200::rt::encode_images(c->impl, pixels, items, height, width);
         std::copy(ids.begin(), ids.end(), codes);
     });
 }

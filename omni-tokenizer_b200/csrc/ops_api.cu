@@ -68,6 +68,110 @@ int launch_status(int rc, const char *what) {
 
 } // namespace omni_b200
 
+
+namespace omni_b200 {
+
+size_t attention_rows_workspace(size_t rows, int heads, int head_dim, int dtype, int fused) {
+    const int hdp = padded_head_dim(head_dim);
+    if (hdp < 0 || heads <= 0 || rows == 0)
+        return 0;
+    const long long d = static_cast<long long>(heads) * head_dim;
+    const long long s_token = fused ? 3 * d : d;
+    const bool direct = dtype != OMNI_B200_F32 && head_dim % 8 == 0 && s_token % 8 == 0;
+    if (direct)
+        return 0;
+    const size_t one = (rows * static_cast<size_t>(heads) * hdp * 2 + 255) / 256 * 256;
+    return 3 * one;
+}
+
+// `batch` sequences of n tokens stacked as batch*n rows.  Items are contiguous
+// along the token axis, so the packed copy [heads, batch*n, hdp] is also a
+// (hdp, n, heads, batch) view with s_batch = n*hdp.
+int attention_rows(const void *q, const void *k, const void *v, void *out, size_t n, int batch,
+                   int heads, int head_dim, size_t block, size_t valid, const int *lengths,
+                   int fused, int dtype, int out_dtype, void *workspace, size_t workspace_bytes,
+                   cudaStream_t s) {
+    g_error.clear();
+    if (!q || !out || (!fused && (!k || !v)))
+        return fail(1, "attention_rows: null tensor pointer");
+    if (n == 0 || batch <= 0 || heads <= 0 || head_dim <= 0 || (valid == 0 && !lengths) ||
+        n * static_cast<size_t>(batch) > (1u << 30))
+        return fail(1, "attention_rows: sizes must be positive");
+    if (dtype < OMNI_B200_F32 || dtype > OMNI_B200_F16 || out_dtype < OMNI_B200_F32 ||
+        out_dtype > OMNI_B200_F16)
+        return fail(1, "attention_rows: invalid dtype");
+    const int hdp = padded_head_dim(head_dim);
+    if (hdp < 0)
+        return fail(4, "attention_rows: head_dim above 128 is not supported");
+    const size_t rows = n * static_cast<size_t>(batch);
+    const long long d = static_cast<long long>(heads) * head_dim;
+    const long long s_token = fused ? 3 * d : d;
+    const void *qp = q, *kp = fused ? static_cast<const char *>(q) + d * (dtype ? 2 : 4) : k,
+               *vp = fused ? static_cast<const char *>(q) + 2 * d * (dtype ? 2 : 4) : v;
+    FmhaArgs a;
+    TensorView view;
+    view.d = head_dim;
+    view.tokens = static_cast<int>(n);
+    view.heads = heads;
+    view.batch = batch;
+    view.s_token = s_token;
+    view.s_head = head_dim;
+    view.s_batch = s_token * static_cast<long long>(n);
+    const size_t need = attention_rows_workspace(rows, heads, head_dim, dtype, fused);
+    const bool direct = need == 0 && tma_view_ok(qp, view) && tma_view_ok(kp, view) &&
+                        tma_view_ok(vp, view);
+    if (direct) {
+        a.q_ptr = qp;
+        a.k_ptr = kp;
+        a.v_ptr = vp;
+        a.q = a.k = a.v = view;
+        a.bf16 = dtype == OMNI_B200_BF16;
+    } else {
+        const size_t one = (rows * static_cast<size_t>(heads) * hdp * 2 + 255) / 256 * 256;
+        if (!workspace || workspace_bytes < 3 * one)
+            return fail(1, "attention_rows: workspace too small (need " +
+                               std::to_string(3 * one) + " bytes)");
+        char *w = static_cast<char *>(workspace);
+        const void *src[3] = {qp, kp, vp};
+        for (int i = 0; i < 3; ++i) {
+            const int rc = pack_heads(src[i], dtype, s_token, head_dim, static_cast<int>(rows), heads,
+                                      head_dim, hdp, w + i * one, s);
+            if (rc)
+                return cuda_fail(static_cast<cudaError_t>(rc), "attention_rows: pack");
+        }
+        TensorView pv;
+        pv.d = hdp;
+        pv.tokens = static_cast<int>(n);
+        pv.heads = heads;
+        pv.batch = batch;
+        pv.s_token = hdp;
+        pv.s_head = static_cast<long long>(rows) * hdp;
+        pv.s_batch = static_cast<long long>(n) * hdp;
+        a.q_ptr = w;
+        a.k_ptr = w + one;
+        a.v_ptr = w + 2 * one;
+        a.q = a.k = a.v = pv;
+        a.bf16 = dtype != OMNI_B200_F16;
+    }
+    a.out = out;
+    a.out_dtype = out_dtype;
+    a.o_st = d;
+    a.o_sh = head_dim;
+    a.o_sb = d * static_cast<long long>(n);
+    a.lengths = lengths;
+    a.valid = valid > n || valid == 0 ? static_cast<int>(n) : static_cast<int>(valid);
+    a.block = block > n ? static_cast<int>(n) : static_cast<int>(block);
+    a.skip_padded_q = 0;
+    a.scale = 1.0 / std::sqrt(static_cast<double>(head_dim));
+    a.out_d = head_dim; // packed operands are hdp wide; the output keeps head_dim
+    a.err = kernel_error_word();
+    if (!a.err)
+        return fail(7, "attention_rows: no CUDA device");
+    return launch_status(fmha_launch(a, s), "attention_rows");
+}
+
+} // namespace omni_b200
+
 using namespace omni_b200;
 
 extern "C" {
@@ -144,98 +248,15 @@ int omni_b200_attention_bhld(const void *q, const void *k, const void *v, void *
 }
 
 size_t omni_b200_attention_rows_workspace(size_t n, int heads, int head_dim, int dtype, int fused) {
-    const int hdp = padded_head_dim(head_dim);
-    if (hdp < 0 || heads <= 0 || n == 0)
-        return 0;
-    const long long d = static_cast<long long>(heads) * head_dim;
-    const long long s_token = fused ? 3 * d : d;
-    const bool direct = dtype != OMNI_B200_F32 && head_dim % 8 == 0 && s_token % 8 == 0;
-    if (direct)
-        return 0;
-    const size_t one = (n * static_cast<size_t>(heads) * hdp * 2 + 255) / 256 * 256;
-    return 3 * one;
+    return attention_rows_workspace(n, heads, head_dim, dtype, fused);
 }
 
 int omni_b200_attention_rows(const void *q, const void *k, const void *v, void *out, size_t n,
                              int heads, int head_dim, size_t block, size_t valid, int fused,
                              int dtype, int out_dtype, void *workspace, size_t workspace_bytes,
                              void *stream) {
-    g_error.clear();
-    if (!q || !out || (!fused && (!k || !v)))
-        return fail(1, "attention_rows: null tensor pointer");
-    if (n == 0 || heads <= 0 || head_dim <= 0 || valid == 0 || n > (1u << 30))
-        return fail(1, "attention_rows: sizes must be positive");
-    if (dtype < OMNI_B200_F32 || dtype > OMNI_B200_F16 || out_dtype < OMNI_B200_F32 ||
-        out_dtype > OMNI_B200_F16)
-        return fail(1, "attention_rows: invalid dtype");
-    const int hdp = padded_head_dim(head_dim);
-    if (hdp < 0)
-        return fail(4, "attention_rows: head_dim above 128 is not supported");
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    const long long d = static_cast<long long>(heads) * head_dim;
-    const long long s_token = fused ? 3 * d : d;
-    const void *qp = q, *kp = fused ? static_cast<const char *>(q) + d * (dtype ? 2 : 4) : k,
-               *vp = fused ? static_cast<const char *>(q) + 2 * d * (dtype ? 2 : 4) : v;
-    FmhaArgs a;
-    TensorView view;
-    view.d = head_dim;
-    view.tokens = static_cast<int>(n);
-    view.heads = heads;
-    view.batch = 1;
-    view.s_token = s_token;
-    view.s_head = head_dim;
-    view.s_batch = s_token * static_cast<long long>(n);
-    const size_t need = omni_b200_attention_rows_workspace(n, heads, head_dim, dtype, fused);
-    const bool direct = need == 0 && tma_view_ok(qp, view) && tma_view_ok(kp, view) &&
-                        tma_view_ok(vp, view);
-    if (direct) {
-        a.q_ptr = qp;
-        a.k_ptr = kp;
-        a.v_ptr = vp;
-        a.q = a.k = a.v = view;
-        a.bf16 = dtype == OMNI_B200_BF16;
-    } else {
-        const size_t one = (n * static_cast<size_t>(heads) * hdp * 2 + 255) / 256 * 256;
-        if (!workspace || workspace_bytes < 3 * one)
-            return fail(1, "attention_rows: workspace too small (need " +
-                               std::to_string(3 * one) + " bytes)");
-        char *w = static_cast<char *>(workspace);
-        const void *src[3] = {qp, kp, vp};
-        for (int i = 0; i < 3; ++i) {
-            const int rc = pack_heads(src[i], dtype, s_token, head_dim, static_cast<int>(n), heads,
-                                      head_dim, hdp, w + i * one, s);
-            if (rc)
-                return cuda_fail(static_cast<cudaError_t>(rc), "attention_rows: pack");
-        }
-        TensorView pv;
-        pv.d = hdp;
-        pv.tokens = static_cast<int>(n);
-        pv.heads = heads;
-        pv.batch = 1;
-        pv.s_token = hdp;
-        pv.s_head = static_cast<long long>(n) * hdp;
-        pv.s_batch = pv.s_head * heads;
-        a.q_ptr = w;
-        a.k_ptr = w + one;
-        a.v_ptr = w + 2 * one;
-        a.q = a.k = a.v = pv;
-        a.bf16 = dtype != OMNI_B200_F16;
-    }
-    a.out = out;
-    a.out_dtype = out_dtype;
-    a.o_st = d;
-    a.o_sh = head_dim;
-    a.o_sb = d * static_cast<long long>(n);
-    a.lengths = nullptr;
-    a.valid = valid > n ? static_cast<int>(n) : static_cast<int>(valid);
-    a.block = block > n ? static_cast<int>(n) : static_cast<int>(block);
-    a.skip_padded_q = 0;
-    a.scale = 1.0 / std::sqrt(static_cast<double>(head_dim));
-    a.out_d = head_dim; // packed operands are hdp wide; the output keeps head_dim
-    a.err = kernel_error_word();
-    if (!a.err)
-        return fail(7, "attention_rows: no CUDA device");
-    return launch_status(fmha_launch(a, s), "attention_rows");
+    return attention_rows(q, k, v, out, n, 1, heads, head_dim, block, valid, nullptr, fused, dtype,
+                          out_dtype, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
 int omni_b200_squares(const void *x, void *out, size_t rows, size_t cols, int dtype, int out_dtype,

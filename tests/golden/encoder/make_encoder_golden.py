@@ -33,6 +33,7 @@ def main():
     ov.write_random_model(HERE / "audio.omni", ov.audio_config(**AUDIO_CFG), seed=11)
     ov.write_random_model(HERE / "image.omni", ov.image_config(**IMAGE_CFG), seed=12)
     rng = np.random.default_rng(2024)
+    rng_batch = np.random.default_rng(2025)  # the batch fixtures leave the single-item draws unchanged
     out = {}
     with ref.load(HERE / "audio.omni", backend=abi.CPU) as m:
         s = m.context()
@@ -43,6 +44,16 @@ def main():
             out[f"audio{i}_valid"] = np.int32(valid)
             out[f"audio{i}_codes"] = codes
             out[f"audio{i}_features"] = s.features(len(codes))
+        # A batch for the batched extension: segments of one frame count with
+        # different valid lengths, each run alone through the reference.
+        mels = rng_batch.uniform(-1.5, 1.5, (4, AUDIO_CFG["mel"], 64)).astype(np.float32)
+        valid = np.array([64, 33, 8, 57], np.int32)
+        codes, feats = [], []
+        for mel, v in zip(mels, valid):
+            codes.append(s.encode_audio(mel, int(v)))
+            feats.append(s.features(len(codes[-1])))
+        out["audio_batch_mel"], out["audio_batch_valid"] = mels, valid
+        out["audio_batch_codes"], out["audio_batch_features"] = np.concatenate(codes), np.concatenate(feats)
         s.close()
     with ref.load(HERE / "image.omni", backend=abi.CPU) as m:
         s = m.context()
@@ -52,6 +63,13 @@ def main():
             out[f"image{i}_pixels"] = px
             out[f"image{i}_codes"] = codes
             out[f"image{i}_features"] = s.features(len(codes))
+        pxs = rng_batch.uniform(-1, 1, (5, 3, 32, 24)).astype(np.float32)
+        codes, feats = [], []
+        for px in pxs:
+            codes.append(s.encode_image(px))
+            feats.append(s.features(len(codes[-1])))
+        out["image_batch_pixels"] = pxs
+        out["image_batch_codes"], out["image_batch_features"] = np.concatenate(codes), np.concatenate(feats)
         s.close()
     np.savez_compressed(HERE / "golden.npz", **out)
     print("wrote", HERE / "golden.npz", {k: v.shape for k, v in out.items() if k.endswith("codes")})

@@ -70,9 +70,24 @@ def test_outer_abi_declares_and_exports_the_15_entry_points():
     import omni_tokenizer_b200.abi as abi
 
     names = abi_symbols()
-    assert names == sorted(abi.SYMBOLS) and len(names) == 15
-    lib = abi.OmniLib(ROOT / "omni-tokenizer_b200" / "libomni_b200.so")  # binds all 15
+    assert names == sorted(abi.SYMBOLS + abi.EXTENSION_SYMBOLS) and len(abi.SYMBOLS) == 15
+    assert all(n.startswith("omni_b200_") for n in abi.EXTENSION_SYMBOLS)
+    lib = abi.OmniLib(ROOT / "omni-tokenizer_b200" / "libomni_b200.so")  # binds all 15 and the extension
+    assert lib.batched
     assert lib.lib.omni_version().startswith(b"0.1.0")
+
+
+def test_batched_extension_argument_errors_without_a_device():
+    load_package()
+    import omni_tokenizer_b200.abi as abi
+
+    lib = abi.OmniLib(ROOT / "omni-tokenizer_b200" / "libomni_b200.so")
+    count = C.c_size_t(7)
+    valid = (C.c_uint32 * 1)(8)
+    assert lib.lib.omni_b200_encode_audio_batch(None, None, 1, 8, valid, None, 0, C.byref(count)) == 1
+    assert b"Invalid audio pointers" in lib.lib.omni_last_error()
+    assert lib.lib.omni_b200_encode_images(None, None, 1, 8, 8, None, 0, C.byref(count)) == 1
+    assert b"Invalid image pointers" in lib.lib.omni_last_error()
 
 
 def test_outer_abi_errors_without_a_device(tmp_path):

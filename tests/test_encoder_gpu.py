@@ -121,6 +121,68 @@ def test_image_encoder_matches_reference(abi, ours, golden):
         s.close()
 
 
+def test_batched_audio_matches_per_item_reference(abi, ours, golden):
+    """omni_b200_encode_audio_batch: segments of one frame count with different
+    valid lengths equal the reference run segment by segment."""
+    cb = _codebook("audio")
+    mels, valid = golden["audio_batch_mel"], golden["audio_batch_valid"]
+    want_codes, want = golden["audio_batch_codes"].astype(np.int64), golden["audio_batch_features"]
+    with ours.load(GOLDEN / "audio.omni") as m:
+        s = m.context()
+        codes = s.encode_audio_batch(mels, valid)
+        feats = s.features(len(codes))
+        assert feats.shape == want.shape
+        np.testing.assert_allclose(feats, want, rtol=1e-4, atol=1e-4)
+        _check_codes(codes.astype(np.int64), want_codes, feats, want, cb, False)
+        # Device-resident input gives the same codes.
+        dev = torch.from_numpy(mels).cuda()
+        again = s.encode_audio_batch(tuple(dev.shape), valid, device_ptr=dev.data_ptr())
+        np.testing.assert_array_equal(again, codes)
+        s.close()
+
+
+def test_batched_images_match_per_item_reference(abi, ours, golden):
+    cb = _codebook("image")
+    pxs = golden["image_batch_pixels"]
+    want_codes, want = golden["image_batch_codes"].astype(np.int64), golden["image_batch_features"]
+    with ours.load(GOLDEN / "image.omni") as m:
+        s = m.context()
+        codes = s.encode_images(pxs, patch=8)
+        feats = s.features(len(codes))
+        assert feats.shape == want.shape
+        assert np.abs(feats - want).max() <= 1 / 128
+        _check_codes(codes.astype(np.int64), want_codes, feats, want, cb, True)
+        dev = torch.from_numpy(pxs).cuda()
+        again = s.encode_images(tuple(dev.shape), patch=8, device_ptr=dev.data_ptr())
+        np.testing.assert_array_equal(again, codes)
+        # Non-finite input anywhere in the batch fails the call.
+        bad = pxs.copy()
+        bad[3, 1, 5, 7] = np.inf
+        with pytest.raises(abi.OmniError) as e:
+            s.encode_images(bad, patch=8)
+        assert e.value.status == 1 and "non-finite" in str(e.value)
+        s.close()
+
+
+def test_batched_images_across_chunks(abi, ours):
+    """A batch larger than one chunk (host input double-buffered through the
+    copy stream) equals the same images sent in single-chunk pieces."""
+    rng = np.random.default_rng(91)
+    pxs = rng.uniform(-1, 1, (20000, 3, 32, 24)).astype(np.float32)  # 12 rows per image: 3 chunks
+    with ours.load(GOLDEN / "image.omni") as m:
+        s = m.context()
+        whole = s.encode_images(pxs, patch=8)
+        whole_f = s.features(len(whole))
+        parts, parts_f = [], []
+        for i in range(0, len(pxs), 5000):
+            parts.append(s.encode_images(pxs[i:i + 5000], patch=8))
+            parts_f.append(s.features(len(parts[-1])))
+        parts, parts_f = np.concatenate(parts), np.concatenate(parts_f)
+        assert np.abs(whole_f - parts_f).max() <= 1 / 128
+        _check_codes(whole.astype(np.int64), parts.astype(np.int64), whole_f, parts_f, _codebook("image"), True)
+        s.close()
+
+
 def test_live_reference_cross_check(abi, ours):
     """Same inputs through the reference CPU library (when built) and this library."""
     ref_path = ROOT / "oracle" / "_ref" / "libomni_ref_full.so"
