@@ -82,7 +82,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         # toolkit the library was built with.
         cuda_lib = Path(nvcc()).resolve().parent.parent / "lib64"
         cmd = [nvcc()] + ARCH + ["-shared", "-o", str(LIB)] + [str(o) for o in objs] + [
-            "-L", str(cuda_lib), "-lcublas", "-Xlinker", f"-rpath={cuda_lib}"]
+            "-L", str(cuda_lib), "-lcublas", "-lcublasLt", "-Xlinker", f"-rpath={cuda_lib}"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stderr}")

@@ -219,48 +219,47 @@ __global__ void k_to_float(const void *x, float *y, bool bf16, size_t n) {
     GRID_STRIDE(i, n) { y[i] = ld(x, i, bf16); }
 }
 
-// One warp per (query t, head h): pass 1 keeps the scores of keys < limit(t)
-// in shared memory and their maximum, pass 2 their exponentials and sum, pass
-// 3 accumulates the output in key order, each lane owning head-dim columns.
-__global__ void k_attention_f32(const float *q, const float *k, const float *v, float *y, size_t n,
-                                size_t heads, size_t hd, size_t block, size_t valid) {
-    extern __shared__ float sm[];
-    const int wib = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float *scores = sm + static_cast<size_t>(wib) * n;
-    const size_t task = static_cast<size_t>(blockIdx.x) * (blockDim.x >> 5) + wib;
-    if (task >= n * heads)
+// Scores -> probabilities in place, one warp per score row.  Rows are
+// [items, heads, n] of n scores each; row t of item b keeps keys below
+// limit = min(n, valid[b]) (and the block window), p = exp(z - max) / total as
+// the reference's Ops::attention; masked keys become 0.
+template <int PER_LANE>
+__global__ void k_softmax_rows(float *s, size_t items, size_t heads, size_t n, const int *valid,
+                               size_t valid_all, size_t block) {
+    const size_t row = static_cast<size_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= items * heads * n)
         return;
-    const size_t t = task / heads, h = task % heads, d = heads * hd;
-    size_t limit = n < valid ? n : valid;
+    const size_t b = row / (heads * n), t = row % n;
+    size_t limit = valid ? static_cast<size_t>(valid[b] > 0 ? valid[b] : 0) : valid_all;
+    limit = limit < n ? limit : n;
     if (block)
         limit = limit < (t / block + 1) * block ? limit : (t / block + 1) * block;
-    const float scale = 1.f / sqrtf(static_cast<float>(hd));
-    const float *qr = q + t * d + h * hd;
+    float *z = s + row * n;
+    float v[PER_LANE];
     float mx = -INFINITY;
-    for (size_t s = lane; s < limit; s += 32) {
-        const float *kr = k + s * d + h * hd;
-        float z = 0.f;
-        for (size_t j = 0; j < hd; ++j)
-            z = __fadd_rn(z, __fmul_rn(__fmul_rn(qr[j], scale), kr[j]));
-        scores[s] = z;
-        mx = fmaxf(mx, z);
+#pragma unroll
+    for (int i = 0; i < PER_LANE; ++i) {
+        const size_t c = lane + 32 * static_cast<size_t>(i);
+        v[i] = c < limit ? z[c] : -INFINITY;
+        mx = fmaxf(mx, v[i]);
     }
     for (int o = 16; o > 0; o >>= 1)
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     float total = 0.f;
-    for (size_t s = lane; s < limit; s += 32) {
-        const float e = expf(scores[s] - mx);
-        scores[s] = e;
-        total += e;
+#pragma unroll
+    for (int i = 0; i < PER_LANE; ++i) {
+        const size_t c = lane + 32 * static_cast<size_t>(i);
+        v[i] = c < limit ? expf(v[i] - mx) : 0.f;
+        total += v[i];
     }
     for (int o = 16; o > 0; o >>= 1)
         total += __shfl_xor_sync(0xffffffffu, total, o);
-    __syncwarp();
-    for (size_t j = lane; j < hd; j += 32) {
-        float acc = 0.f;
-        for (size_t s = 0; s < limit; ++s)
-            acc = __fadd_rn(acc, __fmul_rn(scores[s] / total, v[s * d + h * hd + j]));
-        y[t * d + h * hd + j] = acc;
+#pragma unroll
+    for (int i = 0; i < PER_LANE; ++i) {
+        const size_t c = lane + 32 * static_cast<size_t>(i);
+        if (c < n)
+            z[c] = v[i] / total;
     }
 }
 
@@ -344,17 +343,21 @@ int to_float(const void *x, float *y, bool bf16, size_t n, cudaStream_t s) {
     k_to_float<<<blocks_for(n, 256), 256, 0, s>>>(x, y, bf16, n);
     return status();
 }
-int attention_f32(const float *q, const float *k, const float *v, float *y, size_t n, size_t heads,
-                  size_t hd, size_t block, size_t valid, cudaStream_t s) {
-    constexpr int kWarps = 4;
-    const size_t smem = static_cast<size_t>(kWarps) * n * sizeof(float);
-    if (smem > 200 * 1024)
-        return -2; // sequences longer than 12800 keys are not supported here
-    // Per device: the attribute belongs to the current device's copy of the kernel.
-    cudaFuncSetAttribute(k_attention_f32, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    const size_t tasks = n * heads;
-    k_attention_f32<<<static_cast<unsigned>((tasks + kWarps - 1) / kWarps), kWarps * 32, smem, s>>>(
-        q, k, v, y, n, heads, hd, block, valid);
+int softmax_rows(float *scores, size_t items, size_t heads, size_t n, const int *valid, size_t valid_all,
+                 size_t block, cudaStream_t s) {
+    const size_t rows = items * heads * n;
+    if (rows == 0)
+        return 0;
+    constexpr int kWarps = 8;
+    const unsigned grid = static_cast<unsigned>((rows + kWarps - 1) / kWarps);
+    if (n <= 512)
+        k_softmax_rows<16><<<grid, kWarps * 32, 0, s>>>(scores, items, heads, n, valid, valid_all, block);
+    else if (n <= 1536)
+        k_softmax_rows<48><<<grid, kWarps * 32, 0, s>>>(scores, items, heads, n, valid, valid_all, block);
+    else if (n <= 4096)
+        k_softmax_rows<128><<<grid, kWarps * 32, 0, s>>>(scores, items, heads, n, valid, valid_all, block);
+    else
+        return -2; // longer rows are not produced by the graphs (audio n <= 1500)
     return status();
 }
 

@@ -51,10 +51,11 @@ int image_patches(const float *pixels, void *y, size_t count, size_t height, siz
 int convert(const float *x, void *y, bool bf16, size_t n, cudaStream_t s);
 // bf16/fp32 -> fp32.
 int to_float(const void *x, float *y, bool bf16, size_t n, cudaStream_t s);
-// fp32 multi-head attention on [n, heads*hd] rows (the fp32 audio profile):
-// scores (q*scale).k, softmax over keys < limit(t), output in fp32.
-int attention_f32(const float *q, const float *k, const float *v, float *y, size_t n, size_t heads,
-                  size_t hd, size_t block, size_t valid, cudaStream_t s);
+// Attention probabilities in place over [items, heads, n, n] fp32 scores:
+// row t of item b keeps keys < min(n, valid[b] (or valid_all when valid is
+// null), block window end); p = exp(z - max) / total, masked keys 0.  n <= 4096.
+int softmax_rows(float *scores, size_t items, size_t heads, size_t n, const int *valid, size_t valid_all,
+                 size_t block, cudaStream_t s);
 
 } // namespace graph
 } // namespace omni_b200

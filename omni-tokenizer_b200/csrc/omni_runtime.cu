@@ -10,9 +10,10 @@
 // vq_sm100.cu / vq_stream_sm100.cu; norms: norms.cu); linears are cuBLAS
 // GEMMs (fp32 in the audio profile, bf16 x bf16 -> fp32 in the image profile)
 // followed by the bias / bf16-rounding epilogue; the remaining operators are
-// graph_kernels.cu.  Audio-profile attention runs in fp32 on the CUDA cores
-// (the reference's audio kernels are fp32-accurate 3xTF32); setting
-// OMNI_B200_AUDIO_BF16=1 routes it through the tcgen05 kernel instead.
+// graph_kernels.cu.  Audio-profile attention stays fp32 (the reference's audio
+// kernels are fp32-accurate 3xTF32): fp32 cuBLAS GEMMs for the scores and the
+// weighted values around a masked-softmax kernel; setting
+// OMNI_B200_AUDIO_BF16=1 routes it through the bf16 tcgen05 kernel instead.
 #include "fmha.h"
 #include "graph_kernels.h"
 #include "omni_abi.h"
@@ -23,7 +24,10 @@
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
+#include <array>
+#include <cublasLt.h>
 #include <cublas_v2.h>
+#include <map>
 #include <cuda_runtime.h>
 #include <fstream>
 #include <limits>
@@ -341,6 +345,10 @@ struct Context {
     std::shared_ptr<Model> model;
     cudaStream_t stream = nullptr;
     cublasHandle_t blas = nullptr;
+    // Activations come from this context's own stream-ordered pool, which keeps
+    // its memory between calls (a pool with the default release threshold
+    // returns it at every synchronisation and re-maps it on the next call).
+    cudaMemPool_t pool = nullptr;
     std::shared_ptr<Memory> memory = std::make_shared<Memory>();
     std::atomic<bool> cancelled{false};
     std::atomic_flag running = ATOMIC_FLAG_INIT;
@@ -352,6 +360,12 @@ struct Context {
     // ready[i] / done[i]), overlapping the graph of the previous chunk.
     cudaStream_t copy = nullptr;
     cudaEvent_t ready[2] = {}, done[2] = {}, start = nullptr;
+    // cuBLASLt linears: handle, workspace and the chosen algorithm per shape
+    // (m, n, k, bf16, fused bias).
+    cublasLtHandle_t lt = nullptr;
+    void *lt_ws = nullptr;
+    size_t lt_ws_bytes = 0;
+    std::map<std::array<long long, 5>, std::pair<bool, cublasLtMatmulAlgo_t>> lt_algos;
 
     ~Context() {
         features = {};
@@ -366,10 +380,16 @@ struct Context {
                 cudaEventDestroy(e);
         if (blas)
             cublasDestroy(blas);
+        if (lt)
+            cublasLtDestroy(lt);
+        if (lt_ws)
+            cudaFree(lt_ws);
         if (copy)
             cudaStreamDestroy(copy);
         if (stream)
             cudaStreamDestroy(stream);
+        if (pool)
+            cudaMemPoolDestroy(pool);
     }
     void check() const {
         if (cancelled.load())
@@ -383,7 +403,7 @@ struct Context {
         t.bf16 = bf16;
         const size_t bytes = t.bytes() ? t.bytes() : 1;
         void *p = nullptr;
-        cuda_ok(cudaMallocAsync(&p, bytes, stream), "activation allocation");
+        cuda_ok(cudaMallocFromPoolAsync(&p, bytes, pool, stream), "activation allocation");
         memory->add(bytes);
         auto mem = memory;
         cudaStream_t s = stream;
@@ -400,8 +420,66 @@ struct Context {
 };
 
 namespace {
-// y = x W^T (+ b): cuBLAS GEMM into fp32, then the bias / rounding epilogue.
-// bias_after_round: the reference's image_conv -- r(r(x W^T) + b).
+// One cuBLASLt matmul D = x W^T (+ bias in the epilogue) in the tensor's
+// own type (fp32 accumulate; bf16 results rounded once, after the bias).
+// Returns false when cuBLASLt offers no algorithm for the shape.
+bool lt_linear(Context &c, const Tensor &x, const Tensor &w, const void *bias, Tensor &y) {
+    const size_t m = x.rows, n = w.rows, k = x.cols;
+    const std::array<long long, 5> key{static_cast<long long>(m), static_cast<long long>(n),
+                                       static_cast<long long>(k), x.bf16 ? 1 : 0, bias ? 1 : 0};
+    const cudaDataType_t t = x.bf16 ? CUDA_R_16BF : CUDA_R_32F;
+    cublasLtMatmulDesc_t op = nullptr;
+    cublasLtMatrixLayout_t la = nullptr, lb = nullptr, lc = nullptr;
+    auto cleanup = [&] {
+        if (la)
+            cublasLtMatrixLayoutDestroy(la);
+        if (lb)
+            cublasLtMatrixLayoutDestroy(lb);
+        if (lc)
+            cublasLtMatrixLayoutDestroy(lc);
+        if (op)
+            cublasLtMatmulDescDestroy(op);
+    };
+    // Column-major view: D^T [n, m] = W [k, n]^T * X^T [k, m].
+    blas_ok(cublasLtMatmulDescCreate(&op, CUBLAS_COMPUTE_32F, CUDA_R_32F), "matmul desc");
+    const cublasOperation_t ta = CUBLAS_OP_T, tb = CUBLAS_OP_N;
+    cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_TRANSA, &ta, sizeof ta);
+    cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_TRANSB, &tb, sizeof tb);
+    if (bias) {
+        const cublasLtEpilogue_t ep = CUBLASLT_EPILOGUE_BIAS;
+        cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_EPILOGUE, &ep, sizeof ep);
+        cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_BIAS_POINTER, &bias, sizeof bias);
+    }
+    cublasLtMatrixLayoutCreate(&la, t, k, n, k);
+    cublasLtMatrixLayoutCreate(&lb, t, k, m, k);
+    cublasLtMatrixLayoutCreate(&lc, t, n, m, n);
+    auto it = c.lt_algos.find(key);
+    if (it == c.lt_algos.end()) {
+        cublasLtMatmulPreference_t pref = nullptr;
+        cublasLtMatmulPreferenceCreate(&pref);
+        cublasLtMatmulPreferenceSetAttribute(pref, CUBLASLT_MATMUL_PREF_MAX_WORKSPACE_BYTES, &c.lt_ws_bytes,
+                                             sizeof c.lt_ws_bytes);
+        cublasLtMatmulHeuristicResult_t res{};
+        int found = 0;
+        const cublasStatus_t st = cublasLtMatmulAlgoGetHeuristic(c.lt, op, la, lb, lc, lc, pref, 1, &res, &found);
+        cublasLtMatmulPreferenceDestroy(pref);
+        it = c.lt_algos.emplace(key, std::make_pair(st == CUBLAS_STATUS_SUCCESS && found > 0, res.algo)).first;
+    }
+    if (!it->second.first) {
+        cleanup();
+        return false;
+    }
+    const float one = 1.f, zero = 0.f;
+    const cublasStatus_t st = cublasLtMatmul(c.lt, op, &one, w.data(), la, x.data(), lb, &zero, y.data(), lc,
+                                             y.data(), lc, &it->second.second, c.lt_ws, c.lt_ws_bytes, c.stream);
+    cleanup();
+    blas_ok(st, "linear");
+    return true;
+}
+
+// y = x W^T (+ b).  bias_after_round: the reference's image_conv -- r(r(x W^T) + b).
+// cuBLASLt with the bias in its epilogue when it has an algorithm; otherwise a
+// cuBLAS GEMM into fp32 followed by the bias / rounding epilogue kernel.
 Tensor linear(Context &c, const Tensor &x, const Tensor &w, const Tensor *b,
               bool bias_after_round = false) {
     require(x.cols == w.cols, "Linear dimensions disagree", OMNI_INVALID_MODEL);
@@ -409,22 +487,25 @@ Tensor linear(Context &c, const Tensor &x, const Tensor &w, const Tensor *b,
     Tensor y = c.make(m, n, x.bf16);
     if (m == 0)
         return y;
-    Tensor acc_holder;
-    float *acc = x.bf16 ? static_cast<float *>(c.scratch(m * n * 4, acc_holder))
-                        : static_cast<float *>(y.data());
-    const float one = 1.f, zero = 0.f;
-    blas_ok(cublasGemmEx(c.blas, CUBLAS_OP_T, CUBLAS_OP_N, static_cast<int>(n), static_cast<int>(m),
-                         static_cast<int>(k), &one, w.data(), x.bf16 ? CUDA_R_16BF : CUDA_R_32F,
-                         static_cast<int>(k), x.data(), x.bf16 ? CUDA_R_16BF : CUDA_R_32F,
-                         static_cast<int>(k), &zero, acc, CUDA_R_32F, static_cast<int>(n),
-                         x.bf16 ? CUBLAS_COMPUTE_32F : CUBLAS_COMPUTE_32F_PEDANTIC,
-                         CUBLAS_GEMM_DEFAULT),
-            "linear");
     const bool fused_bias = b && !bias_after_round;
-    cuda_ok(static_cast<cudaError_t>(graph::linear_epilogue(acc, fused_bias ? b->data() : nullptr,
-                                                            b ? b->bf16 : false, y.data(), y.bf16, m,
-                                                            n, c.stream)),
-            "linear epilogue");
+    const bool lt_ok = c.lt && w.bf16 == x.bf16 && (!fused_bias || b->bf16 == x.bf16) &&
+                       lt_linear(c, x, w, fused_bias ? b->data() : nullptr, y);
+    if (!lt_ok) {
+        Tensor acc_holder;
+        float *acc = x.bf16 ? static_cast<float *>(c.scratch(m * n * 4, acc_holder))
+                            : static_cast<float *>(y.data());
+        const float one = 1.f, zero = 0.f;
+        blas_ok(cublasGemmEx(c.blas, CUBLAS_OP_T, CUBLAS_OP_N, static_cast<int>(n), static_cast<int>(m),
+                             static_cast<int>(k), &one, w.data(), x.bf16 ? CUDA_R_16BF : CUDA_R_32F,
+                             static_cast<int>(k), x.data(), x.bf16 ? CUDA_R_16BF : CUDA_R_32F,
+                             static_cast<int>(k), &zero, acc, CUDA_R_32F, static_cast<int>(n),
+                             x.bf16 ? CUBLAS_COMPUTE_32F : CUBLAS_COMPUTE_32F_PEDANTIC, CUBLAS_GEMM_DEFAULT),
+                "linear");
+        cuda_ok(static_cast<cudaError_t>(graph::linear_epilogue(acc, fused_bias ? b->data() : nullptr,
+                                                                b ? b->bf16 : false, y.data(), y.bf16, m,
+                                                                n, c.stream)),
+                "linear epilogue");
+    }
     if (b && bias_after_round)
         cuda_ok(static_cast<cudaError_t>(graph::bias(y.data(), b->data(), y.bf16, m, n, c.stream)),
                 "bias");
@@ -458,15 +539,34 @@ Tensor attention(Context &c, const Tensor &q, const Tensor *k, const Tensor *v, 
     const size_t rows = q.rows, n = rows / batch, d = fused ? q.cols / 3 : q.cols, hd = d / heads;
     Tensor y = c.make(rows, d, q.bf16);
     if (!q.bf16 && !c.audio_bf16) {
+        // fp32 profile: per item, S = scale Q K^T for all heads (one strided
+        // batched fp32 GEMM), masked softmax in place, O = P V.
         require(!fused, "fp32 fused attention is not used by the graphs", OMNI_INTERNAL_ERROR);
-        for (size_t b = 0; b < batch; ++b) {
-            const size_t off = b * n * d;
-            cuda_ok(static_cast<cudaError_t>(graph::attention_f32(
-                        static_cast<const float *>(q.data()) + off, static_cast<const float *>(k->data()) + off,
-                        static_cast<const float *>(v->data()) + off, static_cast<float *>(y.data()) + off, n,
-                        heads, hd, block, static_cast<size_t>(valid[b]), c.stream)),
-                    "attention");
-        }
+        const long long nn = static_cast<long long>(n) * n;
+        Tensor scores = c.make(batch * heads * n, n, false);
+        float *S = static_cast<float *>(scores.data());
+        const float scale = 1.f / std::sqrt(static_cast<float>(hd)), one = 1.f, zero = 0.f;
+        const float *Q = static_cast<const float *>(q.data()), *K = static_cast<const float *>(k->data()),
+                    *V = static_cast<const float *>(v->data());
+        float *O = static_cast<float *>(y.data());
+        const int ni = static_cast<int>(n), di = static_cast<int>(d), hi = static_cast<int>(hd);
+        for (size_t b = 0; b < batch; ++b)
+            blas_ok(cublasGemmStridedBatchedEx(c.blas, CUBLAS_OP_T, CUBLAS_OP_N, ni, ni, hi, &scale,
+                                               K + b * n * d, CUDA_R_32F, di, static_cast<long long>(hd),
+                                               Q + b * n * d, CUDA_R_32F, di, static_cast<long long>(hd), &zero,
+                                               S + b * heads * nn, CUDA_R_32F, ni, nn, static_cast<int>(heads),
+                                               CUBLAS_COMPUTE_32F_PEDANTIC, CUBLAS_GEMM_DEFAULT),
+                    "attention scores");
+        cuda_ok(static_cast<cudaError_t>(graph::softmax_rows(S, batch, heads, n, valid_dev,
+                                                             static_cast<size_t>(valid[0]), block, c.stream)),
+                "attention softmax");
+        for (size_t b = 0; b < batch; ++b)
+            blas_ok(cublasGemmStridedBatchedEx(c.blas, CUBLAS_OP_N, CUBLAS_OP_N, hi, ni, ni, &one, V + b * n * d,
+                                               CUDA_R_32F, di, static_cast<long long>(hd), S + b * heads * nn,
+                                               CUDA_R_32F, ni, nn, &zero, O + b * n * d, CUDA_R_32F, di,
+                                               static_cast<long long>(hd), static_cast<int>(heads),
+                                               CUBLAS_COMPUTE_32F_PEDANTIC, CUBLAS_GEMM_DEFAULT),
+                    "attention values");
         return y;
     }
     const int dt = q.bf16 ? OMNI_B200_BF16 : OMNI_B200_F32;
@@ -860,6 +960,20 @@ int omni_context_create(omni_model *m, omni_context **out) {
         omni_b200::rt::blas_ok(cublasCreate(&c->impl.blas), "cuBLAS handle");
         omni_b200::rt::blas_ok(cublasSetStream(c->impl.blas, c->impl.stream), "cuBLAS stream");
         omni_b200::rt::cuda_ok(cudaStreamCreateWithFlags(&c->impl.copy, cudaStreamNonBlocking), "stream create");
+        cudaMemPoolProps props{};
+        props.allocType = cudaMemAllocationTypePinned;
+        props.location.type = cudaMemLocationTypeDevice;
+        props.location.id = m->impl->device;
+        omni_b200::rt::cuda_ok(cudaMemPoolCreate(&c->impl.pool, &props), "memory pool");
+        uint64_t keep = ~uint64_t(0);
+        omni_b200::rt::cuda_ok(cudaMemPoolSetAttribute(c->impl.pool, cudaMemPoolAttrReleaseThreshold, &keep),
+                               "memory pool");
+        const char *lt = std::getenv("OMNI_B200_CUBLASLT");
+        if (!(lt && *lt == '0')) {
+            omni_b200::rt::blas_ok(cublasLtCreate(&c->impl.lt), "cuBLASLt handle");
+            c->impl.lt_ws_bytes = size_t(32) << 20;
+            omni_b200::rt::cuda_ok(cudaMalloc(&c->impl.lt_ws, c->impl.lt_ws_bytes), "cuBLASLt workspace");
+        }
         for (cudaEvent_t *e : {&c->impl.ready[0], &c->impl.ready[1], &c->impl.done[0], &c->impl.done[1],
                                &c->impl.start})
             omni_b200::rt::cuda_ok(cudaEventCreateWithFlags(e, cudaEventDisableTiming), "event create");
