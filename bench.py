@@ -59,10 +59,13 @@ CONFIGS = {
     "c4": dict(kind="encoder", modality="audio", items=16, mel=80, frames=3000, width=1024, layers=24, heads=16,
                ffn=4096, positions=1500, block=1500, vocab=16384, seed=1004, audio_bf16=False,
                workload="full audio encoder (BASELINE config 4 body: 24 layers, d 1024, 16 heads, ffn 4096, "
-                        "80 mel x 3000 frames; reference head: pool 4, fp32 VQ over 16384x1024)"),
+                        "80 mel x 3000 frames; reference head: pool 4, fp32 VQ over 16384x1024; the reference's "
+                        "fp32 audio profile)"),
     "c4_bf16": dict(kind="encoder", modality="audio", items=16, mel=80, frames=3000, width=1024, layers=24,
                     heads=16, ffn=4096, positions=1500, block=1500, vocab=16384, seed=1004, audio_bf16=True,
-                    workload="config 4 with OMNI_B200_AUDIO_BF16=1 (attention on the bf16 tcgen05 kernel)"),
+                    workload="full audio encoder, BASELINE config 4 precision (bf16 weights and activations, "
+                             "fp32 LayerNorm statistics): this library's OMNI_B200_AUDIO_BF16=1 mode, same shapes "
+                             "as c4"),
     # 378 = 27 x 14: the 27x27 patch grid a stride-14 conv takes from a 384x384
     # image; the reference ABI wants sides that are multiples of the patch.
     "c5": dict(kind="encoder", modality="image", items=512, size=378, patch=14, grid=27, width=1152, layers=27,
@@ -351,10 +354,19 @@ def cpu_encoder_sample(cfg, tmpdir, repeats=1):
     return per_item, O.cpu_threads(), sample
 
 
+def fp32_emulation_available():
+    """Whether the cuBLAS bound in this process offers BF16x9 fp32 emulation."""
+    import ctypes
+
+    try:
+        lib = ctypes.CDLL("libcublas.so.12", mode=os.RTLD_LAZY | os.RTLD_NOLOAD)
+    except OSError:
+        return False
+    return hasattr(lib, "cublasSetEmulationStrategy")
+
+
 def run_encoder(args, cfg, reference=False):
     import tempfile
-
-    import torch
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -388,6 +400,17 @@ def run_encoder(args, cfg, reference=False):
         print(json.dumps(line), flush=True)
         return 0
 
+    # This library loads before torch, so that its cuBLAS (the toolkit's, with
+    # fp32 emulation) is the one the process binds rather than torch's older copy.
+    if cfg.get("audio_bf16"):
+        os.environ["OMNI_B200_AUDIO_BF16"] = "1"
+    load_package()
+    import omni_tokenizer_b200.abi as abi
+
+    lib = abi.OmniLib(ROOT / "omni-tokenizer_b200" / "libomni_b200.so")
+    emulated = fp32_emulation_available() and os.environ.get("OMNI_B200_FP32_EMULATION", "") != "0"
+    import torch
+
     torch.cuda.set_device(local)
     dist = None
     if world > 1:
@@ -397,12 +420,6 @@ def run_encoder(args, cfg, reference=False):
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                 device_id=torch.device("cuda", local))
-    if cfg.get("audio_bf16"):
-        os.environ["OMNI_B200_AUDIO_BF16"] = "1"
-    load_package()
-    import omni_tokenizer_b200.abi as abi
-
-    lib = abi.OmniLib(ROOT / "omni-tokenizer_b200" / "libomni_b200.so")
     # Every rank writes the same seeded model into its own temporary directory
     # (no shared filesystem is assumed between ranks).
     ov, mc = encoder_model_config(cfg)
@@ -436,21 +453,6 @@ def run_encoder(args, cfg, reference=False):
         session = model.context()
         for _ in range(max(args.warmup, 3)):
             encode_batch(session, cfg, host, dev)
-        # Kernel launches of one step, by name, through the profiler (untimed).
-        launches_step, library_launches = None, None
-        try:
-            from torch.profiler import ProfilerActivity, profile
-
-            with profile(activities=[ProfilerActivity.CUDA]) as prof:
-                encode_batch(session, cfg, host, dev)
-                torch.cuda.synchronize()
-            names = [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA
-                     and "memcpy" not in e.name.lower() and "memset" not in e.name.lower()]
-            lib_like = ("gemm", "cutlass", "cublas", "nvjet", "xmma", "splitk", "reduce_1block")
-            library_launches = sum(1 for n in names if any(k in n.lower() for k in lib_like))
-            launches_step = len(names) - library_launches
-        except Exception:
-            pass
         sampler = ClockSampler(local)
         sampler.start()
         t_clock0 = time.perf_counter()
@@ -464,6 +466,22 @@ def run_encoder(args, cfg, reference=False):
         # The reference's single-item calls on a sample of the rank's items.
         sample = min(mine, 16 if cfg["modality"] == "image" else 4)
         item_elapsed, _ = timed(lambda: np.concatenate([encode_item(session, cfg, x) for x in host[:sample]]), 1)
+        # Kernel launches of one step, by name, through the profiler -- after the
+        # timed regions: an attached profiler slows every later launch.
+        launches_step, library_launches = None, None
+        try:
+            from torch.profiler import ProfilerActivity, profile
+
+            with profile(activities=[ProfilerActivity.CUDA]) as prof:
+                encode_batch(session, cfg, host, dev)
+                torch.cuda.synchronize()
+            names = [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA
+                     and "memcpy" not in e.name.lower() and "memset" not in e.name.lower()]
+            lib_like = ("gemm", "cutlass", "cublas", "nvjet", "xmma", "splitk", "reduce_1block", "inf_patching")
+            library_launches = sum(1 for n in names if any(k in n.lower() for k in lib_like))
+            launches_step = len(names) - library_launches
+        except Exception:
+            pass
         peak_ws = session.peak_workspace
         session.close()
     clocks = sampler.summary(t_clock0, t_clock1)
@@ -516,6 +534,8 @@ def run_encoder(args, cfg, reference=False):
                 "per_item_abi": {"value": per_item_value, "unit": unit_name, "items": sample,
                                  "call": "omni_encode_" + cfg["modality"] + " (the reference's single-item call, "
                                          "host buffers)"},
+                "fp32_gemms": ("BF16x9-emulated fp32 (cuBLAS)" if emulated else "fp32 on the CUDA cores")
+                              if cfg["modality"] == "audio" and not cfg.get("audio_bf16") else None,
                 "l2": "weights and activations far above L2 size per step; no flush",
                 "model_write_s": round(t_write, 1),
                 "peak_workspace_bytes": peak_ws,

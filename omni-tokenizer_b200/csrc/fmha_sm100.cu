@@ -1146,12 +1146,9 @@ int padded_head_dim(int hd) {
 
 template <int HDP, bool BF16> int launch_typed(FmhaParams &p, int grid, cudaStream_t stream) {
     using S = FmhaShape<HDP>;
-    static std::once_flag once;
-    static cudaError_t attr = cudaSuccess;
-    std::call_once(once, [] {
-        attr = cudaFuncSetAttribute(fmha_fwd_kernel<HDP, BF16>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM_BYTES);
-    });
+    static std::atomic<unsigned long long> done{0};
+    const cudaError_t attr =
+        set_smem_limit(reinterpret_cast<const void *>(fmha_fwd_kernel<HDP, BF16>), S::SMEM_BYTES, done);
     if (attr != cudaSuccess)
         return static_cast<int>(attr);
     fmha_fwd_kernel<HDP, BF16><<<grid, kThreads, S::SMEM_BYTES, stream>>>(p);

@@ -39,6 +39,148 @@ int status() { return static_cast<int>(cudaGetLastError()); }
     for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < (n);         \
          i += static_cast<size_t>(gridDim.x) * blockDim.x)
 
+// 16-byte vectors: 8 bf16 or 4 fp32 values.
+template <bool BF16> constexpr int kVec = BF16 ? 8 : 4;
+
+template <bool BF16> __device__ __forceinline__ void vload(const void *p, size_t i, float *v) {
+    const uint4 u = *reinterpret_cast<const uint4 *>(static_cast<const char *>(p) + i * (BF16 ? 2 : 4));
+    if constexpr (BF16) {
+        const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&u);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float2 f = __bfloat1622float2(h[k]);
+            v[2 * k] = f.x;
+            v[2 * k + 1] = f.y;
+        }
+    } else {
+        v[0] = __uint_as_float(u.x);
+        v[1] = __uint_as_float(u.y);
+        v[2] = __uint_as_float(u.z);
+        v[3] = __uint_as_float(u.w);
+    }
+}
+
+template <bool BF16> __device__ __forceinline__ void vstore(void *p, size_t i, const float *v) {
+    uint4 u;
+    if constexpr (BF16) {
+        __nv_bfloat162 *h = reinterpret_cast<__nv_bfloat162 *>(&u);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            h[k] = __floats2bfloat162_rn(v[2 * k], v[2 * k + 1]);
+    } else {
+        u = make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]), __float_as_uint(v[2]), __float_as_uint(v[3]));
+    }
+    *reinterpret_cast<uint4 *>(static_cast<char *>(p) + i * (BF16 ? 2 : 4)) = u;
+}
+
+__device__ __forceinline__ float gelu_erf(float z) {
+    return __fmul_rn(__fmul_rn(0.5f, z), __fadd_rn(1.f, erff(__fmul_rn(z, 0.7071067811865475244f))));
+}
+
+template <bool BF16> __global__ void k_gelu_vec(void *x, size_t nvec) {
+    constexpr int N = kVec<BF16>;
+    GRID_STRIDE(i, nvec) {
+        float v[N];
+        vload<BF16>(x, i * N, v);
+#pragma unroll
+        for (int k = 0; k < N; ++k)
+            v[k] = gelu_erf(v[k]);
+        vstore<BF16>(x, i * N, v);
+    }
+}
+
+template <bool BF16> __global__ void k_add_vec(void *x, const void *y, size_t nvec) {
+    constexpr int N = kVec<BF16>;
+    GRID_STRIDE(i, nvec) {
+        float a[N], b[N];
+        vload<BF16>(x, i * N, a);
+        vload<BF16>(y, i * N, b);
+#pragma unroll
+        for (int k = 0; k < N; ++k)
+            a[k] = __fadd_rn(a[k], b[k]);
+        vstore<BF16>(x, i * N, a);
+    }
+}
+
+// x[r, c] = r(x[r, c] + b[c]) over whole vectors (cols % vector == 0).
+template <bool BF16> __global__ void k_bias_vec(void *x, const void *b, size_t nvec, size_t cols) {
+    constexpr int N = kVec<BF16>;
+    GRID_STRIDE(i, nvec) {
+        float a[N], c[N];
+        vload<BF16>(x, i * N, a);
+        vload<BF16>(b, (i * N) % cols, c);
+#pragma unroll
+        for (int k = 0; k < N; ++k)
+            a[k] = __fadd_rn(a[k], c[k]);
+        vstore<BF16>(x, i * N, a);
+    }
+}
+
+// One warp per row, the row in registers (VPL vectors per lane): optionally
+// x = r(x + z) written back (the residual), then y = r(((x - mean) inv) w + b)
+// with mean and var as the reference's norm (fp32, biased variance).
+template <bool BF16, int VPL>
+__global__ void k_add_norm(void *x, const void *z, const void *w, const void *b, void *y, size_t rows, int cols,
+                           float eps) {
+    constexpr int N = kVec<BF16>;
+    const size_t row = static_cast<size_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= rows)
+        return;
+    const size_t base = row * static_cast<size_t>(cols);
+    float v[VPL][N];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+        const int c = (i * 32 + lane) * N;
+        if (c < cols) {
+            vload<BF16>(x, base + c, v[i]);
+            if (z) {
+                float t[N];
+                vload<BF16>(z, base + c, t);
+#pragma unroll
+                for (int k = 0; k < N; ++k)
+                    v[i][k] = rnd(__fadd_rn(v[i][k], t[k]), BF16);
+                vstore<BF16>(x, base + c, v[i]);
+            }
+#pragma unroll
+            for (int k = 0; k < N; ++k)
+                s = __fadd_rn(s, v[i][k]);
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1)
+        s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+    const float mean = s / static_cast<float>(cols);
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+        const int c = (i * 32 + lane) * N;
+        if (c < cols) {
+#pragma unroll
+            for (int k = 0; k < N; ++k) {
+                const float d = __fsub_rn(v[i][k], mean);
+                q = __fadd_rn(q, __fmul_rn(d, d));
+            }
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1)
+        q = __fadd_rn(q, __shfl_xor_sync(0xffffffffu, q, o));
+    const float inv = 1.f / sqrtf(q / static_cast<float>(cols) + eps);
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+        const int c = (i * 32 + lane) * N;
+        if (c < cols) {
+            float wv[N], bv[N];
+            vload<BF16>(w, c, wv);
+            vload<BF16>(b, c, bv);
+#pragma unroll
+            for (int k = 0; k < N; ++k)
+                v[i][k] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[i][k], mean), inv), wv[k]), bv[k]);
+            vstore<BF16>(y, base + c, v[i]);
+        }
+    }
+}
+
 __global__ void k_linear_epilogue(const float *acc, const void *b, bool bbf16, void *y, bool bf16,
                                   size_t rows, size_t cols) {
     GRID_STRIDE(i, rows * cols) {
@@ -92,9 +234,7 @@ __global__ void k_layer_norm(const void *x, const void *w, const void *b, void *
 
 __global__ void k_gelu(void *x, bool bf16, size_t n) {
     GRID_STRIDE(i, n) {
-        const float z = ld(x, i, bf16);
-        st(x, i, __fmul_rn(__fmul_rn(0.5f, z), __fadd_rn(1.f, erff(__fmul_rn(z, 0.7071067811865475244f)))),
-           bf16);
+        st(x, i, gelu_erf(ld(x, i, bf16)), bf16);
     }
 }
 
@@ -265,8 +405,18 @@ __global__ void k_softmax_rows(float *s, size_t items, size_t heads, size_t n, c
 
 } // namespace
 
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+int bias(void *x, const void *b, bool bf16, size_t rows, size_t cols, cudaStream_t s);
+
 int linear_epilogue(const float *acc, const void *b, bool bbf16, void *y, bool bf16, size_t rows,
                     size_t cols, cudaStream_t s) {
+    if (static_cast<const void *>(acc) == y && !bf16) { // fp32 in place: only the bias
+        if (!b)
+            return 0;
+        if (!bbf16)
+            return bias(y, b, false, rows, cols, s);
+    }
     k_linear_epilogue<<<blocks_for(rows * cols, 256), 256, 0, s>>>(acc, b, bbf16, y, bf16, rows, cols);
     return status();
 }
@@ -277,15 +427,94 @@ int layer_norm(const void *x, const void *w, const void *b, void *y, bool bf16, 
     return status();
 }
 int gelu(void *x, bool bf16, size_t n, cudaStream_t s) {
-    k_gelu<<<blocks_for(n, 256), 256, 0, s>>>(x, bf16, n);
+    const size_t N = bf16 ? 8 : 4, nvec = aligned16(x) ? n / N : 0, done = nvec * N;
+    if (nvec) {
+        if (bf16)
+            k_gelu_vec<true><<<blocks_for(nvec, 256), 256, 0, s>>>(x, nvec);
+        else
+            k_gelu_vec<false><<<blocks_for(nvec, 256), 256, 0, s>>>(x, nvec);
+    }
+    if (done < n)
+        k_gelu<<<blocks_for(n - done, 256), 256, 0, s>>>(static_cast<char *>(x) + done * (bf16 ? 2 : 4), bf16,
+                                                         n - done);
     return status();
 }
 int add(void *x, const void *y, bool bf16, size_t n, cudaStream_t s) {
-    k_add<<<blocks_for(n, 256), 256, 0, s>>>(x, y, bf16, n);
+    const size_t N = bf16 ? 8 : 4, nvec = aligned16(x) && aligned16(y) ? n / N : 0, done = nvec * N;
+    const size_t es = bf16 ? 2 : 4;
+    if (nvec) {
+        if (bf16)
+            k_add_vec<true><<<blocks_for(nvec, 256), 256, 0, s>>>(x, y, nvec);
+        else
+            k_add_vec<false><<<blocks_for(nvec, 256), 256, 0, s>>>(x, y, nvec);
+    }
+    if (done < n)
+        k_add<<<blocks_for(n - done, 256), 256, 0, s>>>(static_cast<char *>(x) + done * es,
+                                                        static_cast<const char *>(y) + done * es, bf16, n - done);
     return status();
 }
+
+namespace {
+template <bool BF16, int VPL>
+void launch_add_norm(void *x, const void *z, const void *w, const void *b, void *y, size_t rows, size_t cols,
+                     float eps, cudaStream_t s) {
+    constexpr int kRows = 8; // warps (rows) per block
+    k_add_norm<BF16, VPL><<<static_cast<unsigned>((rows + kRows - 1) / kRows), kRows * 32, 0, s>>>(
+        x, z, w, b, y, rows, static_cast<int>(cols), eps);
+}
+template <bool BF16>
+bool add_norm_vec(void *x, const void *z, const void *w, const void *b, void *y, size_t rows, size_t cols,
+                  float eps, cudaStream_t s) {
+    const size_t per = 32 * static_cast<size_t>(kVec<BF16>), need = (cols + per - 1) / per;
+    if (need <= 1)
+        launch_add_norm<BF16, 1>(x, z, w, b, y, rows, cols, eps, s);
+    else if (need <= 2)
+        launch_add_norm<BF16, 2>(x, z, w, b, y, rows, cols, eps, s);
+    else if (need <= 4)
+        launch_add_norm<BF16, 4>(x, z, w, b, y, rows, cols, eps, s);
+    else if (need <= 6)
+        launch_add_norm<BF16, 6>(x, z, w, b, y, rows, cols, eps, s);
+    else if (need <= 8)
+        launch_add_norm<BF16, 8>(x, z, w, b, y, rows, cols, eps, s);
+    else if (need <= 12)
+        launch_add_norm<BF16, 12>(x, z, w, b, y, rows, cols, eps, s);
+    else if (need <= 16)
+        launch_add_norm<BF16, 16>(x, z, w, b, y, rows, cols, eps, s);
+    else
+        return false;
+    return true;
+}
+} // namespace
+
+int add_layer_norm(void *x, const void *z, const void *w, const void *b, void *y, bool bf16, size_t rows,
+                   size_t cols, float eps, cudaStream_t s) {
+    if (rows == 0)
+        return 0;
+    const size_t N = bf16 ? 8 : 4;
+    const bool vec = cols % N == 0 && aligned16(x) && (!z || aligned16(z)) && aligned16(w) && aligned16(b) &&
+                     aligned16(y);
+    if (vec && (bf16 ? add_norm_vec<true>(x, z, w, b, y, rows, cols, eps, s)
+                     : add_norm_vec<false>(x, z, w, b, y, rows, cols, eps, s)))
+        return status();
+    if (z) {
+        const int rc = add(x, z, bf16, rows * cols, s);
+        if (rc)
+            return rc;
+    }
+    return layer_norm(x, w, b, y, bf16, rows, cols, eps, s);
+}
 int bias(void *x, const void *b, bool bf16, size_t rows, size_t cols, cudaStream_t s) {
-    k_bias<<<blocks_for(rows * cols, 256), 256, 0, s>>>(x, b, bf16, rows, cols);
+    const size_t N = bf16 ? 8 : 4, n = rows * cols;
+    if (cols % N == 0 && aligned16(x) && aligned16(b)) {
+        if (n) {
+            if (bf16)
+                k_bias_vec<true><<<blocks_for(n / N, 256), 256, 0, s>>>(x, b, n / N, cols);
+            else
+                k_bias_vec<false><<<blocks_for(n / N, 256), 256, 0, s>>>(x, b, n / N, cols);
+        }
+        return status();
+    }
+    k_bias<<<blocks_for(n, 256), 256, 0, s>>>(x, b, bf16, rows, cols);
     return status();
 }
 int conv_gather(const void *x, void *y, bool bf16, size_t segments, size_t rows, size_t cols,

@@ -19,6 +19,10 @@ int linear_epilogue(const float *acc, const void *bias, bool bias_bf16, void *y,
 // Layer norm over each row: r((x - mean) * inv * w + b), inv = 1/sqrt(var + eps).
 int layer_norm(const void *x, const void *w, const void *b, void *y, bool bf16, size_t rows,
                size_t cols, float eps, cudaStream_t s);
+// x = r(x + z) in place when z is given, then y = layer norm of x (as above):
+// one warp per row with the row in registers (rows up to 2048 columns).
+int add_layer_norm(void *x, const void *z, const void *w, const void *b, void *y, bool bf16, size_t rows,
+                   size_t cols, float eps, cudaStream_t s);
 // In place: x = r(0.5 x (1 + erf(x / sqrt 2))).
 int gelu(void *x, bool bf16, size_t n, cudaStream_t s);
 // In place: x = r(x + y) over the first n elements.

@@ -12,8 +12,10 @@
 // followed by the bias / bf16-rounding epilogue; the remaining operators are
 // graph_kernels.cu.  Audio-profile attention stays fp32 (the reference's audio
 // kernels are fp32-accurate 3xTF32): fp32 cuBLAS GEMMs for the scores and the
-// weighted values around a masked-softmax kernel; setting
-// OMNI_B200_AUDIO_BF16=1 routes it through the bf16 tcgen05 kernel instead.
+// weighted values around a masked-softmax kernel.  OMNI_B200_AUDIO_BF16=1
+// selects this library's bf16 audio mode instead: bf16 weights (converted once
+// per model) and activations with the reference's bf16 rounding points, the
+// tcgen05 attention kernel, fp32 VQ.
 #include "fmha.h"
 #include "graph_kernels.h"
 #include "omni_abi.h"
@@ -28,7 +30,9 @@
 #include <cublasLt.h>
 #include <cublas_v2.h>
 #include <map>
+#include <mutex>
 #include <cuda_runtime.h>
+#include <dlfcn.h>
 #include <fstream>
 #include <limits>
 #include <memory>
@@ -121,6 +125,23 @@ struct Model {
     const Tensor *opt(const std::string &name) const {
         auto it = w.find(name);
         return it == w.end() ? nullptr : &it->second;
+    }
+    // bf16 copies of an fp32 (audio) model's tensors for the bf16 audio mode,
+    // made once, by the first context that asks for them (all but the codebook).
+    std::unordered_map<std::string, Tensor> w16;
+    std::once_flag w16_once;
+    const Tensor &get(const std::string &name, bool bf16) const {
+        if (!bf16)
+            return get(name);
+        auto it = w16.find(name);
+        require(it != w16.end(), "Missing tensor: " + name, OMNI_INVALID_MODEL);
+        return it->second;
+    }
+    const Tensor *opt(const std::string &name, bool bf16) const {
+        if (!bf16)
+            return opt(name);
+        auto it = w16.find(name);
+        return it == w16.end() ? nullptr : &it->second;
     }
 };
 
@@ -356,6 +377,12 @@ struct Context {
     omni_trace_callback trace = nullptr;
     void *trace_user = nullptr;
     bool audio_bf16 = false;
+    // fp32-profile GEMMs through cuBLAS's BF16x9 emulation of fp32 on the tensor
+    // cores instead of fp32 on the CUDA cores.
+    bool fp32_emulated = false;
+    cublasComputeType_t fp32_compute() const {
+        return fp32_emulated ? CUBLAS_COMPUTE_32F_EMULATED_16BFX9 : CUBLAS_COMPUTE_32F_PEDANTIC;
+    }
     // Host inputs are copied on `copy` into two staging buffers (events
     // ready[i] / done[i]), overlapping the graph of the previous chunk.
     cudaStream_t copy = nullptr;
@@ -489,7 +516,7 @@ Tensor linear(Context &c, const Tensor &x, const Tensor &w, const Tensor *b,
         return y;
     const bool fused_bias = b && !bias_after_round;
     const bool lt_ok = c.lt && w.bf16 == x.bf16 && (!fused_bias || b->bf16 == x.bf16) &&
-                       lt_linear(c, x, w, fused_bias ? b->data() : nullptr, y);
+                       (x.bf16 || !c.fp32_emulated) && lt_linear(c, x, w, fused_bias ? b->data() : nullptr, y);
     if (!lt_ok) {
         Tensor acc_holder;
         float *acc = x.bf16 ? static_cast<float *>(c.scratch(m * n * 4, acc_holder))
@@ -499,7 +526,7 @@ Tensor linear(Context &c, const Tensor &x, const Tensor &w, const Tensor *b,
                              static_cast<int>(k), &one, w.data(), x.bf16 ? CUDA_R_16BF : CUDA_R_32F,
                              static_cast<int>(k), x.data(), x.bf16 ? CUDA_R_16BF : CUDA_R_32F,
                              static_cast<int>(k), &zero, acc, CUDA_R_32F, static_cast<int>(n),
-                             x.bf16 ? CUBLAS_COMPUTE_32F : CUBLAS_COMPUTE_32F_PEDANTIC, CUBLAS_GEMM_DEFAULT),
+                             x.bf16 ? CUBLAS_COMPUTE_32F : c.fp32_compute(), CUBLAS_GEMM_DEFAULT),
                 "linear");
         cuda_ok(static_cast<cudaError_t>(graph::linear_epilogue(acc, fused_bias ? b->data() : nullptr,
                                                                 b ? b->bf16 : false, y.data(), y.bf16, m,
@@ -512,10 +539,13 @@ Tensor linear(Context &c, const Tensor &x, const Tensor &w, const Tensor *b,
     return y;
 }
 
-Tensor layer_norm(Context &c, const Tensor &x, const Tensor &w, const Tensor &b, float eps) {
+// x = r(x + z) in place (when z is given; the residual), then the layer norm of x.
+Tensor add_norm(Context &c, Tensor &x, const Tensor *z, const Tensor &w, const Tensor &b, float eps) {
+    require(!z || (z->cols == x.cols && z->rows >= x.rows && z->bf16 == x.bf16), "Residual dimensions disagree",
+            OMNI_INTERNAL_ERROR);
     Tensor y = c.make(x.rows, x.cols, x.bf16);
-    cuda_ok(static_cast<cudaError_t>(graph::layer_norm(x.data(), w.data(), b.data(), y.data(), x.bf16,
-                                                       x.rows, x.cols, eps, c.stream)),
+    cuda_ok(static_cast<cudaError_t>(graph::add_layer_norm(x.data(), z ? z->data() : nullptr, w.data(), b.data(),
+                                                           y.data(), x.bf16, x.rows, x.cols, eps, c.stream)),
             "layer norm");
     return y;
 }
@@ -555,7 +585,7 @@ Tensor attention(Context &c, const Tensor &q, const Tensor *k, const Tensor *v, 
                                                K + b * n * d, CUDA_R_32F, di, static_cast<long long>(hd),
                                                Q + b * n * d, CUDA_R_32F, di, static_cast<long long>(hd), &zero,
                                                S + b * heads * nn, CUDA_R_32F, ni, nn, static_cast<int>(heads),
-                                               CUBLAS_COMPUTE_32F_PEDANTIC, CUBLAS_GEMM_DEFAULT),
+                                               c.fp32_compute(), CUBLAS_GEMM_DEFAULT),
                     "attention scores");
         cuda_ok(static_cast<cudaError_t>(graph::softmax_rows(S, batch, heads, n, valid_dev,
                                                              static_cast<size_t>(valid[0]), block, c.stream)),
@@ -565,7 +595,7 @@ Tensor attention(Context &c, const Tensor &q, const Tensor *k, const Tensor *v, 
                                                CUDA_R_32F, di, static_cast<long long>(hd), S + b * heads * nn,
                                                CUDA_R_32F, ni, nn, &zero, O + b * n * d, CUDA_R_32F, di,
                                                static_cast<long long>(hd), static_cast<int>(heads),
-                                               CUBLAS_COMPUTE_32F_PEDANTIC, CUBLAS_GEMM_DEFAULT),
+                                               c.fp32_compute(), CUBLAS_GEMM_DEFAULT),
                     "attention values");
         return y;
     }
@@ -710,16 +740,34 @@ void finite_or_fail(Context &c, const Tensor &flag) {
 // ceil(valid[i] / 8), concatenated in segment order.
 std::vector<uint16_t> encode_audio_batch(Context &c, const float *mel, size_t count, uint32_t frames,
                                          const uint32_t *valid) {
-    const Model &m = *c.model;
+    Model &model = *c.model;
+    const Model &m = model;
     const Config &cfg = m.cfg;
     c.check();
+    // bf16 audio mode (OMNI_B200_AUDIO_BF16=1): weights and activations in bf16
+    // with the reference's bf16 rounding points (as its image graph); the VQ
+    // stays fp32, on the bf16 features, against the fp32 codebook.
+    const bool bf = c.audio_bf16;
+    if (bf)
+        std::call_once(model.w16_once, [&] {
+            for (const auto &kv : model.w) {
+                if (kv.first == "codebook.weight" || kv.second.bf16)
+                    continue;
+                Tensor t = weight_tensor(kv.second.rows, kv.second.cols, true);
+                cuda_ok(static_cast<cudaError_t>(graph::convert(static_cast<const float *>(kv.second.data()),
+                                                                t.data(), true, t.size(), c.stream)),
+                        "bf16 weights");
+                model.w16.emplace(kv.first, std::move(t));
+            }
+            cuda_ok(cudaStreamSynchronize(c.stream), "bf16 weights");
+        });
     const size_t C = cfg.input_channels, T = frames, L = (T + 1) / 2, W = cfg.width;
     std::vector<size_t> offset(count + 1, 0);
     for (size_t i = 0; i < count; ++i)
         offset[i + 1] = offset[i] + (valid[i] + 7) / 8;
     Tensor flag = c.make(1, 1, false);
     cuda_ok(cudaMemsetAsync(flag.data(), 0, 4, c.stream), "input check");
-    Tensor features = c.make(offset[count], W, false);
+    Tensor features = c.make(offset[count], W, bf);
     std::vector<int> keys(count);
     for (size_t i = 0; i < count; ++i)
         keys[i] = static_cast<int>((valid[i] + 1) / 2);
@@ -732,19 +780,27 @@ std::vector<uint16_t> encode_audio_batch(Context &c, const float *mel, size_t co
         cuda_ok(static_cast<cudaError_t>(graph::frames_major(src, static_cast<float *>(x.data()), items, C, T,
                                                              c.stream)),
                 "frames");
+        if (bf) {
+            Tensor x16 = c.make(items * T, C, true);
+            cuda_ok(static_cast<cudaError_t>(graph::convert(static_cast<const float *>(x.data()), x16.data(), true,
+                                                            x.size(), c.stream)),
+                    "frames");
+            x = x16;
+        }
         auto conv = [&](const Tensor &in, size_t rows, size_t stride, const char *name) {
             const size_t out_rows = (rows + stride - 1) / stride;
             Tensor g = c.make(items * out_rows, in.cols * 3, in.bf16);
             cuda_ok(static_cast<cudaError_t>(graph::conv_gather(in.data(), g.data(), in.bf16, items, rows,
                                                                 in.cols, stride, c.stream)),
                     "conv gather");
-            Tensor y = linear(c, g, m.get(std::string(name) + ".weight"), m.opt(std::string(name) + ".bias"));
+            Tensor y = linear(c, g, m.get(std::string(name) + ".weight", bf),
+                              m.opt(std::string(name) + ".bias", bf));
             gelu_in_place(c, y);
             return y;
         };
         x = conv(x, T, 1, "conv1");
         x = conv(x, T, 2, "conv2");
-        const Tensor &pos = m.get("embed_positions.weight");
+        const Tensor &pos = m.get("embed_positions.weight", bf);
         cuda_ok(static_cast<cudaError_t>(graph::add_periodic(x.data(), pos.data(), x.bf16, x.size(), L * W,
                                                              c.stream)),
                 "positions");
@@ -753,26 +809,34 @@ std::vector<uint16_t> encode_audio_batch(Context &c, const float *mel, size_t co
         Tensor keys_dev = c.make(items, 1, false);
         cuda_ok(cudaMemcpyAsync(keys_dev.data(), chunk_keys.data(), items * 4, cudaMemcpyHostToDevice, c.stream),
                 "key counts");
+        // Each residual add runs fused with the layer norm that follows it; the
+        // MLP output `mlp` of layer i joins x at the start of layer i + 1.
+        Tensor mlp;
         for (uint32_t i = 0; i < cfg.layers; ++i) {
             c.check();
             const std::string p = "layers." + std::to_string(i) + ".";
-            Tensor z = layer_norm(c, x, m.get(p + "self_attn_layer_norm.weight"),
-                                  m.get(p + "self_attn_layer_norm.bias"), 1e-5f);
+            Tensor z = add_norm(c, x, i ? &mlp : nullptr, m.get(p + "self_attn_layer_norm.weight", bf),
+                                m.get(p + "self_attn_layer_norm.bias", bf), 1e-5f);
+            if (i)
+                trace(c, x, "layer." + std::to_string(i - 1));
             auto proj = [&](const Tensor &in, const std::string &name) {
-                return linear(c, in, m.get(name + ".weight"), m.opt(name + ".bias"));
+                return linear(c, in, m.get(name + ".weight", bf), m.opt(name + ".bias", bf));
             };
             Tensor q = proj(z, p + "self_attn.q_proj"), k = proj(z, p + "self_attn.k_proj"),
                    v = proj(z, p + "self_attn.v_proj");
             z = attention(c, q, &k, &v, cfg.heads, cfg.block_size, false, items, chunk_keys,
                           static_cast<const int *>(keys_dev.data()));
+            q = {}, k = {}, v = {};
             z = proj(z, p + "self_attn.out_proj");
-            add_in_place(c, x, z);
-            z = layer_norm(c, x, m.get(p + "final_layer_norm.weight"), m.get(p + "final_layer_norm.bias"), 1e-5f);
+            z = add_norm(c, x, &z, m.get(p + "final_layer_norm.weight", bf), m.get(p + "final_layer_norm.bias", bf),
+                         1e-5f);
             z = proj(z, p + "fc1");
             gelu_in_place(c, z);
-            z = proj(z, p + "fc2");
-            add_in_place(c, x, z);
-            trace(c, x, "layer." + std::to_string(i));
+            mlp = proj(z, p + "fc2");
+        }
+        if (cfg.layers) {
+            add_in_place(c, x, mlp);
+            trace(c, x, "layer." + std::to_string(cfg.layers - 1));
         }
         c.check();
         const size_t pooled_rows = (L + cfg.pool_size - 1) / cfg.pool_size;
@@ -782,14 +846,22 @@ std::vector<uint16_t> encode_audio_batch(Context &c, const float *mel, size_t co
                 "pool");
         // pool over the stacked rows equals pool per segment: L is a multiple of
         // the pool size (frames % 8 == 0), so no group straddles two segments.
+        const size_t es = bf ? 2 : 4;
         for (size_t b = 0; b < items; ++b) {
             const size_t rows = offset[i0 + b + 1] - offset[i0 + b];
-            cuda_ok(cudaMemcpyAsync(static_cast<float *>(features.data()) + offset[i0 + b] * W,
-                                    static_cast<const float *>(pooled.data()) + b * pooled_rows * W,
-                                    rows * W * 4, cudaMemcpyDeviceToDevice, c.stream),
+            cuda_ok(cudaMemcpyAsync(static_cast<char *>(features.data()) + offset[i0 + b] * W * es,
+                                    static_cast<const char *>(pooled.data()) + b * pooled_rows * W * es,
+                                    rows * W * es, cudaMemcpyDeviceToDevice, c.stream),
                     "features");
         }
     });
+    if (bf) { // fp32 VQ on the bf16 features
+        Tensor f32 = c.make(features.rows, features.cols, false);
+        cuda_ok(static_cast<cudaError_t>(graph::to_float(features.data(), static_cast<float *>(f32.data()), true,
+                                                         features.size(), c.stream)),
+                "features");
+        features = f32;
+    }
     auto ids = quantize(c, features, m.get("codebook.weight"), m.cbnorm);
     finite_or_fail(c, flag);
     c.features = features;
@@ -833,13 +905,17 @@ std::vector<uint16_t> encode_images(Context &c, const float *pixels, size_t coun
                                                              c.stream)),
                 "positions");
         trace(c, x, "embedding");
+        // Residual adds fused with the following norm, as in the audio graph.
+        Tensor mlp;
         for (uint32_t i = 0; i < cfg.layers; ++i) {
             c.check();
             const std::string p = "blocks." + std::to_string(i) + ".";
             auto proj = [&](const Tensor &in, const std::string &name) {
                 return linear(c, in, m.get(name + ".weight"), m.opt(name + ".bias"));
             };
-            Tensor z = layer_norm(c, x, m.get(p + "norm1.weight"), m.get(p + "norm1.bias"), 1e-6f);
+            Tensor z = add_norm(c, x, i ? &mlp : nullptr, m.get(p + "norm1.weight"), m.get(p + "norm1.bias"), 1e-6f);
+            if (i)
+                trace(c, x, "layer." + std::to_string(i - 1));
             if (i == 0)
                 trace(c, z, "norm1.0");
             z = proj(z, p + "attn.qkv");
@@ -849,21 +925,22 @@ std::vector<uint16_t> encode_images(Context &c, const float *pixels, size_t coun
             if (i == 0)
                 trace(c, z, "attention.0");
             z = proj(z, p + "attn.proj");
-            add_in_place(c, x, z);
+            z = add_norm(c, x, &z, m.get(p + "norm2.weight"), m.get(p + "norm2.bias"), 1e-6f);
             if (i == 0)
                 trace(c, x, "residual1.0");
-            z = layer_norm(c, x, m.get(p + "norm2.weight"), m.get(p + "norm2.bias"), 1e-6f);
             z = proj(z, p + "mlp.fc1");
             if (i == 0)
                 trace(c, z, "fc1.0");
             gelu_in_place(c, z);
             if (i == 0)
                 trace(c, z, "gelu.0");
-            z = proj(z, p + "mlp.fc2");
+            mlp = proj(z, p + "mlp.fc2");
             if (i == 0)
-                trace(c, z, "fc2.0");
-            add_in_place(c, x, z);
-            trace(c, x, "layer." + std::to_string(i));
+                trace(c, mlp, "fc2.0");
+        }
+        if (cfg.layers) {
+            add_in_place(c, x, mlp);
+            trace(c, x, "layer." + std::to_string(cfg.layers - 1));
         }
         c.check();
         x = linear(c, x, m.get("quant_conv.weight"), &m.get("quant_conv.bias"), true);
@@ -979,6 +1056,24 @@ int omni_context_create(omni_model *m, omni_context **out) {
             omni_b200::rt::cuda_ok(cudaEventCreateWithFlags(e, cudaEventDisableTiming), "event create");
         const char *fast = std::getenv("OMNI_B200_AUDIO_BF16");
         c->impl.audio_bf16 = fast && *fast && *fast != '0';
+        // fp32-profile GEMMs: BF16x9 emulation when the process's cuBLAS has it
+        // (resolved at run time: a process may have loaded an older cuBLAS 12,
+        // same soname, before this library).  OMNI_B200_FP32_EMULATION=0 keeps
+        // plain fp32; =1 requires the emulation.
+        const char *emu = std::getenv("OMNI_B200_FP32_EMULATION");
+        const bool off = emu && *emu == '0', required = emu && *emu && *emu != '0';
+        using SetStrategy = cublasStatus_t (*)(cublasHandle_t, cublasEmulationStrategy_t);
+        SetStrategy set = nullptr;
+        if (void *h = dlopen("libcublas.so.12", RTLD_LAZY | RTLD_NOLOAD)) { // the copy already bound
+            set = reinterpret_cast<SetStrategy>(dlsym(h, "cublasSetEmulationStrategy"));
+            dlclose(h);
+        }
+        require(set != nullptr || !required, "OMNI_B200_FP32_EMULATION needs cuBLAS 12.9 or newer in this process",
+                OMNI_UNSUPPORTED);
+        if (set && !off) {
+            omni_b200::rt::blas_ok(set(c->impl.blas, CUBLAS_EMULATION_STRATEGY_EAGER), "cuBLAS emulation strategy");
+            c->impl.fp32_emulated = true;
+        }
         *out = c.release();
     });
 }

@@ -16,6 +16,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 namespace omni_b200 {
 
 // Error codes written to the per-device error word when a bounded wait gives up.
@@ -326,6 +328,23 @@ __device__ __forceinline__ float ex2_approx(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+// Raises a kernel's dynamic shared-memory limit on the current device.  The
+// attribute belongs to the device's copy of the kernel, so it is set once per
+// device; `done` is the call site's bit mask of devices already set.
+inline cudaError_t set_smem_limit(const void *kernel, int bytes, std::atomic<unsigned long long> &done) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess)
+        return e;
+    const unsigned long long bit = dev >= 0 && dev < 64 ? 1ull << dev : 0ull;
+    if (bit && (done.load() & bit))
+        return cudaSuccess;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess && bit)
+        done.fetch_or(bit);
+    return e;
 }
 
 } // namespace omni_b200

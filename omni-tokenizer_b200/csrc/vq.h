@@ -42,7 +42,7 @@ struct VqsParams {
     unsigned *cand;               // fp32 profile: [rows][kVqCandCap]
     int rows, dim, codes, chunks;
     int slices, slice_codes;
-    float delta;                  // fp32 profile: candidate window factor
+    float win_a, win_b;           // fp32 profile: candidate window a |x||c| + b (|x|^2 + |c|^2)
     int *err;
 };
 

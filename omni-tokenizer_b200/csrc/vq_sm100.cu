@@ -386,12 +386,9 @@ int vq_padded_dim(int dim) {
 
 template <int DP> int vq_launch_typed(VqParams &p, int grid, cudaStream_t stream) {
     using S = VqShape<DP>;
-    static std::once_flag once;
-    static cudaError_t attr = cudaSuccess;
-    std::call_once(once, [] {
-        attr = cudaFuncSetAttribute(vq_bf16_kernel<DP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    S::SMEM_BYTES);
-    });
+    static std::atomic<unsigned long long> done{0};
+    const cudaError_t attr =
+        set_smem_limit(reinterpret_cast<const void *>(vq_bf16_kernel<DP>), S::SMEM_BYTES, done);
     if (attr != cudaSuccess)
         return static_cast<int>(attr);
     vq_bf16_kernel<DP><<<grid, kVqThreads, S::SMEM_BYTES, stream>>>(p);

@@ -14,28 +14,31 @@
 //                 id (src/cpu.cpp:260-283, src/internal.h:13-18).
 //
 // fp32 profile on B200.  The tensor cores have no fp32 MMA, so the
-// approximate distances come from kind::tf32 (inputs keep 10 mantissa bits).
-// The candidate window is therefore a bound written for this kernel, not the
-// reference's fp32 gamma: for every code
-//   |approx(c) - exact(c)| <= delta * (|x|^2 + |c|^2),
-//   delta = 2^-8 + (2 dim + 8) 2^-23
-// (TF32 input error 2^-10 per factor, fp32 accumulation, the fp32 norms and
-// the final fma; 2|x.c| <= |x|^2 + |c|^2 bounds the dot-product terms, and
-// delta carries a factor of two of slack).  With b the code of the smallest
-// approximate distance, the exact nearest code c* satisfies
-//   approx(c*) - delta(|x|^2 + |c*|^2) <= approx(b) + delta(|x|^2 + |b|^2),
-// so the candidate set {c : approx(c) - delta(...c) <= approx(b) + delta(...b)}
-// contains c* and every code whose direct distance ties with it.  The
-// reference's own candidate set also contains c* (its gamma bound), and both
-// pick the smallest (direct distance, id) among candidates, so the ids agree.
-// Non-finite approximate distances are always candidates; a row with more than
-// kVqCandCap candidates is scored against every code (brute force).
+// approximate distances come from kind::tf32 (inputs truncated to 10 mantissa
+// bits).  The candidate window is therefore a bound written for this kernel,
+// not the reference's fp32 gamma: for every code
+//   |approx(c) - exact(c)| <= w(c) = a |x| |c| + b (|x|^2 + |c|^2),
+//   a = 2^-7 + (dim + 1) 2^-21,   b = (dim + 4) 2^-22
+// The dot product carries the tf32 truncation, at most 2^-10 per factor, so
+// 2|x.c - tf32 dot| <= (2^-8 + 2^-19) sum_k |x_k c_k| <= (2^-8 + 2^-19)|x||c|
+// (Cauchy-Schwarz), plus the fp32 accumulation, at most dim 2^-23 per unit of
+// sum |x_k c_k|; the fp32 norms and the final fma add at most (dim + 2) 2^-24
+// (|x|^2 + |c|^2).  a and b carry a factor of two of slack over these, and
+// |x| |c| is taken as sqrt(|x|^2) sqrt(|c|^2) of the fp32 norms.  With b* the
+// code of the smallest approximate distance, the exact nearest code c* satisfies
+//   approx(c*) - w(c*) <= approx(b*) + w(b*),
+// so the candidate set {c : approx(c) - w(c) <= approx(b*) + w(b*)} contains c*
+// and every code whose direct distance ties with it.  The reference's own
+// candidate set also contains c* (its gamma bound), and both pick the smallest
+// (direct distance, id) among candidates, so the ids agree.  Non-finite
+// approximate distances are always candidates; a row with more than
+// kVqCandCap candidates is scored against every code (vq_brute_fp64).
 //
 // Passes (one launch each):
 //   kVqsBf16    bf16 profile, keys[row] = (order bits of dist) << 32 | id
 //   kVqsApprox  fp32 profile, keys[row] = approximate best (same key form)
 //   kVqsCand    fp32 profile, appends candidates to cand[row][kVqCandCap]
-// followed by vq_refine_fp64 (fp32) or vqs_finish (bf16).
+// followed by vq_refine_fp64 and vq_brute_fp64 (fp32) or vqs_finish (bf16).
 //
 // Kernel layout: persistent grid over units (128-row tile, codebook slice);
 // warp 4 TMA producer, warp 5 TMEM owner and tcgen05.mma issuer, warps 0-3
@@ -225,11 +228,12 @@ __global__ void __launch_bounds__(kVqsThreads, 1) vq_stream_kernel(const __grid_
                     const int b = static_cast<int>(key & 0xffffffffu);
                     const float best = vqs_from_order_bits(static_cast<uint32_t>(key >> 32));
                     const float cb = static_cast<const float *>(p.cbnorm)[b];
-                    thr = best + p.delta * (xn + cb);
+                    thr = best + p.win_a * sqrtf(xn) * sqrtf(cb) + p.win_b * (xn + cb);
                 }
                 if (!(thr < INFINITY)) // non-finite: every code is a candidate
                     thr = INFINITY;
             }
+            const float sx = MODE == kVqsCand ? p.win_a * sqrtf(xn) : 0.f;
             const __nv_bfloat162 x2 = __float2bfloat162_rn(xn);
             const __nv_bfloat162 neg2 = __floats2bfloat162_rn(-2.f, -2.f);
             float best = INFINITY;
@@ -291,7 +295,7 @@ __global__ void __launch_bounds__(kVqsThreads, 1) vq_stream_kernel(const __grid_
                                 }
                             } else {
                                 // Candidate unless provably outside the window.
-                                const float lo = dist - p.delta * (xn + cnk);
+                                const float lo = dist - (sx * sqrtf(cnk) + p.win_b * (xn + cnk));
                                 if (!(lo <= thr) && isfinite(lo) && thr < INFINITY)
                                     continue;
                                 const unsigned slot = atomicAdd(p.cand_count + row, 1u);
@@ -323,10 +327,18 @@ __global__ void __launch_bounds__(kVqsThreads, 1) vq_stream_kernel(const __grid_
         tmem_dealloc(tmem, 512);
 }
 
-// Exact fp64 re-scoring of the candidates, one warp per row; rows whose list
-// overflowed are scored against every code.  The winner is the smallest
-// (direct distance, id) with a distance below +inf (src/cpu.cpp:272-282);
-// a row without one keeps id 0.
+__device__ __forceinline__ void vq_write_id(void *ids, int row, double best, unsigned best_id, int ids_u16) {
+    const unsigned id = best < INFINITY ? best_id : 0u;
+    if (ids_u16)
+        static_cast<uint16_t *>(ids)[row] = static_cast<uint16_t>(id);
+    else
+        static_cast<int32_t *>(ids)[row] = static_cast<int32_t>(id);
+}
+
+// Exact fp64 re-scoring of the candidates, one warp per row (rows whose list
+// overflowed are left to vq_brute_fp64).  The winner is the smallest (direct
+// distance, id) with a distance below +inf (src/cpu.cpp:272-282); a row
+// without one keeps id 0.
 __global__ void vq_refine_fp64(const float *x, const float *codebook, const unsigned *cand_count,
                                const unsigned *cand, void *ids, int rows, int dim, int codes,
                                int ids_u16) {
@@ -334,14 +346,14 @@ __global__ void vq_refine_fp64(const float *x, const float *codebook, const unsi
     const int lane = threadIdx.x & 31;
     for (int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < rows; row += warps) {
         const unsigned n = cand_count[row];
-        const bool brute = n > static_cast<unsigned>(kVqCandCap);
-        const int count = brute ? codes : static_cast<int>(n);
+        if (n > static_cast<unsigned>(kVqCandCap))
+            continue;
+        const int count = static_cast<int>(n);
         const float *xr = x + static_cast<long long>(row) * dim;
         double best = INFINITY;
         unsigned best_id = 0xffffffffu;
         for (int j = lane; j < count; j += 32) {
-            const unsigned code = brute ? static_cast<unsigned>(j)
-                                        : cand[static_cast<long long>(row) * kVqCandCap + j];
+            const unsigned code = cand[static_cast<long long>(row) * kVqCandCap + j];
             const float *cr = codebook + static_cast<long long>(code) * dim;
             double direct = 0.0;
             for (int k = 0; k < dim; ++k) {
@@ -362,12 +374,84 @@ __global__ void vq_refine_fp64(const float *x, const float *codebook, const unsi
                 best_id = oi;
             }
         }
-        if (lane == 0) {
-            const unsigned id = best < INFINITY ? best_id : 0u;
-            if (ids_u16)
-                static_cast<uint16_t *>(ids)[row] = static_cast<uint16_t>(id);
-            else
-                static_cast<int32_t *>(ids)[row] = static_cast<int32_t>(id);
+        if (lane == 0)
+            vq_write_id(ids, row, best, best_id, ids_u16);
+    }
+}
+
+// Rows whose candidate list overflowed: every code scored with the same direct
+// fp64 sum, one block per row.  Each thread owns codes j = t, t + 256, ... and
+// sums its code's terms in column order; x streams through shared memory in
+// 1024-column pieces.
+constexpr int kBruteThreads = 256, kBrutePiece = 1024;
+__global__ void __launch_bounds__(kBruteThreads) vq_brute_fp64(const float *x, const float *codebook,
+                                                               const unsigned *cand_count, void *ids, int rows,
+                                                               int dim, int codes, int ids_u16) {
+    __shared__ double xs[kBrutePiece];
+    __shared__ double red_d[kBruteThreads / 32];
+    __shared__ unsigned red_i[kBruteThreads / 32];
+    constexpr int kPerThread = 8; // codes per pass of a thread
+    for (int row = blockIdx.x; row < rows; row += gridDim.x) {
+        if (cand_count[row] <= static_cast<unsigned>(kVqCandCap))
+            continue; // uniform over the block
+        const float *xr = x + static_cast<long long>(row) * dim;
+        double best = INFINITY;
+        unsigned best_id = 0xffffffffu;
+        for (int c0 = 0; c0 < codes; c0 += kBruteThreads * kPerThread) {
+            double acc[kPerThread];
+#pragma unroll
+            for (int i = 0; i < kPerThread; ++i)
+                acc[i] = 0.0;
+            for (int k0 = 0; k0 < dim; k0 += kBrutePiece) {
+                const int kn = min(kBrutePiece, dim - k0);
+                __syncthreads();
+                for (int k = threadIdx.x; k < kn; k += kBruteThreads)
+                    xs[k] = static_cast<double>(xr[k0 + k]);
+                __syncthreads();
+#pragma unroll
+                for (int i = 0; i < kPerThread; ++i) {
+                    const int code = c0 + i * kBruteThreads + threadIdx.x;
+                    if (code >= codes)
+                        continue;
+                    const float *cr = codebook + static_cast<long long>(code) * dim + k0;
+                    double a = acc[i];
+                    for (int k = 0; k < kn; ++k) {
+                        const double delta = xs[k] - static_cast<double>(__ldg(cr + k));
+                        a = __dadd_rn(a, __dmul_rn(delta, delta));
+                    }
+                    acc[i] = a;
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < kPerThread; ++i) {
+                const int code = c0 + i * kBruteThreads + threadIdx.x;
+                if (code < codes && (acc[i] < best || (acc[i] == best && static_cast<unsigned>(code) < best_id))) {
+                    best = acc[i];
+                    best_id = static_cast<unsigned>(code);
+                }
+            }
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const double ob = __shfl_xor_sync(0xffffffffu, best, off);
+            const unsigned oi = __shfl_xor_sync(0xffffffffu, best_id, off);
+            if (ob < best || (ob == best && oi < best_id)) {
+                best = ob;
+                best_id = oi;
+            }
+        }
+        if ((threadIdx.x & 31) == 0) {
+            red_d[threadIdx.x >> 5] = best;
+            red_i[threadIdx.x >> 5] = best_id;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            for (int w = 1; w < kBruteThreads / 32; ++w)
+                if (red_d[w] < best || (red_d[w] == best && red_i[w] < best_id)) {
+                    best = red_d[w];
+                    best_id = red_i[w];
+                }
+            vq_write_id(ids, row, best, best_id, ids_u16);
         }
     }
 }
@@ -396,12 +480,9 @@ __global__ void vqs_init(unsigned long long *keys, unsigned *cand_count, int row
 namespace {
 template <bool TF32, int MODE> int vqs_launch_typed(const VqsParams &p, int grid, cudaStream_t stream) {
     using S = VqsShape<TF32>;
-    static std::once_flag once;
-    static cudaError_t attr = cudaSuccess;
-    std::call_once(once, [] {
-        attr = cudaFuncSetAttribute(vq_stream_kernel<TF32, MODE>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM_BYTES);
-    });
+    static std::atomic<unsigned long long> done{0};
+    const cudaError_t attr = set_smem_limit(reinterpret_cast<const void *>(vq_stream_kernel<TF32, MODE>),
+                                            S::SMEM_BYTES, done);
     if (attr != cudaSuccess)
         return static_cast<int>(attr);
     vq_stream_kernel<TF32, MODE><<<grid, kVqsThreads, S::SMEM_BYTES, stream>>>(p);
@@ -462,8 +543,10 @@ int vq_stream_launch(const VqArgs &a, int profile_fp32, cudaStream_t stream) {
     p.dim = a.dim;
     p.codes = a.codes;
     p.chunks = (a.dim + kc - 1) / kc;
-    p.delta = static_cast<float>((std::ldexp(1.0, -8) + (2.0 * a.dim + 8) * std::ldexp(1.0, -23)) *
-                                 1.0001);
+    // Window coefficients (see the top of this file), rounded up by 1e-4 for
+    // the fp32 evaluation of the window itself.
+    p.win_a = static_cast<float>((std::ldexp(1.0, -7) + (a.dim + 1.0) * std::ldexp(1.0, -21)) * 1.0001);
+    p.win_b = static_cast<float>((a.dim + 4.0) * std::ldexp(1.0, -22) * 1.0001);
     p.err = a.err;
     const int grid = plan_units(p);
     const int threads = 256;
@@ -485,6 +568,9 @@ int vq_stream_launch(const VqArgs &a, int profile_fp32, cudaStream_t stream) {
     vq_refine_fp64<<<rb < 8192 ? rb : 8192, threads, 0, stream>>>(
         static_cast<const float *>(a.x), static_cast<const float *>(a.codebook), p.cand_count,
         p.cand, a.ids, a.rows, a.dim, a.codes, a.ids_u16);
+    vq_brute_fp64<<<a.rows < 4 * sm_count() ? a.rows : 4 * sm_count(), kBruteThreads, 0, stream>>>(
+        static_cast<const float *>(a.x), static_cast<const float *>(a.codebook), p.cand_count, a.ids, a.rows,
+        a.dim, a.codes, a.ids_u16);
     return static_cast<int>(cudaGetLastError());
 }
 

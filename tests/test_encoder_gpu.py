@@ -183,6 +183,82 @@ def test_batched_images_across_chunks(abi, ours):
         s.close()
 
 
+_EMULATED_PROBE = r"""
+import sys, json
+import numpy as np
+sys.path.insert(0, sys.argv[1])
+from tests.conftest import load_package
+load_package()
+import omni_tokenizer_b200.abi as abi
+lib = abi.OmniLib(sys.argv[2])
+import ctypes, os
+emulated = hasattr(ctypes.CDLL("libcublas.so.12", mode=os.RTLD_LAZY | os.RTLD_NOLOAD), "cublasSetEmulationStrategy")
+g = dict(np.load(sys.argv[3]))
+out = {"emulated": np.array(emulated)}
+with lib.load(sys.argv[4]) as m:
+    s = m.context()
+    for i in range(3):
+        codes = s.encode_audio(g[f"audio{i}_mel"], int(g[f"audio{i}_valid"]))
+        out[f"codes{i}"], out[f"features{i}"] = codes, s.features(len(codes))
+    codes = s.encode_audio_batch(g["audio_batch_mel"], g["audio_batch_valid"])
+    out["codes_batch"], out["features_batch"] = codes, s.features(len(codes))
+    s.close()
+np.savez(sys.argv[5], **out)
+"""
+
+
+def test_audio_fp32_emulation_matches_reference(abi, ours, golden, tmp_path):
+    """In a process without torch this library's own cuBLAS (with BF16x9 fp32
+    emulation) is bound, and fp32-profile GEMMs run emulated: features stay
+    within the fp32 tolerance of the reference."""
+    import subprocess
+    import sys
+
+    lib_path = ours.path
+    out = tmp_path / "emulated.npz"
+    subprocess.run([sys.executable, "-c", _EMULATED_PROBE, str(ROOT), lib_path, str(GOLDEN / "golden.npz"),
+                    str(GOLDEN / "audio.omni"), str(out)], check=True, timeout=300)
+    got = dict(np.load(out))
+    if not bool(got["emulated"]):
+        pytest.skip("the toolkit's cuBLAS has no fp32 emulation")
+    cb = _codebook("audio")
+    for i in range(3):
+        want = golden[f"audio{i}_features"]
+        np.testing.assert_allclose(got[f"features{i}"], want, rtol=1e-4, atol=1e-4)
+        _check_codes(got[f"codes{i}"].astype(np.int64), golden[f"audio{i}_codes"].astype(np.int64),
+                     got[f"features{i}"], want, cb, False)
+    np.testing.assert_allclose(got["features_batch"], golden["audio_batch_features"], rtol=1e-4, atol=1e-4)
+
+
+def test_audio_bf16_mode_matches_graph_oracle(abi, ours, golden, monkeypatch):
+    """OMNI_B200_AUDIO_BF16=1: the audio graph in bf16 (bf16 weights and
+    activations, the reference's bf16 rounding points) against the numpy graph
+    restatement in the same profile (oracle/encoder.py, itself pinned to the
+    reference's fixtures).  Summation orders differ, so a rounded intermediate
+    may land one bf16 ulp apart: features within 4 ulps of the largest
+    feature, on average within a quarter ulp."""
+    from oracle import encoder as E
+
+    model = E.load_model(GOLDEN / "audio.omni")
+    cb = _codebook("audio")
+    monkeypatch.setenv("OMNI_B200_AUDIO_BF16", "1")
+    with ours.load(GOLDEN / "audio.omni") as m:
+        s = m.context()
+        cases = [(golden[f"audio{i}_mel"][None], [int(golden[f"audio{i}_valid"])]) for i in range(3)]
+        cases.append((golden["audio_batch_mel"], list(golden["audio_batch_valid"])))
+        for mels, valid in cases:
+            codes = s.encode_audio_batch(mels, valid)
+            feats = s.features(len(codes))
+            want = np.concatenate([E.audio(model, mel, v, bf16=True)[1] for mel, v in zip(mels, valid)])
+            assert feats.shape == want.shape
+            ulp = 2.0 ** (np.floor(np.log2(np.abs(want).max())) - 7)
+            diff = np.abs(feats - want)
+            assert diff.max() <= 4 * ulp and diff.mean() <= 0.25 * ulp, (diff.max(), diff.mean(), ulp)
+            want_codes = O.quantize(want, cb, O.squares(cb)).astype(np.int64)
+            _check_codes(codes.astype(np.int64), want_codes, feats, want, cb, False)
+        s.close()
+
+
 def test_live_reference_cross_check(abi, ours):
     """Same inputs through the reference CPU library (when built) and this library."""
     ref_path = ROOT / "oracle" / "_ref" / "libomni_ref_full.so"

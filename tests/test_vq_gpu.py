@@ -156,3 +156,32 @@ def test_vq_fp32_ties_and_nan_rows(ob):
     want = O.quantize(x, cb, bf16=False).astype(np.int64)
     assert got[0] == 7 and got[5] == 0
     assert np.array_equal(got, want)
+
+
+def test_vq_fp32_large_feature_norms(ob):
+    """Features far longer than the codes (|x| ~ 180 against |c| ~ 32, the
+    regime of pooled audio features): the candidate window must still hold the
+    exact nearest code, and stay narrow enough to avoid the brute-force path."""
+    rng = np.random.default_rng(2026)
+    rows, dim, codes = 160, 1024, 16384
+    x = (rng.standard_normal((rows, dim)) * 5.6).astype(np.float32)
+    cb = rng.standard_normal((codes, dim)).astype(np.float32)
+    got, _ = _gpu_quantize(ob, x, cb, profile=0)
+    want = O.quantize(x, cb, bf16=False).astype(np.int64)
+    assert np.array_equal(got, want), f"{int((got != want).sum())} rows differ"
+
+
+def test_vq_fp32_candidate_overflow_scores_every_code(ob):
+    """More than kVqCandCap (32) exact ties: the row falls back to scoring every
+    code in fp64, and the smallest tied id wins."""
+    rng = np.random.default_rng(7)
+    rows, dim, codes = 5, 256, 3000
+    x = rng.standard_normal((rows, dim)).astype(np.float32)
+    cb = rng.standard_normal((codes, dim)).astype(np.float32)
+    tied = np.sort(rng.choice(np.arange(100, codes), size=40, replace=False))
+    cb[tied] = x[1]
+    cb[tied[:3] - 50] = x[3] + np.float32(1e-3)  # near, not tied
+    got, _ = _gpu_quantize(ob, x, cb, profile=0, ids_u16=False)
+    want = O.quantize(x, cb, bf16=False).astype(np.int64)
+    assert got[1] == tied[0]
+    assert np.array_equal(got, want)
