@@ -6,9 +6,13 @@
 // sums use __fmul_rn / __fadd_rn where the reference's order matters, so that
 // the compiler does not contract them into FMAs the reference does not use.
 #include "graph_kernels.h"
+#include "sm100.cuh"
 
 #include <cuda_bf16.h>
 #include <stdint.h>
+
+#include <atomic>
+#include <mutex>
 
 namespace omni_b200 {
 namespace graph {
@@ -77,42 +81,120 @@ __device__ __forceinline__ float gelu_erf(float z) {
     return __fmul_rn(__fmul_rn(0.5f, z), __fadd_rn(1.f, erff(__fmul_rn(z, 0.7071067811865475244f))));
 }
 
-template <bool BF16> __global__ void k_gelu_vec(void *x, size_t nvec) {
+// Elementwise kernels keep two 16-byte vectors per thread in flight: both are
+// loaded before either is computed or stored.
+template <bool BF16> __global__ void k_gelu_vec(void *__restrict__ x, size_t nvec) {
     constexpr int N = kVec<BF16>;
-    GRID_STRIDE(i, nvec) {
-        float v[N];
-        vload<BF16>(x, i * N, v);
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < nvec; i += 2 * stride) {
+        const size_t j = i + stride;
+        float v[2][N];
+        vload<BF16>(x, i * N, v[0]);
+        if (j < nvec)
+            vload<BF16>(x, j * N, v[1]);
 #pragma unroll
-        for (int k = 0; k < N; ++k)
-            v[k] = gelu_erf(v[k]);
-        vstore<BF16>(x, i * N, v);
+        for (int u = 0; u < 2; ++u)
+#pragma unroll
+            for (int k = 0; k < N; ++k)
+                v[u][k] = gelu_erf(v[u][k]);
+        vstore<BF16>(x, i * N, v[0]);
+        if (j < nvec)
+            vstore<BF16>(x, j * N, v[1]);
     }
 }
 
-template <bool BF16> __global__ void k_add_vec(void *x, const void *y, size_t nvec) {
-    constexpr int N = kVec<BF16>;
-    GRID_STRIDE(i, nvec) {
-        float a[N], b[N];
-        vload<BF16>(x, i * N, a);
-        vload<BF16>(y, i * N, b);
+// bf16 GELU by table: the input of the bf16 profile's GELU is a bf16 value, so
+// the result is a function of its 16 bits.  g_gelu_bf16[bits] holds exactly
+// what k_gelu_vec<true> stores for that input (built on the device with the
+// same gelu_erf and rounding), and the table kernel looks it up from shared memory.
+__device__ uint16_t g_gelu_bf16[65536];
+
+__global__ void k_gelu_table_build() {
+    GRID_STRIDE(i, 65536) {
+        const float v = __uint_as_float(static_cast<uint32_t>(i) << 16);
+        g_gelu_bf16[i] = __bfloat16_as_ushort(__float2bfloat16_rn(gelu_erf(v)));
+    }
+}
+
+constexpr int kGeluTableThreads = 1024;
+constexpr size_t kGeluTableSmem = 65536 * sizeof(uint16_t);
+
+__global__ void __launch_bounds__(kGeluTableThreads) k_gelu_table(uint4 *__restrict__ x, size_t nvec) {
+    extern __shared__ uint4 table4[];
+    const uint4 *src = reinterpret_cast<const uint4 *>(g_gelu_bf16);
+    for (int i = threadIdx.x; i < 65536 / 8; i += kGeluTableThreads)
+        table4[i] = src[i];
+    __syncthreads();
+    const uint16_t *table = reinterpret_cast<const uint16_t *>(table4);
+    const size_t stride = static_cast<size_t>(gridDim.x) * kGeluTableThreads;
+    constexpr int U = 4; // vectors in flight per thread
+    for (size_t i = blockIdx.x * static_cast<size_t>(kGeluTableThreads) + threadIdx.x; i < nvec; i += U * stride) {
+        uint4 v[U];
 #pragma unroll
-        for (int k = 0; k < N; ++k)
-            a[k] = __fadd_rn(a[k], b[k]);
-        vstore<BF16>(x, i * N, a);
+        for (int u = 0; u < U; ++u)
+            if (i + u * stride < nvec)
+                v[u] = x[i + u * stride];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            uint32_t *w = reinterpret_cast<uint32_t *>(&v[u]);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                w[k] = table[w[k] & 0xffffu] | (static_cast<uint32_t>(table[w[k] >> 16]) << 16);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+            if (i + u * stride < nvec)
+                x[i + u * stride] = v[u];
+    }
+}
+
+template <bool BF16> __global__ void k_add_vec(void *__restrict__ x, const void *__restrict__ y, size_t nvec) {
+    constexpr int N = kVec<BF16>;
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < nvec; i += 2 * stride) {
+        const size_t j = i + stride;
+        const bool two = j < nvec;
+        float a[2][N], b[2][N];
+        vload<BF16>(x, i * N, a[0]);
+        vload<BF16>(y, i * N, b[0]);
+        if (two) {
+            vload<BF16>(x, j * N, a[1]);
+            vload<BF16>(y, j * N, b[1]);
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+#pragma unroll
+            for (int k = 0; k < N; ++k)
+                a[u][k] = __fadd_rn(a[u][k], b[u][k]);
+        vstore<BF16>(x, i * N, a[0]);
+        if (two)
+            vstore<BF16>(x, j * N, a[1]);
     }
 }
 
 // x[r, c] = r(x[r, c] + b[c]) over whole vectors (cols % vector == 0).
-template <bool BF16> __global__ void k_bias_vec(void *x, const void *b, size_t nvec, size_t cols) {
+template <bool BF16>
+__global__ void k_bias_vec(void *__restrict__ x, const void *__restrict__ b, size_t nvec, size_t cols) {
     constexpr int N = kVec<BF16>;
-    GRID_STRIDE(i, nvec) {
-        float a[N], c[N];
-        vload<BF16>(x, i * N, a);
-        vload<BF16>(b, (i * N) % cols, c);
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < nvec; i += 2 * stride) {
+        const size_t j = i + stride;
+        const bool two = j < nvec;
+        float a[2][N], c[2][N];
+        vload<BF16>(x, i * N, a[0]);
+        vload<BF16>(b, (i * N) % cols, c[0]);
+        if (two) {
+            vload<BF16>(x, j * N, a[1]);
+            vload<BF16>(b, (j * N) % cols, c[1]);
+        }
 #pragma unroll
-        for (int k = 0; k < N; ++k)
-            a[k] = __fadd_rn(a[k], c[k]);
-        vstore<BF16>(x, i * N, a);
+        for (int u = 0; u < 2; ++u)
+#pragma unroll
+            for (int k = 0; k < N; ++k)
+                a[u][k] = __fadd_rn(a[u][k], c[u][k]);
+        vstore<BF16>(x, i * N, a[0]);
+        if (two)
+            vstore<BF16>(x, j * N, a[1]);
     }
 }
 
@@ -120,8 +202,8 @@ template <bool BF16> __global__ void k_bias_vec(void *x, const void *b, size_t n
 // x = r(x + z) written back (the residual), then y = r(((x - mean) inv) w + b)
 // with mean and var as the reference's norm (fp32, biased variance).
 template <bool BF16, int VPL>
-__global__ void k_add_norm(void *x, const void *z, const void *w, const void *b, void *y, size_t rows, int cols,
-                           float eps) {
+__global__ void k_add_norm(void *__restrict__ x, const void *__restrict__ z, const void *__restrict__ w,
+                           const void *__restrict__ b, void *__restrict__ y, size_t rows, int cols, float eps) {
     constexpr int N = kVec<BF16>;
     const size_t row = static_cast<size_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
@@ -129,20 +211,37 @@ __global__ void k_add_norm(void *x, const void *z, const void *w, const void *b,
         return;
     const size_t base = row * static_cast<size_t>(cols);
     float v[VPL][N];
+    // All of the row's loads are issued before any arithmetic or store.
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+        const int c = (i * 32 + lane) * N;
+        if (c < cols)
+            vload<BF16>(x, base + c, v[i]);
+    }
+    if (z) {
+        float t[VPL][N];
+#pragma unroll
+        for (int i = 0; i < VPL; ++i) {
+            const int c = (i * 32 + lane) * N;
+            if (c < cols)
+                vload<BF16>(z, base + c, t[i]);
+        }
+#pragma unroll
+        for (int i = 0; i < VPL; ++i) {
+            const int c = (i * 32 + lane) * N;
+            if (c < cols) {
+#pragma unroll
+                for (int k = 0; k < N; ++k)
+                    v[i][k] = rnd(__fadd_rn(v[i][k], t[i][k]), BF16);
+                vstore<BF16>(x, base + c, v[i]);
+            }
+        }
+    }
     float s = 0.f;
 #pragma unroll
     for (int i = 0; i < VPL; ++i) {
         const int c = (i * 32 + lane) * N;
         if (c < cols) {
-            vload<BF16>(x, base + c, v[i]);
-            if (z) {
-                float t[N];
-                vload<BF16>(z, base + c, t);
-#pragma unroll
-                for (int k = 0; k < N; ++k)
-                    v[i][k] = rnd(__fadd_rn(v[i][k], t[k]), BF16);
-                vstore<BF16>(x, base + c, v[i]);
-            }
 #pragma unroll
             for (int k = 0; k < N; ++k)
                 s = __fadd_rn(s, v[i][k]);
@@ -426,13 +525,48 @@ int layer_norm(const void *x, const void *w, const void *b, void *y, bool bf16, 
         k_layer_norm<<<static_cast<unsigned>(rows), 256, 0, s>>>(x, w, b, y, bf16, cols, eps);
     return status();
 }
+namespace {
+// The table is built once per device; the table kernel's shared-memory limit
+// is raised once per device as well.
+std::atomic<unsigned long long> g_gelu_table_ready{0}, g_gelu_smem_set{0};
+std::mutex g_gelu_mutex;
+
+bool gelu_table(cudaStream_t s) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+        return false;
+    const unsigned long long bit = 1ull << dev;
+    if (g_gelu_table_ready.load() & bit)
+        return true;
+    std::lock_guard<std::mutex> guard(g_gelu_mutex);
+    if (!(g_gelu_table_ready.load() & bit)) {
+        if (set_smem_limit(reinterpret_cast<const void *>(k_gelu_table), static_cast<int>(kGeluTableSmem),
+                           g_gelu_smem_set) != cudaSuccess)
+            return false;
+        k_gelu_table_build<<<64, 1024, 0, s>>>();
+        if (cudaGetLastError() != cudaSuccess || cudaStreamSynchronize(s) != cudaSuccess)
+            return false;
+        g_gelu_table_ready.fetch_or(bit);
+    }
+    return true;
+}
+} // namespace
+
 int gelu(void *x, bool bf16, size_t n, cudaStream_t s) {
     const size_t N = bf16 ? 8 : 4, nvec = aligned16(x) ? n / N : 0, done = nvec * N;
     if (nvec) {
-        if (bf16)
+        if (bf16 && gelu_table(s)) {
+            int sms = 148, dev = 0;
+            cudaGetDevice(&dev);
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+            const size_t want = (nvec + kGeluTableThreads - 1) / kGeluTableThreads;
+            const unsigned grid = static_cast<unsigned>(want < static_cast<size_t>(sms) ? want : sms);
+            k_gelu_table<<<grid, kGeluTableThreads, kGeluTableSmem, s>>>(static_cast<uint4 *>(x), nvec);
+        } else if (bf16) {
             k_gelu_vec<true><<<blocks_for(nvec, 256), 256, 0, s>>>(x, nvec);
-        else
+        } else {
             k_gelu_vec<false><<<blocks_for(nvec, 256), 256, 0, s>>>(x, nvec);
+        }
     }
     if (done < n)
         k_gelu<<<blocks_for(n - done, 256), 256, 0, s>>>(static_cast<char *>(x) + done * (bf16 ? 2 : 4), bf16,
@@ -458,7 +592,7 @@ namespace {
 template <bool BF16, int VPL>
 void launch_add_norm(void *x, const void *z, const void *w, const void *b, void *y, size_t rows, size_t cols,
                      float eps, cudaStream_t s) {
-    constexpr int kRows = 8; // warps (rows) per block
+    constexpr int kRows = 4; // warps (rows) per block
     k_add_norm<BF16, VPL><<<static_cast<unsigned>((rows + kRows - 1) / kRows), kRows * 32, 0, s>>>(
         x, z, w, b, y, rows, static_cast<int>(cols), eps);
 }
