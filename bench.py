@@ -1,7 +1,8 @@
 #!/usr/bin/env python
 """Benchmark of the omni-tokenizer hot path on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c1|c3|vq_audio|vq_image]
+    python bench.py [--gpus N] [--steps K] [--warmup W]
+                    [--config c2|c1|c3|vq_audio|vq_image|c4|c4_bf16|c5] [--items N]
                     [--impl ours|reference]
 
 Default workload (--config c2): BASELINE config 2, the SigLIP-shaped encoder
@@ -25,6 +26,14 @@ no collective on the data path (timing uses one all-reduce of a scalar).
 
 --impl reference times the reference's CPU implementation (oracle/_ref, or
 the oracle port when the reference was not compiled here) on the same metric.
+
+Whole encoders (--config c4|c4_bf16|c5, BASELINE configs 4 and 5): a seeded
+random-weight OMNIVQ01 model of production shape is written per run and loaded
+through the omni_* C ABI of libomni_b200.so; value = items/s (images/s, or
+audio seconds/s) through the batched call on device-resident inputs, e2e = the
+same call on host buffers; items split evenly across ranks (strong scaling);
+the CPU baseline is the reference's own CPU library, extrapolated from 1- and
+2-layer models.
 """
 
 from __future__ import annotations
@@ -789,8 +798,14 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=5.0, help="CPU baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--items", type=int, default=None,
+                    help="whole-encoder configs: items per step (default: the config's; smaller for profiling)")
     args = ap.parse_args()
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config])
+    if args.items is not None:
+        if cfg["kind"] != "encoder" or args.items <= 0:
+            ap.error("--items applies to the whole-encoder configs and must be positive")
+        cfg["items"] = args.items
     if cfg["kind"] == "encoder":
         return run_encoder(args, cfg, reference=args.impl == "reference")
     if args.impl == "reference":
