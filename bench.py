@@ -439,7 +439,8 @@ def run_encoder(args, cfg, reference=False):
     # Strong scaling: the step's items split evenly across ranks.
     share = [len(r) for r in np.array_split(np.arange(cfg["items"]), world)]
     mine = share[rank]
-    host = encoder_inputs(cfg, mine, cfg["seed"] + 7919 * rank)
+    # Host inputs live in pinned memory (the e2e leg copies them every step).
+    host = torch.from_numpy(encoder_inputs(cfg, mine, cfg["seed"] + 7919 * rank)).pin_memory().numpy()
     dev = torch.from_numpy(host).cuda()
 
     def barrier():
@@ -504,7 +505,7 @@ def run_encoder(args, cfg, reference=False):
     value = items_total * unit_per_item / elapsed
     e2e_value = cfg["items"] * e2e_steps * unit_per_item / e2e_elapsed
     per_item_value = sample * world * unit_per_item / item_elapsed
-    tflops = items_total * flops_item / elapsed / 1e12
+    tflops = items_total * flops_item / elapsed / 1e12 / world  # per GPU
     pk, pk_kind = peaks()
     peak = float(pk.get("bf16_tflops_sustained", pk.get("bf16_tflops", 1400.0)))
     cpu = None
@@ -539,7 +540,7 @@ def run_encoder(args, cfg, reference=False):
                 "timing": "wall clock around the synchronous batched call omni_b200_encode_"
                           + ("audio_batch" if cfg["modality"] == "audio" else "images")
                           + " (device-resident inputs; codes copied back), synchronize + barrier on both sides, "
-                            "max over ranks",
+                            "max over ranks; e2e: the same call on pinned host buffers",
                 "per_item_abi": {"value": per_item_value, "unit": unit_name, "items": sample,
                                  "call": "omni_encode_" + cfg["modality"] + " (the reference's single-item call, "
                                          "host buffers)"},
@@ -551,7 +552,7 @@ def run_encoder(args, cfg, reference=False):
             },
             "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak, "unit": "TFLOP/s",
                          "frac": tflops / peak, "traffic": None,
-                         "peak_source": f"{pk_kind} bf16_tflops_sustained (whole-encoder FLOPs / wall time)"},
+                         "peak_source": f"{pk_kind} bf16_tflops_sustained (whole-encoder FLOPs per GPU / wall time)"},
             "e2e": {"value": e2e_value, "unit": unit_name, "h2d_bytes_per_step": in_item * cfg["items"],
                     "d2h_bytes_per_step": codes_bytes // e2e_steps * world},
             "cpu_baseline": cpu,
