@@ -528,43 +528,58 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
             if constexpr (S::PT) {
                 // Per KV tile g: S_0(g+1), S_1(g+1) as soon as the softmax has
                 // read S_0(g), S_1(g); then O_0 += P_0(g) V_g and O_1 += P_1(g) V_g
-                // as each P arrives.  pv_done[i] fires after O_i += P_i V.
+                // as each P arrives.  pv_done[i] fires after O_i += P_i V.  The
+                // loop is pipelined across items: during an item's last KV tile
+                // the next item's first S goes out (its Q sits in the other Q
+                // slot), so the tensor core computes it while the softmax warps
+                // finish the item and run its epilogue.
+                static_assert(S::QBUF >= 2, "cross-item S issue needs a second Q slot");
                 int nq = 0, kv = 0;
-                bool ok = true;
-                for (int u = blockIdx.x; ok && u < items; u += gridDim.x) {
+                bool ok = true, first_s_issued = false;
+                // S_i(g) for both tiles from the Q slot at qb.
+                auto issue_s = [&](uint32_t qb, int g, int st) {
+                    for (int i = 0; i < 2; ++i) {
+                        if (g > 0 && !__all_sync(0xffffffffu, mbar_wait(&s_free[i], (g - 1) & 1, err, kErrWaitS)))
+                            return false;
+                        tc_fence_after();
+                        qk(qb, i, st);
+                        commit(&s_full[i]);
+                    }
+                    commit(&k_empty[st]);
+                    return true;
+                };
+                for (int u = next_work_item(p, blockIdx.x, items); ok && u < items;) {
                     const Item it = decode_item(p, u);
-                    if (it.skip || it.T == 0)
-                        continue;
+                    const int u_next = next_work_item(p, u + gridDim.x, items);
                     const int qs = nq % S::QBUF;
                     const uint32_t qbase = sq + qs * 2 * S::TILE_BYTES;
-                    if (!(ok = __all_sync(0xffffffffu, mbar_wait(&q_full[qs], (nq / S::QBUF) & 1, err, kErrWaitQ))))
-                        break;
-                    // S_i(g0) for the item's first KV tile g0 = kv.
-                    auto issue_s = [&](int g, int st) {
-                        for (int i = 0; i < 2; ++i) {
-                            if (g > 0 && !__all_sync(0xffffffffu, mbar_wait(&s_free[i], (g - 1) & 1, err, kErrWaitS)))
-                                return false;
-                            tc_fence_after();
-                            qk(qbase, i, st);
-                            commit(&s_full[i]);
-                        }
-                        commit(&k_empty[st]);
-                        return true;
-                    };
-                    {
+                    if (!first_s_issued) { // S_i(g0) for the item's first KV tile g0 = kv
                         const int st = kv % S::STAGES;
+                        if (!(ok = __all_sync(0xffffffffu, mbar_wait(&q_full[qs], (nq / S::QBUF) & 1, err, kErrWaitQ))))
+                            break;
                         if (!(ok = __all_sync(0xffffffffu, mbar_wait(&k_full[st], (kv / S::STAGES) & 1, err, kErrWaitK))))
                             break;
-                        if (!(ok = issue_s(kv, st)))
+                        if (!(ok = issue_s(qbase, kv, st)))
                             break;
                     }
+                    first_s_issued = false;
                     for (int j = 0; ok && j < it.T; ++j) {
                         const int g = kv + j, st = g % S::STAGES;
-                        if (j + 1 < it.T) {
+                        if (j + 1 < it.T || u_next < items) {
+                            // The next S: this item's tile j + 1, or the next
+                            // item's first tile (global KV tile g + 1 either way).
                             const int st1 = (g + 1) % S::STAGES;
+                            uint32_t qb = qbase;
+                            if (j + 1 == it.T) {
+                                const int qs1 = (nq + 1) % S::QBUF;
+                                if (!(ok = __all_sync(0xffffffffu, mbar_wait(&q_full[qs1], ((nq + 1) / S::QBUF) & 1, err, kErrWaitQ))))
+                                    break;
+                                qb = sq + qs1 * 2 * S::TILE_BYTES;
+                                first_s_issued = true;
+                            }
                             if (!(ok = __all_sync(0xffffffffu, mbar_wait(&k_full[st1], ((g + 1) / S::STAGES) & 1, err, kErrWaitK))))
                                 break;
-                            if (!(ok = issue_s(g + 1, st1)))
+                            if (!(ok = issue_s(qb, g + 1, st1)))
                                 break;
                         }
                         if (!(ok = __all_sync(0xffffffffu, mbar_wait(&v_full[st], (g / S::STAGES) & 1, err, kErrWaitV))))
@@ -586,6 +601,7 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                         commit(&q_empty[qs]); // every MMA reading this Q slot is done
                     kv += it.T;
                     ++nq;
+                    u = u_next;
                 }
             } else {
                 int nq = 0, kv = 0, n_items = 0;
