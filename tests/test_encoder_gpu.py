@@ -324,3 +324,75 @@ def test_api_behaviour(abi, ours, golden):
     with pytest.raises(abi.OmniError) as e:
         ours.load(GOLDEN / "golden.npz")
     assert e.value.status == 3
+
+
+def test_plain_cublas_fallback_matches_reference(abi, ours, golden, monkeypatch):
+    """OMNI_B200_CUBLASLT=0: linears as plain cuBLAS GEMMs plus the separate
+    bias / rounding epilogue kernel -- the same results within the tolerances."""
+    monkeypatch.setenv("OMNI_B200_CUBLASLT", "0")
+    cb = _codebook("image")
+    with ours.load(GOLDEN / "image.omni") as m:
+        s = m.context()
+        for i in range(3):
+            codes = s.encode_image(golden[f"image{i}_pixels"])
+            feats = s.features(len(codes))
+            want = golden[f"image{i}_features"]
+            assert np.abs(feats - want).max() <= 1 / 128
+            _check_codes(codes.astype(np.int64), golden[f"image{i}_codes"].astype(np.int64), feats, want, cb, True)
+        s.close()
+    with ours.load(GOLDEN / "audio.omni") as m:
+        s = m.context()
+        codes = s.encode_audio_batch(golden["audio_batch_mel"], golden["audio_batch_valid"])
+        np.testing.assert_allclose(s.features(len(codes)), golden["audio_batch_features"], rtol=1e-4, atol=1e-4)
+        s.close()
+
+
+def test_concurrent_contexts_share_a_model(abi, ours):
+    """Several host threads, one context each on one shared model, encoding at
+    the same time: each gets the codes a lone call gets."""
+    import threading
+
+    rng = np.random.default_rng(5)
+    batches = [rng.uniform(-1, 1, (6, 3, 32, 24)).astype(np.float32) for _ in range(4)]
+    with ours.load(GOLDEN / "image.omni") as m:
+        lone = []
+        for b in batches:
+            s = m.context()
+            lone.append(s.encode_images(b, patch=8))
+            s.close()
+        got = [None] * len(batches)
+        errors = []
+
+        def work(k):
+            try:
+                s = m.context()
+                for _ in range(3):
+                    got[k] = s.encode_images(batches[k], patch=8)
+                s.close()
+            except Exception as e:  # reported below
+                errors.append(e)
+
+        threads = [threading.Thread(target=work, args=(k,)) for k in range(len(batches))]
+        for t in threads:
+            t.start()
+        for t in threads:
+            t.join()
+        assert not errors, errors
+        for a, b in zip(got, lone):
+            np.testing.assert_array_equal(a, b)
+
+
+def test_two_devices_in_one_process(abi, ours, golden):
+    """A model and context per device in one process (kernel attributes and the
+    GELU table are per device): both devices give the same codes."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two CUDA devices")
+    px = golden["image_batch_pixels"]
+    out = []
+    for dev in (0, 1):
+        with ours.load(GOLDEN / "image.omni", device=dev) as m:
+            s = m.context()
+            out.append((s.encode_images(px, patch=8), s.features()))
+            s.close()
+    np.testing.assert_array_equal(out[0][0], out[1][0])
+    np.testing.assert_array_equal(out[0][1], out[1][1])
