@@ -462,6 +462,67 @@ __global__ void k_to_float(const void *x, float *y, bool bf16, size_t n) {
 // [items, heads, n] of n scores each; row t of item b keeps keys below
 // limit = min(n, valid[b]) (and the block window), p = exp(z - max) / total as
 // the reference's Ops::attention; masked keys become 0.
+// The same with 16-byte accesses (n % 4 == 0): lane owns columns
+// 4 (lane + 32 i) .. +3.
+template <int VEC_PER_LANE>
+__global__ void k_softmax_rows4(float *__restrict__ s, size_t items, size_t heads, size_t n, const int *valid,
+                                size_t valid_all, size_t block) {
+    const size_t row = static_cast<size_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= items * heads * n)
+        return;
+    const size_t b = row / (heads * n), t = row % n;
+    size_t limit = valid ? static_cast<size_t>(valid[b] > 0 ? valid[b] : 0) : valid_all;
+    limit = limit < n ? limit : n;
+    if (block)
+        limit = limit < (t / block + 1) * block ? limit : (t / block + 1) * block;
+    float4 *z = reinterpret_cast<float4 *>(s + row * n);
+    float4 v[VEC_PER_LANE];
+#pragma unroll
+    for (int i = 0; i < VEC_PER_LANE; ++i) {
+        const size_t c = 4 * (lane + 32 * static_cast<size_t>(i));
+        v[i] = c < n ? z[c / 4] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < VEC_PER_LANE; ++i) {
+        const size_t c = 4 * (lane + 32 * static_cast<size_t>(i));
+        float *e = &v[i].x;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            e[k] = c + k < limit ? e[k] : -INFINITY;
+            mx = fmaxf(mx, e[k]);
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1)
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float total = 0.f;
+#pragma unroll
+    for (int i = 0; i < VEC_PER_LANE; ++i) {
+        const size_t c = 4 * (lane + 32 * static_cast<size_t>(i));
+        float *e = &v[i].x;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            e[k] = c + k < limit ? expf(e[k] - mx) : 0.f;
+            total += e[k];
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1)
+        total += __shfl_xor_sync(0xffffffffu, total, o);
+#pragma unroll
+    for (int i = 0; i < VEC_PER_LANE; ++i) {
+        const size_t c = 4 * (lane + 32 * static_cast<size_t>(i));
+        if (c < n) {
+            float4 w = v[i];
+            w.x /= total;
+            w.y /= total;
+            w.z /= total;
+            w.w /= total;
+            z[c / 4] = w;
+        }
+    }
+}
+
 template <int PER_LANE>
 __global__ void k_softmax_rows(float *s, size_t items, size_t heads, size_t n, const int *valid,
                                size_t valid_all, size_t block) {
@@ -713,6 +774,17 @@ int softmax_rows(float *scores, size_t items, size_t heads, size_t n, const int 
         return 0;
     constexpr int kWarps = 8;
     const unsigned grid = static_cast<unsigned>((rows + kWarps - 1) / kWarps);
+    if (n % 4 == 0 && aligned16(scores)) {
+        if (n <= 512)
+            k_softmax_rows4<4><<<grid, kWarps * 32, 0, s>>>(scores, items, heads, n, valid, valid_all, block);
+        else if (n <= 1536)
+            k_softmax_rows4<12><<<grid, kWarps * 32, 0, s>>>(scores, items, heads, n, valid, valid_all, block);
+        else if (n <= 4096)
+            k_softmax_rows4<32><<<grid, kWarps * 32, 0, s>>>(scores, items, heads, n, valid, valid_all, block);
+        else
+            return -2;
+        return status();
+    }
     if (n <= 512)
         k_softmax_rows<16><<<grid, kWarps * 32, 0, s>>>(scores, items, heads, n, valid, valid_all, block);
     else if (n <= 1536)

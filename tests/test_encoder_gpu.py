@@ -396,3 +396,28 @@ def test_two_devices_in_one_process(abi, ours, golden):
             s.close()
     np.testing.assert_array_equal(out[0][0], out[1][0])
     np.testing.assert_array_equal(out[0][1], out[1][1])
+
+
+def test_multi_device_encoder_matches_one_session(abi, ours, golden):
+    """omni-tokenizer_b200/multidevice.py over every visible device (one thread
+    and context each) returns the codes of a single batched call, in order."""
+    load_package()
+    from omni_tokenizer_b200.multidevice import MultiDeviceEncoder
+
+    devices = list(range(min(torch.cuda.device_count(), 4)))
+    rng = np.random.default_rng(17)
+    px = rng.uniform(-1, 1, (9, 3, 32, 24)).astype(np.float32)
+    mels, valid = golden["audio_batch_mel"], golden["audio_batch_valid"]
+    with ours.load(GOLDEN / "image.omni") as m:
+        s = m.context()
+        want_img = s.encode_images(px, patch=8).reshape(9, -1)
+        s.close()
+    with ours.load(GOLDEN / "audio.omni") as m:
+        s = m.context()
+        want_audio = [s.encode_audio_batch(mel[None], [v]) for mel, v in zip(mels, valid)]
+        s.close()
+    with MultiDeviceEncoder(devices, lib=ours, model_path=GOLDEN / "image.omni") as enc:
+        np.testing.assert_array_equal(enc.encode_images(px, patch=8), want_img)
+    with MultiDeviceEncoder(devices, lib=ours, model_path=GOLDEN / "audio.omni") as enc:
+        for got, want in zip(enc.encode_audio(mels, valid), want_audio):
+            np.testing.assert_array_equal(got, want)
