@@ -509,15 +509,18 @@ __global__ void k_softmax_rows4(float *__restrict__ s, size_t items, size_t head
     }
     for (int o = 16; o > 0; o >>= 1)
         total += __shfl_xor_sync(0xffffffffu, total, o);
+    // One reciprocal per row instead of an IEEE division per score (within an
+    // ulp of p / total; the division was a third of the kernel's instructions).
+    const float inv = 1.f / total;
 #pragma unroll
     for (int i = 0; i < VEC_PER_LANE; ++i) {
         const size_t c = 4 * (lane + 32 * static_cast<size_t>(i));
         if (c < n) {
             float4 w = v[i];
-            w.x /= total;
-            w.y /= total;
-            w.z /= total;
-            w.w /= total;
+            w.x *= inv;
+            w.y *= inv;
+            w.z *= inv;
+            w.w *= inv;
             z[c / 4] = w;
         }
     }
@@ -555,11 +558,12 @@ __global__ void k_softmax_rows(float *s, size_t items, size_t heads, size_t n, c
     }
     for (int o = 16; o > 0; o >>= 1)
         total += __shfl_xor_sync(0xffffffffu, total, o);
+    const float inv = 1.f / total;
 #pragma unroll
     for (int i = 0; i < PER_LANE; ++i) {
         const size_t c = lane + 32 * static_cast<size_t>(i);
         if (c < n)
-            z[c] = v[i] / total;
+            z[c] = v[i] * inv;
     }
 }
 
