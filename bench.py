@@ -382,10 +382,10 @@ def run_encoder(args, cfg, reference=False):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     unit_name, unit_per_item = encoder_unit(cfg)
     flops_item = encoder_flops(cfg)
+    if reference and rank != 0:
+        return 0  # the reference arm runs on rank 0 only
     tmpdir = tempfile.mkdtemp(prefix="omni_bench_")
     if reference:
-        if rank != 0:
-            return 0
         # Each step is one item per model depth; the best of `steps` repeats counts.
         got = cpu_encoder_sample(cfg, tmpdir, repeats=max(1, min(args.steps, 3)))
         if got is None:
