@@ -13,7 +13,8 @@
  * backend interface omni::Ops (omni-tokenizer src/internal.h:52-90); the
  * reference exposes that interface only to C++ (make_cuda(), used by
  * tests/native_cuda_attention.cpp:24-41).  A consumer binds them the same way
- * native.py binds omni.h.
+ * the reference's python/omni_tokenizer/native.py binds omni.h: one ctypes (or
+ * cgo / JNI) declaration per entry point, status codes checked after each call.
  */
 #ifndef OMNI_B200_H
 #define OMNI_B200_H

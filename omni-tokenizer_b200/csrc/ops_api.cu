@@ -52,6 +52,8 @@ int *kernel_error_word() {
 }
 
 int ctx_fail(int code, const char *msg) { return fail(code, msg); }
+// Clears this thread's error message (every entry point starts with it).
+void ctx_clear() { g_error.clear(); }
 
 int launch_status(int rc, const char *what) {
     if (rc == 0)

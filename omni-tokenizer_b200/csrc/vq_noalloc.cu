@@ -24,6 +24,7 @@
 
 namespace omni_b200 {
 int ctx_fail(int code, const char *msg);
+void ctx_clear();
 int *kernel_error_word();
 int launch_status(int rc, const char *what);
 
@@ -70,6 +71,7 @@ extern "C" int omni_b200_vq_argmin_noalloc(const void *x, const void *codebook,
                                            const void *cbnorm, void *ids, size_t rows,
                                            size_t dim, size_t codes, int profile, int ids_u16,
                                            void *stream) {
+    ctx_clear();
     if (!x || !codebook || !cbnorm || !ids)
         return ctx_fail(1, "vq_argmin_noalloc: null pointer");
     if (rows == 0)

@@ -5,10 +5,14 @@ Markers:
 Everything else runs on a CPU-only machine.
 """
 
+import os
 import sys
 from pathlib import Path
 
 ROOT = Path(__file__).resolve().parents[1]
+# The reference checkout, read only by the CPU tests that bind or build from it:
+# $OMNI_REFERENCE, else a `reference` directory beside this repository.
+REFERENCE = Path(os.environ.get("OMNI_REFERENCE") or ROOT.parent / "reference")
 if str(ROOT) not in sys.path:
     sys.path.insert(0, str(ROOT))
 

@@ -33,9 +33,33 @@ ATTENTION = [
     ("attn_keypad_hd64", 300, 2, 64, 0, 217, False, True),
 ]
 
+# Head-major batched attention (oracle.attention_bhld): name, batch, heads, L, hd, lengths, block.
+ATTENTION_BHLD = [
+    ("attn_bhld_varlen_hd64", 3, 2, 100, 64, (100, 67, 1), 0),
+    ("attn_bhld_block_hd72", 2, 2, 90, 72, (90, 83), 40),
+]
+
+
+def bhld_fixtures():
+    """Each (batch, head) slice of a head-major batch is the reference's
+    Ops::attention on one sequence of `heads=1`, valid = lengths[b]."""
+    assert O.ref_available(), "build oracle/_ref first: make -C oracle ref"
+    for name, batch, heads, L, hd, lengths, block in ATTENTION_BHLD:
+        shape = (batch, heads, L, hd)
+        q = O.lcg_values(int(np.prod(shape)), 321).reshape(shape)
+        k = O.lcg_values(int(np.prod(shape)), 654).reshape(shape)
+        v = O.lcg_values(int(np.prod(shape)), 987).reshape(shape)
+        y = np.zeros(shape, np.float32)
+        for b in range(batch):
+            for h in range(heads):
+                y[b, h] = O.attention(q[b, h], k[b, h], v[b, h], 1, block, lengths[b], impl="ref")
+        np.savez_compressed(OUT / f"{name}.npz", kind="attention_bhld", q=q, k=k, v=v, y=y,
+                            lengths=np.array(lengths, np.int32), block=block)
+
 
 def main():
     assert O.ref_available(), "build oracle/_ref first: make -C oracle ref"
+    bhld_fixtures()
     for name, rows, heads, hd, block, valid, fused, bf16 in ATTENTION:
         d = heads * hd
         cols = d * (3 if fused else 1)

@@ -166,3 +166,69 @@ def test_invalid_arguments_fail_loudly(ob):
     assert e.value.status == 4
     st = lib.lib.omni_b200_attention_bhld(None, None, None, None, 1, 1, 1, 64, 1, 1, None, 0, 0, 0.0, None)
     assert st == 1 and b"null" in lib.lib.omni_b200_last_error()
+
+
+# ---------------------------------------------------------------------------
+# The reference's own CUDA gate (tests/native_cuda_attention.cpp:43-95): inputs
+# from its LCG (fused Q|K|V rounded to bf16), output in the input's type, and
+# every element of the boundary query rows within a fixed bound of a float64
+# scalar attention computed from the same values -- 2e-3 for the fused bf16
+# path, 3e-6 for unfused fp32.
+def reference_boundary_rows(n, block, valid):
+    """Query rows the reference checks: the ends, the valid tail and both
+    sides of the 128 / 256 / block / valid boundaries."""
+    rows = {0, n - 1, min(n - 1, valid - 1)}
+    for boundary in (128, 256, block, valid):
+        if boundary and boundary <= n:
+            rows.add(boundary - 1)
+        if boundary < n:
+            rows.add(boundary)
+    return sorted(rows)
+
+
+def reference_rows_fp64(q, k, v, n, heads, hd, block, valid, fused, rows):
+    """native_cuda_attention.cpp:62-90 restated: scores as float64 sums of
+    float32 products (Q, and for fused inputs also K, pre-multiplied by the
+    float32 scale), softmax and the weighted values in float64."""
+    d = heads * hd
+    f32 = np.float32
+    scale = f32(float(hd) ** -0.25) if fused else f32(1) / np.sqrt(f32(hd))
+    out = np.zeros((len(rows), d), np.float64)
+    for i, t in enumerate(rows):
+        limit = min(n, valid)
+        if block:
+            limit = min(limit, (t // block + 1) * block)
+        for h in range(heads):
+            a = (q[t, h * hd:(h + 1) * hd] * scale).astype(np.float64)
+            if fused:
+                kk = (q[:limit, d + h * hd:d + (h + 1) * hd] * scale).astype(np.float64)
+                vv = q[:limit, 2 * d + h * hd:2 * d + (h + 1) * hd].astype(np.float64)
+            else:
+                kk = k[:limit, h * hd:(h + 1) * hd].astype(np.float64)
+                vv = v[:limit, h * hd:(h + 1) * hd].astype(np.float64)
+            s = kk @ a
+            p = np.exp(s - s.max())
+            out[i, h * hd:(h + 1) * hd] = (p / p.sum()) @ vv
+    return out
+
+
+FUSED_BF16_CASES = [(n, 2) for n in (31, 32, 129, 255, 256, 257, 385, 512, 2049)] + \
+                   [(n, 16) for n in (1, 129, 257, 576, 768, 1080, 2049)]
+
+
+@pytest.mark.parametrize("n,heads", FUSED_BF16_CASES)
+def test_reference_fused_bf16_per_element(ob, n, heads):
+    """native_cuda_attention.cpp:238-241: fused hd 96, bf16, bound 2e-3 per element."""
+    hd, block, valid = 96, 0, n
+    d = heads * hd
+    q = O.round_bf16(O.lcg_values(n * 3 * d, 123).reshape(n, 3 * d))
+    tq = torch.from_numpy(q).to(torch.bfloat16).cuda()
+    out = ob.attention_rows(tq, None, None, heads, block=block, valid=valid, fused=True)
+    ob.library().sync_check()
+    assert out.dtype == torch.bfloat16
+    got = out.float().cpu().numpy()
+    assert np.isfinite(got).all()
+    rows = reference_boundary_rows(n, block, valid)
+    want = reference_rows_fp64(q, None, None, n, heads, hd, block, valid, True, rows)
+    err = np.abs(got[rows].astype(np.float64) - want)
+    assert err.max() <= 2e-3, f"n={n} heads={heads}: max error {err.max():.3e} at rows {rows}"

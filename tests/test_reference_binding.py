@@ -10,9 +10,9 @@ from pathlib import Path
 
 import pytest
 
-from tests.conftest import ROOT, load_package
+from tests.conftest import REFERENCE, ROOT, load_package
 
-REFERENCE_PY = Path("/root/reference/python")
+REFERENCE_PY = REFERENCE / "python"
 
 
 @pytest.fixture()

@@ -2,10 +2,15 @@
 
 Rule: codes identical except rows where the
 reference's top-2 distance gap is below 1e-3 relative.  In the bf16 profile
-the distance itself is quantised to bf16, so a row can also flip when the
-fp32 dot product is summed in a different order and lands on the other side
-of a bf16 rounding boundary; such rows are counted separately and must stay
-rare (the reference's own CPU and GPU paths differ the same way).
+that rule only admits exact ties (the distance is a bf16 value, so two
+different distances are at least one bf16 ulp, 2^-8 relative, apart), and a
+second kind of difference is possible: the tensor core sums x.c in another
+order than the reference's sequential fp32 loop, so the fp32 dot can land on
+the other side of a bf16 rounding boundary, which moves that code's distance
+by one bf16 ulp.  Such a "rounding flip" is accepted only when the chosen
+code's distance under the reference's own formula is within one bf16 ulp of
+the reference's best; every flip is counted and printed, and the allowance
+per case is the measured count (see ROUNDING_FLIPS_ALLOWED).
 """
 
 import numpy as np
@@ -47,18 +52,51 @@ def _gpu_quantize(ob, x, cb, ids_u16=True, profile=1):
     return (out.view(np.uint16).astype(np.int64) if ids_u16 else out.astype(np.int64)), norms
 
 
-def _check(x, cb, got, allowed_rounding_flips=0.002, bf16=True):
+def bf16_ulp(v):
+    """Spacing of bf16 values at |v| (8 significant bits)."""
+    e = np.floor(np.log2(np.maximum(np.abs(v), np.finfo(np.float32).tiny)))
+    return np.exp2(e - 7)
+
+
+def reference_bf16_distance(x, cb, rows, codes):
+    """The reference's bf16-profile distance (src/cpu.cpp:216-253) of code
+    codes[i] from row rows[i]: sequential fp32 dot, rounded to bf16 by the
+    linear, then bf16(bf16(|x|^2 + |c|^2) - bf16(2 dot))."""
+    r = O.round_bf16
+    xs, cs = x[rows], cb[codes]
+    acc = np.zeros(len(rows), np.float32)
+    for j in range(x.shape[1]):
+        acc = (acc + xs[:, j] * cs[:, j]).astype(np.float32)
+    xn, cn = O.squares(xs, bf16=True), O.squares(cs, bf16=True)
+    return r(r(xn + cn) - r(np.float32(2) * r(acc)))
+
+
+# Rows per case that may differ from the oracle by a dot-product rounding flip
+# (bf16 profile only): the count measured on a B200, which the tests print.
+ROUNDING_FLIPS_ALLOWED = 0
+
+
+def _check(x, cb, got, bf16=True, what=""):
+    """Returns (rows differing, exact/near ties, rounding flips); asserts the
+    rule above and prints the counts."""
     want = O.quantize(x, cb, bf16=bf16).astype(np.int64)
     mism = np.nonzero(got != want)[0]
-    if len(mism) == 0:
-        return 0
-    d1, d2 = O.quantize_top2(x[mism], cb, bf16=bf16)
-    near_tie = (d2 - d1) < 1e-3 * np.abs(d1)
-    # Remaining rows: the chosen code must be within one bf16 ulp of the best
-    # under the reference's own distance (dot rounding-order flips only).
-    rest = mism[~near_tie]
-    assert len(rest) <= max(1, allowed_rounding_flips * len(x)), f"{len(rest)} rows differ beyond the tie rule"
-    return len(mism)
+    ties = flips = 0
+    if len(mism):
+        d1, d2 = O.quantize_top2(x[mism], cb, bf16=bf16)
+        near_tie = (d2 - d1) < 1e-3 * np.abs(d1)
+        ties = int(near_tie.sum())
+        rest = mism[~near_tie]
+        assert bf16 or len(rest) == 0, f"{what}: {len(rest)} fp32-profile rows differ beyond the tie rule"
+        if len(rest):
+            ours = reference_bf16_distance(x, cb, rest, got[rest])
+            best = reference_bf16_distance(x, cb, rest, want[rest])
+            gap = ours.astype(np.float64) - best
+            assert (gap <= bf16_ulp(best)).all(), f"{what}: a chosen code is more than one bf16 ulp from the best"
+            flips = len(rest)
+    print(f"VQ {what}: rows {len(x)}, differ {len(mism)}, ties {ties}, rounding flips {flips}")
+    assert flips <= ROUNDING_FLIPS_ALLOWED, f"{what}: {flips} rounding flips (allowed {ROUNDING_FLIPS_ALLOWED})"
+    return len(mism), ties, flips
 
 
 @pytest.mark.parametrize("rows,dim,codes", [(300, 64, 2051), (1000, 32, 16384), (129, 16, 700), (257, 128, 1500),
@@ -72,7 +110,7 @@ def test_vq_bf16_matches_oracle(ob, rows, dim, codes):
     # The norms kernel must match the reference's squares bit for bit.
     want_norms = O.squares(cb, bf16=True)
     assert np.array_equal(norms.float().cpu().numpy(), want_norms)
-    _check(x, cb, got)
+    _check(x, cb, got, what=f"bf16 rows={rows} dim={dim} codes={codes}")
 
 
 def test_vq_bf16_tie_known_answer(ob):
@@ -97,7 +135,7 @@ def test_vq_int32_ids_and_normalised_image_features(ob):
     cb /= np.linalg.norm(cb, axis=1, keepdims=True)
     x, cb = O.round_bf16(x), O.round_bf16(cb)
     got, _ = _gpu_quantize(ob, x, cb, ids_u16=False)
-    _check(x, cb, got)
+    _check(x, cb, got, what="normalised image features 777x32 vs 4096")
 
 
 # ---------------------------------------------------------------- wide codes
@@ -111,7 +149,7 @@ def test_vq_bf16_wide_dims_match_oracle(ob, rows, dim, codes):
     got, norms = _gpu_quantize(ob, x, cb)
     assert np.array_equal(norms.float().cpu().numpy(), O.squares(cb, bf16=True))
     assert got[1] == min(9, codes - 1) or O.quantize(x[1:2], cb, bf16=True)[0] == got[1]
-    _check(x, cb, got)
+    _check(x, cb, got, what=f"bf16 wide rows={rows} dim={dim} codes={codes}")
 
 
 # ---------------------------------------------------------------- fp32 profile

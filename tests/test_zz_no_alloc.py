@@ -90,3 +90,9 @@ def test_no_alloc_rejects_batches_beyond_its_scratch(lib):
                                              MAX_ROWS + 1, 64, 300, 1, 0, stream)
     assert st == 1
     assert b"exceed" in lib.lib.omni_b200_last_error()
+    # A successful call after the rejected one leaves no stale message behind.
+    ok = torch.empty(8, dtype=torch.int32, device="cuda")
+    lib.check(lib.lib.omni_b200_vq_argmin_noalloc(x.data_ptr(), cb.data_ptr(), norms.data_ptr(), ok.data_ptr(),
+                                                  8, 64, 300, 1, 0, stream))
+    assert lib.lib.omni_b200_last_error() == b""
+    lib.sync_check(stream)
