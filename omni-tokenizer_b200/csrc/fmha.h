@@ -34,6 +34,23 @@ struct FmhaParams {
     int *err;
 };
 
+// Parameters of the fp32 split-precision kernel (fmha_f32_sm100.cu); tensor
+// maps over fp32 (d, token, head, batch) views with 32-column boxes.
+struct FmhaF32Params {
+    CUtensorMap tq, tk, tv;
+    void *out;
+    long long o_sb, o_sh, o_st; // output strides in elements (batch, head, token)
+    const int *lengths;         // [batch] valid key counts, or nullptr
+    int batch, heads, L, hd;
+    int valid;
+    int block;
+    int skip_padded_q;
+    int out_dtype;
+    int out_vec;
+    float scale_log2;
+    int *err;
+};
+
 struct FmhaArgs {
     const void *q_ptr = nullptr, *k_ptr = nullptr, *v_ptr = nullptr;
     TensorView q, k, v;
@@ -65,5 +82,13 @@ int attention_rows(const void *q, const void *k, const void *v, void *out, size_
                    cudaStream_t stream);
 bool tma_view_ok(const void *base, const TensorView &v);
 int padded_head_dim(int hd);
+
+// fp32 attention with split-precision (3 x tf32) tensor-core products.  The
+// views in `args` count fp32 elements; q, k, v must satisfy
+// tma_view_ok_f32 (16-byte aligned, strides multiples of 4 elements).  Head
+// dims up to 128 (padded to 32, 64 or 128).  Same return codes as fmha_launch.
+int fmha_f32_launch(const FmhaArgs &args, cudaStream_t stream);
+int padded_head_dim_f32(int hd);
+bool tma_view_ok_f32(const void *base, const TensorView &v);
 
 } // namespace omni_b200

@@ -568,9 +568,11 @@ Tensor attention(Context &c, const Tensor &q, const Tensor *k, const Tensor *v, 
                  const int *valid_dev) {
     const size_t rows = q.rows, n = rows / batch, d = fused ? q.cols / 3 : q.cols, hd = d / heads;
     Tensor y = c.make(rows, d, q.bf16);
-    if (!q.bf16 && !c.audio_bf16) {
-        // fp32 profile: per item, S = scale Q K^T for all heads (one strided
-        // batched fp32 GEMM), masked softmax in place, O = P V.
+    if (!q.bf16 && !c.audio_bf16 && padded_head_dim_f32(static_cast<int>(hd)) < 0) {
+        // fp32 profile with head dims beyond the fused kernel's 128: per item,
+        // S = scale Q K^T for all heads (one strided batched fp32 GEMM), masked
+        // softmax in place, O = P V.  Head dims up to 128 take the fused
+        // split-precision kernel through attention_rows below.
         require(!fused, "fp32 fused attention is not used by the graphs", OMNI_INTERNAL_ERROR);
         const long long nn = static_cast<long long>(n) * n;
         Tensor scores = c.make(batch * heads * n, n, false);

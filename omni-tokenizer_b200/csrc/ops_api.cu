@@ -74,16 +74,98 @@ int launch_status(int rc, const char *what) {
 namespace omni_b200 {
 
 size_t attention_rows_workspace(size_t rows, int heads, int head_dim, int dtype, int fused) {
-    const int hdp = padded_head_dim(head_dim);
-    if (hdp < 0 || heads <= 0 || rows == 0)
+    if (heads <= 0 || rows == 0)
         return 0;
     const long long d = static_cast<long long>(heads) * head_dim;
     const long long s_token = fused ? 3 * d : d;
-    const bool direct = dtype != OMNI_B200_F32 && head_dim % 8 == 0 && s_token % 8 == 0;
+    if (dtype == OMNI_B200_F32) {
+        // fp32 kernel: TMA reads rows whose head slices start on 16 bytes.
+        const int hdp = padded_head_dim_f32(head_dim);
+        if (hdp < 0 || (head_dim % 4 == 0 && head_dim >= 32 && s_token % 4 == 0))
+            return 0;
+        const size_t one = (rows * static_cast<size_t>(heads) * hdp * 4 + 255) / 256 * 256;
+        return 3 * one;
+    }
+    const int hdp = padded_head_dim(head_dim);
+    if (hdp < 0)
+        return 0;
+    const bool direct = head_dim % 8 == 0 && s_token % 8 == 0;
     if (direct)
         return 0;
     const size_t one = (rows * static_cast<size_t>(heads) * hdp * 2 + 255) / 256 * 256;
     return 3 * one;
+}
+
+// fp32 operands: the split-precision kernel (no conversion to 16-bit types),
+// reading the rows in place or from an fp32 packed copy.
+int attention_rows_f32(const void *qp, const void *kp, const void *vp, void *out, size_t n, int batch,
+                       int heads, int head_dim, long long s_token, size_t block, size_t valid,
+                       const int *lengths, int out_dtype, void *workspace, size_t workspace_bytes,
+                       cudaStream_t s) {
+    const int hdp = padded_head_dim_f32(head_dim);
+    if (hdp < 0)
+        return fail(4, "attention_rows: fp32 head_dim above 128 is not supported");
+    const size_t rows = n * static_cast<size_t>(batch);
+    const long long d = static_cast<long long>(heads) * head_dim;
+    TensorView view;
+    view.d = head_dim;
+    view.tokens = static_cast<int>(n);
+    view.heads = heads;
+    view.batch = batch;
+    view.s_token = s_token;
+    view.s_head = head_dim;
+    view.s_batch = s_token * static_cast<long long>(n);
+    FmhaArgs a;
+    // In place when every 32-column box starts inside the head (head_dim >= 32)
+    // and the rows are 16-byte aligned; otherwise an fp32 packed copy.
+    const bool direct = head_dim % 4 == 0 && head_dim >= 32 && tma_view_ok_f32(qp, view) &&
+                        tma_view_ok_f32(kp, view) && tma_view_ok_f32(vp, view);
+    if (direct) {
+        a.q_ptr = qp;
+        a.k_ptr = kp;
+        a.v_ptr = vp;
+        a.q = a.k = a.v = view;
+    } else {
+        const size_t one = (rows * static_cast<size_t>(heads) * hdp * 4 + 255) / 256 * 256;
+        if (!workspace || workspace_bytes < 3 * one)
+            return fail(1, "attention_rows: workspace too small (need " + std::to_string(3 * one) + " bytes)");
+        char *w = static_cast<char *>(workspace);
+        const void *src[3] = {qp, kp, vp};
+        for (int i = 0; i < 3; ++i) {
+            const int rc = pack_heads_f32(static_cast<const float *>(src[i]), s_token, head_dim,
+                                          static_cast<int>(rows), heads, head_dim, hdp,
+                                          reinterpret_cast<float *>(w + i * one), s);
+            if (rc)
+                return cuda_fail(static_cast<cudaError_t>(rc), "attention_rows: pack");
+        }
+        TensorView pv;
+        pv.d = hdp;
+        pv.tokens = static_cast<int>(n);
+        pv.heads = heads;
+        pv.batch = batch;
+        pv.s_token = hdp;
+        pv.s_head = static_cast<long long>(rows) * hdp;
+        pv.s_batch = static_cast<long long>(n) * hdp;
+        a.q_ptr = w;
+        a.k_ptr = w + one;
+        a.v_ptr = w + 2 * one;
+        a.q = a.k = a.v = pv;
+    }
+    a.out = out;
+    a.out_dtype = out_dtype;
+    a.o_st = d;
+    a.o_sh = head_dim;
+    a.o_sb = d * static_cast<long long>(n);
+    a.lengths = lengths;
+    a.valid = valid > n || valid == 0 ? static_cast<int>(n) : static_cast<int>(valid);
+    a.block = block > n ? static_cast<int>(n) : static_cast<int>(block);
+    a.skip_padded_q = 0;
+    a.scale = 1.0 / std::sqrt(static_cast<double>(head_dim));
+    a.out_d = head_dim;
+    a.err = kernel_error_word();
+    if (!a.err)
+        return fail(7, "attention_rows: no CUDA device");
+    return launch_status(fmha_f32_launch(a, s), "attention_rows");
 }
 
 // `batch` sequences of n tokens stacked as batch*n rows.  Items are contiguous
@@ -102,14 +184,17 @@ int attention_rows(const void *q, const void *k, const void *v, void *out, size_
     if (dtype < OMNI_B200_F32 || dtype > OMNI_B200_F16 || out_dtype < OMNI_B200_F32 ||
         out_dtype > OMNI_B200_F16)
         return fail(1, "attention_rows: invalid dtype");
-    const int hdp = padded_head_dim(head_dim);
-    if (hdp < 0)
-        return fail(4, "attention_rows: head_dim above 128 is not supported");
     const size_t rows = n * static_cast<size_t>(batch);
     const long long d = static_cast<long long>(heads) * head_dim;
     const long long s_token = fused ? 3 * d : d;
     const void *qp = q, *kp = fused ? static_cast<const char *>(q) + d * (dtype ? 2 : 4) : k,
                *vp = fused ? static_cast<const char *>(q) + 2 * d * (dtype ? 2 : 4) : v;
+    if (dtype == OMNI_B200_F32)
+        return attention_rows_f32(qp, kp, vp, out, n, batch, heads, head_dim, s_token, block, valid, lengths,
+                                  out_dtype, workspace, workspace_bytes, s);
+    const int hdp = padded_head_dim(head_dim);
+    if (hdp < 0)
+        return fail(4, "attention_rows: head_dim above 128 is not supported");
     FmhaArgs a;
     TensorView view;
     view.d = head_dim;
@@ -153,7 +238,7 @@ int attention_rows(const void *q, const void *k, const void *v, void *out, size_
         a.k_ptr = w + one;
         a.v_ptr = w + 2 * one;
         a.q = a.k = a.v = pv;
-        a.bf16 = dtype != OMNI_B200_F16;
+        a.bf16 = dtype == OMNI_B200_BF16;
     }
     a.out = out;
     a.out_dtype = out_dtype;
@@ -211,12 +296,14 @@ int omni_b200_attention_bhld(const void *q, const void *k, const void *v, void *
         return fail(1, "attention_bhld: null tensor pointer");
     if (batch <= 0 || heads <= 0 || L <= 0 || head_dim <= 0 || block < 0)
         return fail(1, "attention_bhld: sizes must be positive");
-    if (dtype != OMNI_B200_BF16 && dtype != OMNI_B200_F16)
-        return fail(1, "attention_bhld: dtype must be BF16 or F16");
+    if (dtype != OMNI_B200_BF16 && dtype != OMNI_B200_F16 && dtype != OMNI_B200_F32)
+        return fail(1, "attention_bhld: dtype must be BF16, F16 or F32");
     if (out_dtype < OMNI_B200_F32 || out_dtype > OMNI_B200_F16)
         return fail(1, "attention_bhld: invalid out_dtype");
-    if (head_dim > 128 || head_dim % 8 != 0)
-        return fail(4, "attention_bhld: head_dim must be a multiple of 8 in [8, 128]");
+    const bool f32 = dtype == OMNI_B200_F32;
+    if (head_dim > 128 || head_dim % (f32 ? 4 : 8) != 0)
+        return fail(4, f32 ? "attention_bhld: fp32 head_dim must be a multiple of 4 in [4, 128]"
+                           : "attention_bhld: head_dim must be a multiple of 8 in [8, 128]");
     FmhaArgs a;
     a.q_ptr = q;
     a.k_ptr = k;
@@ -230,7 +317,8 @@ int omni_b200_attention_bhld(const void *q, const void *k, const void *v, void *
     view.s_head = static_cast<long long>(L) * head_dim;
     view.s_batch = view.s_head * heads;
     a.q = a.k = a.v = view;
-    if (!tma_view_ok(q, view) || !tma_view_ok(k, view) || !tma_view_ok(v, view))
+    if (f32 ? (!tma_view_ok_f32(q, view) || !tma_view_ok_f32(k, view) || !tma_view_ok_f32(v, view))
+            : (!tma_view_ok(q, view) || !tma_view_ok(k, view) || !tma_view_ok(v, view)))
         return fail(1, "attention_bhld: q, k and v must be 16-byte aligned");
     a.bf16 = dtype == OMNI_B200_BF16;
     a.out = out;
@@ -246,6 +334,8 @@ int omni_b200_attention_bhld(const void *q, const void *k, const void *v, void *
     a.err = kernel_error_word();
     if (!a.err)
         return fail(7, "attention_bhld: no CUDA device");
+    if (f32)
+        return launch_status(fmha_f32_launch(a, static_cast<cudaStream_t>(stream)), "attention_bhld");
     return launch_status(fmha_launch(a, static_cast<cudaStream_t>(stream)), "attention_bhld");
 }
 

@@ -1,7 +1,8 @@
-// pack.cu -- repacks attention operands that TMA cannot read directly (fp32
-// inputs of the audio profile, head dims whose rows are not 16-byte multiples,
-// unaligned strides) into a head-major [heads, n, HDP] bf16 buffer with zero
-// padding beyond head_dim.  Replaces the role of pack_kernel in
+// pack.cu -- repacks attention operands that TMA cannot read directly (head
+// dims whose rows are not 16-byte multiples, unaligned strides) into a
+// head-major [heads, n, HDP] buffer with zero padding beyond head_dim: bf16 or
+// fp16 for the 2-byte kernel, fp32 (unchanged values) for the split-precision
+// fp32 kernel.  Replaces the role of pack_kernel in
 // omni-tokenizer src/cuda.cu:226-238 (which fed cuBLAS fp32 SGEMMs).
 #include "pack.h"
 
@@ -41,6 +42,32 @@ __global__ void pack_heads_kernel(const void *src, int dtype, long long s_token,
             dst[i] = *reinterpret_cast<uint32_t *>(&v);
         }
     }
+}
+
+// fp32 copy for the split-precision kernel: one thread per output element.
+__global__ void pack_heads_f32_kernel(const float *src, long long s_token, long long s_head, int n,
+                                      int heads, int hd, int hdp, float *dst) {
+    const long long total = static_cast<long long>(heads) * n * hdp;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int e = static_cast<int>(i % hdp);
+        const long long row = i / hdp; // h * n + t
+        const int t = static_cast<int>(row % n), h = static_cast<int>(row / n);
+        dst[i] = e < hd ? src[t * s_token + h * s_head + e] : 0.f;
+    }
+}
+
+int pack_heads_f32(const float *src, long long s_token, long long s_head, int n, int heads, int hd,
+                   int hdp, float *dst, cudaStream_t stream) {
+    const long long total = static_cast<long long>(heads) * n * hdp;
+    if (total == 0)
+        return 0;
+    long long blocks = (total + 255) / 256;
+    if (blocks > 148 * 16)
+        blocks = 148 * 16;
+    pack_heads_f32_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(src, s_token, s_head, n, heads,
+                                                                             hd, hdp, dst);
+    return static_cast<int>(cudaGetLastError());
 }
 
 int pack_heads(const void *src, int dtype, long long s_token, long long s_head, int n, int heads,

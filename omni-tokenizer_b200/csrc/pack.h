@@ -8,4 +8,7 @@ namespace omni_b200 {
 // source is f16), zero for e >= hd.
 int pack_heads(const void *src, int dtype, long long s_token, long long s_head, int n, int heads,
                int hd, int hdp, void *dst, cudaStream_t stream);
+// fp32 source, fp32 [heads, n, hdp] destination (values copied unchanged).
+int pack_heads_f32(const float *src, long long s_token, long long s_head, int n, int heads, int hd,
+                   int hdp, float *dst, cudaStream_t stream);
 } // namespace omni_b200

@@ -205,6 +205,14 @@ __device__ __forceinline__ void umma_ss_tf32_if(uint32_t issue, uint32_t d_tmem,
                  "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(issue)
                  : "memory");
 }
+// kind::tf32 with A (fp32 words, one per column) in tensor memory.
+__device__ __forceinline__ void umma_ts_tf32_if(uint32_t issue, uint32_t d_tmem, uint32_t a_tmem,
+                                                uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.b32 p, %4, 0;\n\tsetp.ne.b32 q, %5, 0;\n\t"
+                 "@q tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+                 "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(issue)
+                 : "memory");
+}
 __device__ __forceinline__ void umma_ts_if(uint32_t issue, uint32_t d_tmem, uint32_t a_tmem,
                                            uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
     asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.b32 p, %4, 0;\n\tsetp.ne.b32 q, %5, 0;\n\t"
@@ -301,10 +309,11 @@ __host__ __device__ constexpr uint32_t make_idesc_f16(int M, int N, bool bf16, b
            (static_cast<uint32_t>(M >> 4) << 24);
 }
 
-// Instruction descriptor of kind::tf32 (both operands K-major, fp32 accumulate).
-__host__ __device__ constexpr uint32_t make_idesc_tf32(int M, int N) {
-    return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
-           (static_cast<uint32_t>(M >> 4) << 24);
+// Instruction descriptor of kind::tf32 (fp32 accumulate; A K-major; B K-major,
+// or MN-major when b_mn_major -- a layout the ISA allows for tf32 sources).
+__host__ __device__ constexpr uint32_t make_idesc_tf32(int M, int N, bool b_mn_major = false) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | ((b_mn_major ? 1u : 0u) << 16) |
+           (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
 // Layout code of a row of `bytes` (32, 64 or 128) in the swizzled canonical forms.

@@ -66,6 +66,12 @@ int encode_tiled(CUtensorMap *map, const void *base, bool bf16, int rank, const 
                         rank, dims, byte_strides, box, swizzle_bytes);
 }
 
+int encode_tiled_f32(CUtensorMap *map, const void *base, int rank, const uint64_t *dims,
+                     const uint64_t *byte_strides, const uint32_t *box, int swizzle_bytes) {
+    return encode_typed(map, base, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, rank, dims, byte_strides, box,
+                        swizzle_bytes);
+}
+
 int make_map_2d_f32(CUtensorMap *map, const void *base, int cols, long long rows, int box_w,
                     int box_rows) {
     const uint64_t dims[2] = {static_cast<uint64_t>(cols), static_cast<uint64_t>(rows)};

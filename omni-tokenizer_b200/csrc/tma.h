@@ -10,6 +10,9 @@ namespace omni_b200 {
 // (32, 64 or 128) overrides the swizzle implied by the box row bytes.
 int encode_tiled(CUtensorMap *map, const void *base, bool bf16, int rank, const uint64_t *dims,
                  const uint64_t *byte_strides, const uint32_t *box, int swizzle_bytes = 0);
+// fp32 elements; the swizzle follows the box row bytes like encode_tiled.
+int encode_tiled_f32(CUtensorMap *map, const void *base, int rank, const uint64_t *dims,
+                     const uint64_t *byte_strides, const uint32_t *box, int swizzle_bytes = 0);
 // Row-major [rows, cols] matrix; box of box_w columns x box_rows rows.
 int make_map_2d(CUtensorMap *map, const void *base, int cols, long long rows, int box_w,
                 int box_rows, bool bf16 = true);

@@ -51,9 +51,12 @@ def test_argument_errors_need_no_device():
 
 def test_workspace_queries():
     lib = load_package().library()
-    # bf16 head-major rows of 72-wide heads need no repacking; fp32 rows do.
+    # bf16 rows of 72-wide heads and fp32 rows of 64-wide heads are read in
+    # place; fp32 heads of 7 (28-byte rows) are repacked to fp32 [heads, n, 32].
     assert lib.lib.omni_b200_attention_rows_workspace(729, 16, 72, 1, 0) == 0
-    assert lib.lib.omni_b200_attention_rows_workspace(1500, 20, 64, 0, 0) >= 3 * 20 * 1500 * 64 * 2
+    assert lib.lib.omni_b200_attention_rows_workspace(1500, 20, 64, 0, 0) == 0
+    assert lib.lib.omni_b200_attention_rows_workspace(129, 2, 7, 0, 0) >= 3 * 2 * 129 * 32 * 4
+    assert lib.lib.omni_b200_attention_rows_workspace(129, 2, 7, 1, 0) >= 3 * 2 * 129 * 16 * 2
     assert lib.lib.omni_b200_vq_workspace(1000, 64, 16384, 1) >= 8000
 
 

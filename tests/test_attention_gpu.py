@@ -232,3 +232,68 @@ def test_reference_fused_bf16_per_element(ob, n, heads):
     want = reference_rows_fp64(q, None, None, n, heads, hd, block, valid, True, rows)
     err = np.abs(got[rows].astype(np.float64) - want)
     assert err.max() <= 2e-3, f"n={n} heads={heads}: max error {err.max():.3e} at rows {rows}"
+
+
+# native_cuda_attention.cpp:233-242: the unfused fp32 list, bound 3e-6 per element.
+FP32_CASES = []
+for _n in (1, 129, 257, 511, 512, 513, 1500, 201, 401):
+    FP32_CASES += [(_n, 2, 7, 0, _n), (_n, 4, 64, 200, _n - 3 if _n > 3 else 1), (_n, 2, 7, 7, 1)]
+FP32_CASES.append((1, 4, 64, 200, 5))
+FP32_BOUND = 3e-6
+
+
+@pytest.mark.parametrize("n,heads,hd,block,valid", FP32_CASES)
+def test_reference_fp32_per_element(ob, n, heads, hd, block, valid):
+    """fp32 inputs run the split-precision (3 x tf32) kernel with no 16-bit
+    conversion; every element of the reference's boundary rows is within
+    3e-6 of the float64 attention of the same values."""
+    d = heads * hd
+    q = O.lcg_values(n * d, 123).reshape(n, d)
+    k = O.lcg_values(n * d, 456).reshape(n, d)
+    v = O.lcg_values(n * d, 789).reshape(n, d)
+    out = ob.attention_rows(torch.from_numpy(q).cuda(), torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda(),
+                            heads, block=block, valid=valid, out_dtype=torch.float32)
+    ob.library().sync_check()
+    got = out.cpu().numpy()
+    assert np.isfinite(got).all()
+    rows = reference_boundary_rows(n, block, valid)
+    want = reference_rows_fp64(q, k, v, n, heads, hd, block, valid, False, rows)
+    err = np.abs(got[rows].astype(np.float64) - want)
+    assert err.max() <= FP32_BOUND, f"n={n} heads={heads} hd={hd} block={block} valid={valid}: {err.max():.3e}"
+
+
+def _bhld_fp64(q, k, v, b, h, t, limit):
+    scale = np.float32(1) / np.sqrt(np.float32(q.shape[-1]))
+    a = (q[b, h, t] * scale).astype(np.float64)
+    s = k[b, h, :limit].astype(np.float64) @ a
+    p = np.exp(s - s.max())
+    return (p / p.sum()) @ v[b, h, :limit].astype(np.float64)
+
+
+@pytest.mark.parametrize("B,H,L,D,lengths,block", [
+    (3, 2, 700, 64, (100, 333, 700), 0),     # key padding (BASELINE config 3 semantics)
+    (2, 3, 1500, 64, (1500, 1203), 200),     # production audio: block-causal + valid prefix
+    (1, 2, 300, 128, None, 0),               # wide heads (32-key tiles)
+    (2, 2, 257, 32, (257, 5), 0),
+])
+def test_bhld_fp32_per_element(ob, B, H, L, D, lengths, block):
+    g = torch.Generator().manual_seed(L + D)
+    q, k, v = [torch.rand(B, H, L, D, generator=g) * 2 - 1 for _ in range(3)]
+    lt = torch.tensor(lengths, dtype=torch.int32).cuda() if lengths else None
+    out = ob.attention_bhld(q.cuda(), k.cuda(), v.cuda(), lengths=lt, block=block, out_dtype=torch.float32)
+    ob.library().sync_check()
+    got = out.cpu().numpy()
+    qn, kn, vn = q.numpy(), k.numpy(), v.numpy()
+    rng = np.random.default_rng(B * L)
+    worst = 0.0
+    for b in range(B):
+        valid = lengths[b] if lengths else L
+        for t in sorted({0, L - 1, valid - 1, *rng.integers(0, L, size=6).tolist()}):
+            limit = min(L, valid, (t // block + 1) * block if block else L)
+            for h in range(H):
+                want = _bhld_fp64(qn, kn, vn, b, h, t, limit)
+                worst = max(worst, float(np.abs(got[b, h, t] - want).max()))
+    assert worst <= FP32_BOUND, f"max error {worst:.3e}"
+    # The whole batch against the oracle (the reference's fp32 CPU arithmetic).
+    want = O.attention_bhld(qn, kn, vn, lengths=np.array(lengths, np.int32) if lengths else None, block=block)
+    assert np.abs(got - want).max() <= 1e-5
