@@ -354,13 +354,14 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_f32_kernel(const __grid_cons
                 }
             }
         };
-        // O (+)= P_b V_st: P hi / lo from TMEM, V MN-major (rows = keys) with its
-        // 32-column chunks KV_CHUNK bytes apart; per 8-key step the descriptor
-        // moves 8 rows = 1 KB.
+        // O (+)= P_b V_st: P hi / lo from TMEM, V MN-major (rows = keys) in the
+        // 128-byte swizzle of 32-byte atoms (the tf32 MN-major layout): 32-column
+        // chunks KV_CHUNK bytes apart (LBO), 4-row swizzle groups 512 bytes apart
+        // (SBO); per 8-key step the descriptor moves 8 rows = 1 KB.
         auto pv = [&](int b, int st, bool accumulate) {
             const uint32_t ph = S::kP + 2 * NK * b, pl = ph + NK;
-            const uint64_t vh = make_smem_desc(smem_u32(v_hi(st)), S::KV_CHUNK, 1024, kLayoutSW128);
-            const uint64_t vl = make_smem_desc(smem_u32(v_lo(st)), S::KV_CHUNK, 1024, kLayoutSW128);
+            const uint64_t vh = make_smem_desc(smem_u32(v_hi(st)), S::KV_CHUNK, 512, kLayoutSW128A32);
+            const uint64_t vl = make_smem_desc(smem_u32(v_lo(st)), S::KV_CHUNK, 512, kLayoutSW128A32);
 #pragma unroll
             for (int kk = 0; kk < NK / 8; ++kk) {
                 const uint64_t off = static_cast<uint64_t>((kk * 8 * 128) >> 4);
@@ -587,14 +588,15 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_f32_kernel(const __grid_cons
 }
 
 // 4-D (d, token, head, batch) fp32 map with a box of 32 columns x `rows`
-// tokens and 128-byte swizzle.
-int make_map_f32(CUtensorMap *map, const void *base, const TensorView &v, int rows) {
+// tokens: 128-byte swizzle (16-byte atoms) for the K-major operands Q and K,
+// 128-byte swizzle of 32-byte atoms for V (MN-major in O += P V).
+int make_map_f32(CUtensorMap *map, const void *base, const TensorView &v, int rows, bool mn_major = false) {
     const uint64_t dims[4] = {static_cast<uint64_t>(v.d), static_cast<uint64_t>(v.tokens),
                               static_cast<uint64_t>(v.heads), static_cast<uint64_t>(v.batch)};
     const uint64_t strides[3] = {static_cast<uint64_t>(v.s_token) * 4, static_cast<uint64_t>(v.s_head) * 4,
                                  static_cast<uint64_t>(v.s_batch) * 4};
     const uint32_t box[4] = {32u, static_cast<uint32_t>(rows), 1u, 1u};
-    return encode_tiled_f32(map, base, 4, dims, strides, box);
+    return encode_tiled_f32(map, base, 4, dims, strides, box, mn_major ? kSwizzle128Atom32 : 128);
 }
 
 template <int HDP, int NK> int launch(const FmhaArgs &a, FmhaF32Params &p, cudaStream_t stream) {
@@ -606,7 +608,7 @@ template <int HDP, int NK> int launch(const FmhaArgs &a, FmhaF32Params &p, cudaS
         return static_cast<int>(attr);
     int rc = 0;
     if ((rc = make_map_f32(&p.tq, a.q_ptr, a.q, 128)) || (rc = make_map_f32(&p.tk, a.k_ptr, a.k, NK)) ||
-        (rc = make_map_f32(&p.tv, a.v_ptr, a.v, NK)))
+        (rc = make_map_f32(&p.tv, a.v_ptr, a.v, NK, true)))
         return rc;
     static int sms = 0;
     if (!sms) {

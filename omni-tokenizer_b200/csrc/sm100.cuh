@@ -282,7 +282,9 @@ __device__ __forceinline__ void tmem_wait_st() {
 
 // ------------------------------------------------------------- descriptors --
 // Shared-memory matrix descriptor layout types (bits 61-63).
-enum : uint32_t { kLayoutNone = 0, kLayoutSW128 = 2, kLayoutSW64 = 4, kLayoutSW32 = 6 };
+// kLayoutSW128A32: 128-byte swizzle of 32-byte atoms (4-row pattern), the layout of
+// MN-major tf32 operands.
+enum : uint32_t { kLayoutNone = 0, kLayoutSW128A32 = 1, kLayoutSW128 = 2, kLayoutSW64 = 4, kLayoutSW32 = 6 };
 
 // UMMA shared-memory descriptor: start address (>>4) in bits 0-13, leading
 // byte offset (>>4) in 16-29, stride byte offset (>>4) in 32-45, descriptor

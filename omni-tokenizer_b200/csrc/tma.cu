@@ -34,6 +34,8 @@ CUtensorMapSwizzle swizzle_for(int row_bytes) {
 } // namespace
 
 namespace {
+// swizzle_bytes: 32, 64 or 128 (16-byte atoms), kSwizzle128Atom32 (128-byte span of
+// 32-byte atoms), or 0 to follow the box row bytes.
 int encode_typed(CUtensorMap *map, const void *base, CUtensorMapDataType type, int elem_bytes,
                  int rank, const uint64_t *dims, const uint64_t *byte_strides,
                  const uint32_t *box, int swizzle_bytes) {
@@ -53,7 +55,9 @@ int encode_typed(CUtensorMap *map, const void *base, CUtensorMapDataType type, i
     const CUresult r =
         fn(map, type, static_cast<cuuint32_t>(rank), const_cast<void *>(base), d, s, b, e,
            CU_TENSOR_MAP_INTERLEAVE_NONE,
-           swizzle_for(swizzle_bytes > 0 ? swizzle_bytes : static_cast<int>(box[0]) * elem_bytes),
+           swizzle_bytes == kSwizzle128Atom32
+               ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+               : swizzle_for(swizzle_bytes > 0 ? swizzle_bytes : static_cast<int>(box[0]) * elem_bytes),
            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? 0 : static_cast<int>(r) + 1000;
 }

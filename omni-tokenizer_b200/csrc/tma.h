@@ -10,7 +10,11 @@ namespace omni_b200 {
 // (32, 64 or 128) overrides the swizzle implied by the box row bytes.
 int encode_tiled(CUtensorMap *map, const void *base, bool bf16, int rank, const uint64_t *dims,
                  const uint64_t *byte_strides, const uint32_t *box, int swizzle_bytes = 0);
-// fp32 elements; the swizzle follows the box row bytes like encode_tiled.
+// swizzle_bytes value selecting the 128-byte swizzle of 32-byte atoms (the only
+// shared-memory layout the tensor cores read for MN-major tf32 operands).
+constexpr int kSwizzle128Atom32 = -32;
+// fp32 elements; the swizzle follows the box row bytes like encode_tiled unless
+// swizzle_bytes selects one (32, 64, 128 or kSwizzle128Atom32).
 int encode_tiled_f32(CUtensorMap *map, const void *base, int rank, const uint64_t *dims,
                      const uint64_t *byte_strides, const uint32_t *box, int swizzle_bytes = 0);
 // Row-major [rows, cols] matrix; box of box_w columns x box_rows rows.
