@@ -57,6 +57,12 @@ CONFIGS = {
                workload="SigLIP-shaped encoder self-attention op (BASELINE config 2)"),
     "c1": dict(kind="attn", B=1, H=20, L=1500, D=64, dtype="bf16", std=1.0, seed=1001,
                workload="Whisper-shaped encoder self-attention op (BASELINE config 1)"),
+    "c1_f32": dict(kind="attn", B=1, H=20, L=1500, D=64, dtype="f32", std=1.0, seed=1001,
+                   workload="Whisper-shaped encoder self-attention op (BASELINE config 1 shape) in fp32, the "
+                            "reference's audio-profile precision: split-precision (3 x tf32) tensor-core kernel"),
+    "c4_attn_f32": dict(kind="attn", B=16, H=16, L=1500, D=64, dtype="f32", std=1.0, seed=1004,
+                        workload="attention of the fp32 audio encoder (BASELINE config 4 shape: 16 segments, "
+                                 "16 heads, L 1500, head_dim 64), fp32 split-precision kernel"),
     "c3": dict(kind="attn", B=64, H=20, L=1500, D=64, dtype="bf16", std=1.0, seed=1003, varlen=(100, 1500),
                workload="variable-length audio attention batch, key-padding mask (BASELINE config 3)"),
     "vq_audio": dict(kind="vq", N=24000, K=16384, dim=64, seed=1010,
@@ -185,7 +191,7 @@ def attn_inputs(cfg, rank):
 
     B, H, L, D = cfg["B"], cfg["H"], cfg["L"], cfg["D"]
     g = torch.Generator().manual_seed(cfg["seed"] + 7919 * rank)
-    dt = torch.float16 if cfg["dtype"] == "f16" else torch.bfloat16
+    dt = {"f16": torch.float16, "bf16": torch.bfloat16, "f32": torch.float32}[cfg["dtype"]]
     qkv = [(torch.randn(B, H, L, D, generator=g) * cfg["std"]).to(dt).pin_memory() for _ in range(3)]
     lengths = None
     if cfg.get("varlen"):
@@ -636,7 +642,7 @@ def run_ours(args, cfg):
         out = torch.empty_like(q)
         dl = lengths.cuda() if lengths is not None else None
         B, H, L, D = cfg["B"], cfg["H"], cfg["L"], cfg["D"]
-        dt = 2 if cfg["dtype"] == "f16" else 1
+        dt = {"f16": 2, "bf16": 1, "f32": 0}[cfg["dtype"]]
         skip = 1 if lengths is not None else 0
         flops_step = attn_flops(cfg, lengths)
         launches_per_step = 1
@@ -742,6 +748,11 @@ def run_ours(args, cfg):
     e2e_value = flops_step * world / e2e_per_step / 1e12
     pk, pk_kind = peaks()
     peak = float(pk.get("bf16_tflops", 1590.0))
+    peak_source = f"{pk_kind} bf16_tflops (burst)"
+    if cfg.get("dtype") == "f32":
+        # Three tf32 MMAs per fp32 product, tf32 at half the bf16 rate.
+        peak /= 6.0
+        peak_source = f"{pk_kind} bf16_tflops (burst) / 6: three tf32 products per fp32 product at half the bf16 rate"
     achieved = flops_step / launch_s / 1e12
     traffic = None
     tf = ROOT / "profiles" / "traffic.json"
@@ -780,7 +791,7 @@ def run_ours(args, cfg):
             },
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": traffic,
-                         "peak_source": f"{pk_kind} bf16_tflops (burst)"},
+                         "peak_source": peak_source},
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": in_bytes,
                     "d2h_bytes_per_step": out_bytes},
             "cpu_baseline": cpu,
