@@ -1,15 +1,20 @@
 #!/usr/bin/env python
 """Benchmark of the omni-tokenizer hot path on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W]
-                    [--config c2|c1|c3|vq_audio|vq_image|c4|c4_bf16|c5] [--items N]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config NAME] [--items N]
                     [--impl ours|reference]
 
-Default workload (--config c2): BASELINE config 2, the SigLIP-shaped encoder
+Default run: the headline is BASELINE config 2, the SigLIP-shaped encoder
 self-attention op -- batch 32, 16 heads, L=729, head_dim 72, fp16 Q/K/V drawn
 N(0,1)*0.5 from a seed -- the configuration BASELINE.json's metric
 ("attn TFLOP/s vs B200 BF16 peak") is quoted on.  One step = one attention
 pass over that batch; FLOPs per step = 4*B*H*L^2*D (D = 72, not the padded 80).
+The same line carries, under "sub", one record per other configuration the
+metric names, each with its own roofline, cpu_baseline and e2e: c1 (Whisper
+shape, bf16), c1_f32 (the same shape in fp32, the reference's audio profile),
+c3 (variable-length audio batch), c5 (images/s of the whole image encoder),
+c4_bf16 and c4 (audio-s/s of the whole audio encoder, bf16 mode and the fp32
+profile).  --config NAME runs one configuration alone.
 
 * value  -- device-resident inputs, K steps timed with CUDA events between a
             barrier + synchronize on both sides, max over ranks, whole job.
@@ -18,22 +23,25 @@ pass over that batch; FLOPs per step = 4*B*H*L^2*D (D = 72, not the padded 80).
             pinned host memory to the device and the output back.
 * roofline -- algorithmic FLOPs per launch / mean kernel duration (CUDA events
             on the launching stream, measured in this run) vs the measured
-            dense bf16 peak in MEASURED_PEAKS.json.
+            dense bf16 peak in MEASURED_PEAKS.json (fp32 inputs: that peak / 6,
+            three tf32 products per fp32 product at half the bf16 rate).
 * cpu_baseline -- the reference's own CPU attention (src/cpu.cpp compiled into
             oracle/_ref) on the host cores, on a bounded sample (rank 0, N=1).
-Under torchrun (N > 1) every rank runs its own batch (weak scaling); there is
-no collective on the data path (timing uses one all-reduce of a scalar).
+Under torchrun (N > 1) the attention ops run one batch per rank (weak
+scaling), except c3, whose one 64-segment batch is split into length-balanced
+bins (strong scaling); the whole encoders split each step's items across
+ranks (strong scaling).  No collective sits on the data path (timing uses one
+all-reduce of a few scalars).
 
 --impl reference times the reference's CPU implementation (oracle/_ref, or
 the oracle port when the reference was not compiled here) on the same metric.
 
-Whole encoders (--config c4|c4_bf16|c5, BASELINE configs 4 and 5): a seeded
+Whole encoders (c4, c4_bf16, c5; BASELINE configs 4 and 5): a seeded
 random-weight OMNIVQ01 model of production shape is written per run and loaded
 through the omni_* C ABI of libomni_b200.so; value = items/s (images/s, or
 audio seconds/s) through the batched call on device-resident inputs, e2e = the
-same call on host buffers; items split evenly across ranks (strong scaling);
-the CPU baseline is the reference's own CPU library, extrapolated from 1- and
-2-layer models.
+same call on host buffers; the CPU baseline is the reference's own CPU
+library, extrapolated from 1- and 2-layer models.
 """
 
 from __future__ import annotations
@@ -64,6 +72,7 @@ CONFIGS = {
                         workload="attention of the fp32 audio encoder (BASELINE config 4 shape: 16 segments, "
                                  "16 heads, L 1500, head_dim 64), fp32 split-precision kernel"),
     "c3": dict(kind="attn", B=64, H=20, L=1500, D=64, dtype="bf16", std=1.0, seed=1003, varlen=(100, 1500),
+               shard="balanced",
                workload="variable-length audio attention batch, key-padding mask (BASELINE config 3)"),
     "vq_audio": dict(kind="vq", N=24000, K=16384, dim=64, seed=1010,
                      workload="VQ argmin op, audio-shaped (x 24000x64 vs codebook 16384x64, bf16)"),
@@ -186,26 +195,48 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ inputs
-def attn_inputs(cfg, rank):
+def attn_inputs(cfg, rank, world=1):
+    """Q, K, V (pinned host tensors) and the valid lengths of this rank's items.
+
+    Weak-scaling configs give every rank its own seeded batch.  The sharded
+    config (shard="balanced") draws one batch of B variable-length segments from
+    its seed -- every segment from a generator of its own, so the data do not
+    depend on the number of ranks -- and gives rank r the segments of bin r of
+    sharding.balanced_bins (greedy longest-first by L^2)."""
     import torch
 
     B, H, L, D = cfg["B"], cfg["H"], cfg["L"], cfg["D"]
-    g = torch.Generator().manual_seed(cfg["seed"] + 7919 * rank)
     dt = {"f16": torch.float16, "bf16": torch.bfloat16, "f32": torch.float32}[cfg["dtype"]]
+    if cfg.get("shard") == "balanced":
+        lo, hi = cfg["varlen"]
+        all_lengths = np.random.default_rng(cfg["seed"]).integers(lo, hi + 1, size=B).astype(np.int32)
+        load_package()
+        from omni_tokenizer_b200.sharding import balanced_bins
+
+        mine = balanced_bins(all_lengths.tolist(), world)[rank]
+        seg = []
+        for i in mine:
+            g = torch.Generator().manual_seed(cfg["seed"] * 1000 + i)
+            seg.append([torch.randn(1, H, L, D, generator=g) * cfg["std"] for _ in range(3)])
+        qkv = [torch.cat([s[j] for s in seg]).to(dt).pin_memory() for j in range(3)]
+        return qkv, torch.from_numpy(all_lengths[mine].copy()), all_lengths
+    g = torch.Generator().manual_seed(cfg["seed"] + 7919 * rank)
     qkv = [(torch.randn(B, H, L, D, generator=g) * cfg["std"]).to(dt).pin_memory() for _ in range(3)]
     lengths = None
     if cfg.get("varlen"):
         rng = np.random.default_rng(cfg["seed"] + 7919 * rank)
         lo, hi = cfg["varlen"]
         lengths = torch.from_numpy(rng.integers(lo, hi + 1, size=B).astype(np.int32))
-    return qkv, lengths
+    return qkv, lengths, None
 
 
-def attn_flops(cfg, lengths):
-    H, D, L, B = cfg["H"], cfg["D"], cfg["L"], cfg["B"]
+def attn_flops(cfg, lengths, batch=None):
+    """4 H D sum(L_i^2) over the items (valid query x valid key pairs for varlen)."""
+    H, D, L = cfg["H"], cfg["D"], cfg["L"]
     if lengths is not None:
-        return 4.0 * H * D * float(np.sum(lengths.numpy().astype(np.float64) ** 2))
-    return 4.0 * B * H * L * L * D
+        lens = lengths.numpy() if hasattr(lengths, "numpy") else np.asarray(lengths)
+        return 4.0 * H * D * float(np.sum(lens.astype(np.float64) ** 2))
+    return 4.0 * (cfg["B"] if batch is None else batch) * H * L * L * D
 
 
 def vq_inputs(cfg, rank):
@@ -380,65 +411,60 @@ def fp32_emulation_available():
     return hasattr(lib, "cublasSetEmulationStrategy")
 
 
-def run_encoder(args, cfg, reference=False):
+def run_encoder_reference(args, cfg):
+    """The reference arm of a whole-encoder config: its CPU library, rank 0 only."""
     import tempfile
+
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    unit_name, unit_per_item = encoder_unit(cfg)
+    tmpdir = tempfile.mkdtemp(prefix="omni_bench_")
+    # Each step is one item per model depth; the best of `steps` repeats counts.
+    got = cpu_encoder_sample(cfg, tmpdir, repeats=max(1, min(args.steps, 3)))
+    if got is None:
+        return {"impl": "reference", "unavailable": "reference CPU library oracle/_ref/libomni_ref_full.so not built"}
+    per_item, threads, sample = got
+    value = unit_per_item / per_item
+    return {
+        "impl": "reference", "metric": f"{unit_name} (full encoder)", "value": value, "unit": unit_name,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * per_item * cfg["items"], "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32" if cfg["modality"] == "audio" else "bf16",
+        "data": "synthetic (seeded U(-1,1) inputs, random-init weights)",
+        "config": {"workload": cfg["workload"], "config": args.config, "items_per_step": cfg["items"],
+                   "extrapolated": True},
+        "cpu_baseline": {"value": value, "unit": unit_name, "cores": threads, "kind": "reference", "sample": sample},
+        "e2e": {"value": value, "unit": unit_name, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+_CPU_ENCODER_CACHE = {}
+
+
+def run_encoder(args, name, cfg, dist, steps, warmup):
+    """One whole-encoder config on this rank's share of the step's items
+    (strong scaling).  Returns the JSON line on rank 0, None elsewhere."""
+    import tempfile
+
+    import torch
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     unit_name, unit_per_item = encoder_unit(cfg)
     flops_item = encoder_flops(cfg)
-    if reference and rank != 0:
-        return 0  # the reference arm runs on rank 0 only
     tmpdir = tempfile.mkdtemp(prefix="omni_bench_")
-    if reference:
-        # Each step is one item per model depth; the best of `steps` repeats counts.
-        got = cpu_encoder_sample(cfg, tmpdir, repeats=max(1, min(args.steps, 3)))
-        if got is None:
-            print(json.dumps({"impl": "reference", "unavailable": "reference CPU library oracle/_ref/"
-                              "libomni_ref_full.so not built"}), flush=True)
-            return 0
-        per_item, threads, sample = got
-        value = unit_per_item / per_item
-        line = {
-            "impl": "reference", "metric": f"{unit_name} (full encoder)", "value": value, "unit": unit_name,
-            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": 1e3 * per_item * cfg["items"], "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f32" if cfg["modality"] == "audio" else "bf16",
-            "data": "synthetic (seeded U(-1,1) inputs, random-init weights)",
-            "config": {"workload": cfg["workload"], "config": args.config, "items_per_step": cfg["items"],
-                       "extrapolated": True},
-            "cpu_baseline": {"value": value, "unit": unit_name, "cores": threads, "kind": "reference",
-                             "sample": sample},
-            "e2e": {"value": value, "unit": unit_name, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        }
-        print(json.dumps(line), flush=True)
-        return 0
-
-    # This library loads before torch, so that its cuBLAS (the toolkit's, with
-    # fp32 emulation) is the one the process binds rather than torch's older copy.
-    if cfg.get("audio_bf16"):
-        os.environ["OMNI_B200_AUDIO_BF16"] = "1"
     load_package()
     import omni_tokenizer_b200.abi as abi
 
+    os.environ["OMNI_B200_AUDIO_BF16"] = "1" if cfg.get("audio_bf16") else "0"
     lib = abi.OmniLib(ROOT / "omni-tokenizer_b200" / "libomni_b200.so")
     emulated = fp32_emulation_available() and os.environ.get("OMNI_B200_FP32_EMULATION", "") != "0"
-    import torch
-
-    torch.cuda.set_device(local)
-    dist = None
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
-                                device_id=torch.device("cuda", local))
     # Every rank writes the same seeded model into its own temporary directory
     # (no shared filesystem is assumed between ranks).
     ov, mc = encoder_model_config(cfg)
-    model_path = os.path.join(tmpdir, f"{args.config}.omni")
+    model_path = os.path.join(tmpdir, f"{name}.omni")
     t_write = time.perf_counter()
     ov.write_random_model(model_path, mc, seed=cfg["seed"])
     t_write = time.perf_counter() - t_write
@@ -454,11 +480,11 @@ def run_encoder(args, cfg, reference=False):
             dist.barrier()
         torch.cuda.synchronize()
 
-    def timed(fn, steps):
+    def timed(fn, n):
         barrier()
         t0 = time.perf_counter()
         out = 0
-        for _ in range(steps):
+        for _ in range(n):
             out += fn().nbytes
         torch.cuda.synchronize()
         dt = time.perf_counter() - t0
@@ -467,19 +493,19 @@ def run_encoder(args, cfg, reference=False):
 
     with lib.load(model_path, backend=abi.CUDA, device=local) as model:
         session = model.context()
-        for _ in range(max(args.warmup, 3)):
+        for _ in range(max(warmup, 3)):
             encode_batch(session, cfg, host, dev)
         sampler = ClockSampler(local)
         sampler.start()
         t_clock0 = time.perf_counter()
         # value: device-resident inputs through the batched extension.
-        elapsed, _ = timed(lambda: encode_batch(session, cfg, host, dev), args.steps)
+        elapsed, _ = timed(lambda: encode_batch(session, cfg, host, dev), steps)
         t_clock1 = time.perf_counter()
         sampler.stop()
         # e2e: host buffers through the same call (host-to-device copies inside),
         # after one untimed call that sizes the host path's staging buffers.
         encode_batch(session, cfg, host)
-        e2e_steps = max(1, min(args.steps, 3))
+        e2e_steps = max(1, min(steps, 3))
         e2e_elapsed, codes_bytes = timed(lambda: encode_batch(session, cfg, host), e2e_steps)
         # The reference's single-item calls on a sample of the rank's items (one
         # untimed call first, for the single-item shapes' buffers).
@@ -511,7 +537,7 @@ def run_encoder(args, cfg, reference=False):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         elapsed, e2e_elapsed, item_elapsed = t.tolist()
 
-    items_total = cfg["items"] * args.steps
+    items_total = cfg["items"] * steps
     value = items_total * unit_per_item / elapsed
     e2e_value = cfg["items"] * e2e_steps * unit_per_item / e2e_elapsed
     per_item_value = sample * world * unit_per_item / item_elapsed
@@ -520,70 +546,68 @@ def run_encoder(args, cfg, reference=False):
     peak = float(pk.get("bf16_tflops_sustained", pk.get("bf16_tflops", 1400.0)))
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        got = cpu_encoder_sample(cfg, tmpdir)
+        key = cfg["modality"]  # the reference's CPU profile: fp32 audio, bf16 image
+        if key not in _CPU_ENCODER_CACHE:
+            _CPU_ENCODER_CACHE[key] = cpu_encoder_sample(cfg, tmpdir)
+        got = _CPU_ENCODER_CACHE[key]
         if got is not None:
             per_item, threads, sample_text = got
             cpu = {"value": unit_per_item / per_item, "unit": unit_name, "cores": threads, "kind": "reference",
-                   "sample": sample_text}
+                   "sample": sample_text + ("; the reference runs audio in fp32 only" if cfg.get("audio_bf16")
+                                            else "")}
     in_item = int(np.prod(host.shape[1:])) * 4
-    if rank == 0:
-        line = {
-            "metric": f"{unit_name} (full encoder)",
-            "value": value,
-            "unit": unit_name,
-            "n_gpus": world,
-            "steps": args.steps,
-            "warmup": max(args.warmup, 3),
-            "ms_per_step": 1e3 * elapsed / args.steps,
-            "higher_is_better": True,
-            "scaling": "strong",
-            "vs_baseline": None,
-            "dtype": "f32" if (cfg["modality"] == "audio" and not cfg.get("audio_bf16")) else "bf16",
-            "data": "synthetic (seeded U(-1,1) inputs, random-init weights of the named shape)",
-            "config": {
-                "workload": cfg["workload"],
-                "config": args.config,
-                "items_per_step": cfg["items"],
-                "items_per_rank": share,
-                "flops_per_item": flops_item,
-                "parallelism": f"item-sharded replicas x{world}" if world > 1 else "single GPU",
-                "timing": "wall clock around the synchronous batched call omni_b200_encode_"
-                          + ("audio_batch" if cfg["modality"] == "audio" else "images")
-                          + " (device-resident inputs; codes copied back), synchronize + barrier on both sides, "
-                            "max over ranks; e2e: the same call on pinned host buffers",
-                "per_item_abi": {"value": per_item_value, "unit": unit_name, "items": sample,
-                                 "call": "omni_encode_" + cfg["modality"] + " (the reference's single-item call, "
-                                         "host buffers)"},
-                "fp32_gemms": ("BF16x9-emulated fp32 (cuBLAS)" if emulated else "fp32 on the CUDA cores")
-                              if cfg["modality"] == "audio" and not cfg.get("audio_bf16") else None,
-                "l2": "weights and activations far above L2 size per step; no flush",
-                "model_write_s": round(t_write, 1),
-                "peak_workspace_bytes": peak_ws,
-            },
-            "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak, "unit": "TFLOP/s",
-                         "frac": tflops / peak, "traffic": None,
-                         "peak_source": f"{pk_kind} bf16_tflops_sustained (whole-encoder FLOPs per GPU / wall time)"},
-            "e2e": {"value": e2e_value, "unit": unit_name, "h2d_bytes_per_step": in_item * cfg["items"],
-                    "d2h_bytes_per_step": codes_bytes // e2e_steps * world},
-            "cpu_baseline": cpu,
-            "gpu_launches": None if launches_step is None else launches_step * args.steps,
-            "library_launches": None if library_launches is None else library_launches * args.steps,
-            "clocks": clocks,
-        }
-        print(json.dumps(line), flush=True)
-    if dist is not None:
-        dist.barrier()
-        dist.destroy_process_group()
-    return 0
+    if rank != 0:
+        return None
+    return {
+        "metric": f"{unit_name} (full encoder)",
+        "value": value,
+        "unit": unit_name,
+        "n_gpus": world,
+        "steps": steps,
+        "warmup": max(warmup, 3),
+        "ms_per_step": 1e3 * elapsed / steps,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f32" if (cfg["modality"] == "audio" and not cfg.get("audio_bf16")) else "bf16",
+        "data": "synthetic (seeded U(-1,1) inputs, random-init weights of the named shape)",
+        "config": {
+            "workload": cfg["workload"],
+            "config": name,
+            "items_per_step": cfg["items"],
+            "items_per_rank": share,
+            "flops_per_item": flops_item,
+            "parallelism": f"item-sharded replicas x{world}" if world > 1 else "single GPU",
+            "timing": "wall clock around the synchronous batched call omni_b200_encode_"
+                      + ("audio_batch" if cfg["modality"] == "audio" else "images")
+                      + " (device-resident inputs; codes copied back), synchronize + barrier on both sides, "
+                        "max over ranks; e2e: the same call on pinned host buffers",
+            "per_item_abi": {"value": per_item_value, "unit": unit_name, "items": sample,
+                             "call": "omni_encode_" + cfg["modality"] + " (the reference's single-item call, "
+                                     "host buffers)"},
+            "fp32_gemms": ("BF16x9-emulated fp32 (cuBLAS)" if emulated else "fp32 on the CUDA cores")
+                          if cfg["modality"] == "audio" and not cfg.get("audio_bf16") else None,
+            "l2": "weights and activations far above L2 size per step; no flush",
+            "model_write_s": round(t_write, 1),
+            "peak_workspace_bytes": peak_ws,
+        },
+        "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak, "unit": "TFLOP/s",
+                     "frac": tflops / peak, "traffic": None,
+                     "peak_source": f"{pk_kind} bf16_tflops_sustained (whole-encoder FLOPs per GPU / wall time)"},
+        "e2e": {"value": e2e_value, "unit": unit_name, "h2d_bytes_per_step": in_item * cfg["items"],
+                "d2h_bytes_per_step": codes_bytes // e2e_steps * world},
+        "cpu_baseline": cpu,
+        "gpu_launches": None if launches_step is None else launches_step * steps,
+        "library_launches": None if library_launches is None else library_launches * steps,
+        "clocks": clocks,
+    }
 
 
 # ------------------------------------------------------------------ arms
 def run_reference(args, cfg):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
-        return 0
-    from oracle import oracle as O
-
+        return None
     # Size each step's sample so that warmup + steps end within ~2 minutes.
     probe_work, probe_t, threads, kind, _ = cpu_reference_sample(cfg, 0.0, items=1)
     per_unit = max(probe_t, 1e-4)
@@ -599,7 +623,7 @@ def run_reference(args, cfg):
         seconds += s
     value = work / seconds / 1e12
     unit = "TFLOP/s"
-    line = {
+    return {
         "impl": "reference", "metric": METRIC if cfg["kind"] == "attn" else "VQ TFLOP/s", "value": value,
         "unit": unit, "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1e3 * seconds / args.steps, "higher_is_better": True, "scaling": "weak",
@@ -608,28 +632,20 @@ def run_reference(args, cfg):
         "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": kind, "sample": sample},
         "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
-    return 0
 
 
-def run_ours(args, cfg):
+def run_ours(args, name, cfg, dist, steps, warmup):
+    """One op config (attention or VQ).  Returns the JSON line on rank 0."""
     import torch
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dist = None
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     ob = load_package()
     lib = ob.library()
     stream = torch.cuda.Stream()
     sp = stream.cuda_stream
+    strong = cfg.get("shard") == "balanced"
 
     def barrier():
         if dist is not None:
@@ -637,14 +653,17 @@ def run_ours(args, cfg):
         torch.cuda.synchronize()
 
     if cfg["kind"] == "attn":
-        (hq, hk, hv), lengths = attn_inputs(cfg, rank)
+        (hq, hk, hv), lengths, all_lengths = attn_inputs(cfg, rank, world)
         q, k, v = (t.cuda() for t in (hq, hk, hv))
         out = torch.empty_like(q)
         dl = lengths.cuda() if lengths is not None else None
-        B, H, L, D = cfg["B"], cfg["H"], cfg["L"], cfg["D"]
+        B, H, L, D = q.shape
         dt = {"f16": 2, "bf16": 1, "f32": 0}[cfg["dtype"]]
         skip = 1 if lengths is not None else 0
-        flops_step = attn_flops(cfg, lengths)
+        flops_step = attn_flops(cfg, lengths, batch=B)
+        # Whole-job FLOPs of one step: every rank's batch (weak), or the one
+        # sharded batch (strong).
+        job_flops_step = attn_flops(cfg, all_lengths) if strong else flops_step * world
         launches_per_step = 1
         in_bytes = 3 * q.numel() * q.element_size()
         out_bytes = out.numel() * out.element_size()
@@ -672,6 +691,7 @@ def run_ours(args, cfg):
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
         ids = torch.empty(N, dtype=torch.int32, device="cuda")
         flops_step = 2.0 * N * K * dim
+        job_flops_step = flops_step * world
         launches_per_step = 3
 
         def step():
@@ -690,7 +710,7 @@ def run_ours(args, cfg):
 
     # ---- warm-up
     with torch.cuda.stream(stream):
-        for _ in range(max(args.warmup, 3)):
+        for _ in range(max(warmup, 3)):
             step()
     lib.sync_check(sp)
 
@@ -702,7 +722,7 @@ def run_ours(args, cfg):
     t_wall0 = time.perf_counter()
     with torch.cuda.stream(stream):
         ev[0].record(stream)
-        for _ in range(args.steps):
+        for _ in range(steps):
             step()
         ev[1].record(stream)
     stream.synchronize()
@@ -714,7 +734,7 @@ def run_ours(args, cfg):
     # ---- per-launch duration of the dominant kernel (events around single launches)
     pairs = []
     with torch.cuda.stream(stream):
-        for _ in range(min(args.steps, 50)):
+        for _ in range(min(steps, 50)):
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(stream)
             step()
@@ -726,7 +746,7 @@ def run_ours(args, cfg):
     clocks = sampler.summary(t_wall0, t_wall1)
 
     # ---- end to end through the host-buffer C ABI
-    e2e_steps = max(3, min(args.steps, 30))
+    e2e_steps = max(3, min(steps, 30))
     with ob.Context(local) as ctx:
         e2e_step(ctx)  # allocate buffers
         barrier()
@@ -743,9 +763,8 @@ def run_ours(args, cfg):
     else:
         e2e_per_step = e2e_elapsed / e2e_steps
 
-    total_flops = flops_step * args.steps * world
-    value = total_flops / elapsed / 1e12
-    e2e_value = flops_step * world / e2e_per_step / 1e12
+    value = job_flops_step * steps / elapsed / 1e12
+    e2e_value = job_flops_step / e2e_per_step / 1e12
     pk, pk_kind = peaks()
     peak = float(pk.get("bf16_tflops", 1590.0))
     peak_source = f"{pk_kind} bf16_tflops (burst)"
@@ -754,11 +773,13 @@ def run_ours(args, cfg):
         peak /= 6.0
         peak_source = f"{pk_kind} bf16_tflops (burst) / 6: three tf32 products per fp32 product at half the bf16 rate"
     achieved = flops_step / launch_s / 1e12
-    traffic = None
+    traffic, traffic_source = None, None
     tf = ROOT / "profiles" / "traffic.json"
     if tf.is_file():
         try:
-            traffic = json.loads(tf.read_text()).get(args.config)
+            rec = json.loads(tf.read_text()).get(name)
+            if isinstance(rec, dict):
+                traffic, traffic_source = rec.get("bytes"), rec.get("source")
         except Exception:
             traffic = None
 
@@ -767,66 +788,122 @@ def run_ours(args, cfg):
         work, secs, threads, kind, sample = cpu_reference_sample(cfg, args.cpu_seconds)
         cpu = {"value": work / secs / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": kind, "sample": sample}
 
-    if rank == 0:
-        line = {
-            "metric": METRIC if cfg["kind"] == "attn" else "VQ TFLOP/s (distance GEMM + argmin)",
-            "value": value,
-            "unit": "TFLOP/s",
-            "n_gpus": world,
-            "steps": args.steps,
-            "warmup": max(args.warmup, 3),
-            "ms_per_step": 1e3 * elapsed / args.steps,
-            "higher_is_better": True,
-            "scaling": "weak",
-            "vs_baseline": None,
-            "dtype": dtype_name,
-            "data": "synthetic (seeded, BASELINE shapes)",
-            "config": {
-                "workload": cfg["workload"],
-                "config": args.config,
-                "per_gpu_flops_per_step": flops_step,
-                "parallelism": f"item-sharded replicas x{world}" if world > 1 else "single GPU",
-                "l2": f"working set {working_set / 2**20:.0f} MiB vs 126 MiB L2, no flush"
-                      if working_set > L2_BYTES else "working set below L2 size: L2-resident between steps",
-            },
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak, "traffic": traffic,
-                         "peak_source": peak_source},
-            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": in_bytes,
-                    "d2h_bytes_per_step": out_bytes},
-            "cpu_baseline": cpu,
-            "gpu_launches": launches_per_step * args.steps,
-            "clocks": clocks,
-        }
-        print(json.dumps(line), flush=True)
-    if dist is not None:
-        dist.barrier()
-        dist.destroy_process_group()
-    return 0
+    if rank != 0:
+        return None
+    return {
+        "metric": METRIC if cfg["kind"] == "attn" else "VQ TFLOP/s (distance GEMM + argmin)",
+        "value": value,
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": steps,
+        "warmup": max(warmup, 3),
+        "ms_per_step": 1e3 * elapsed / steps,
+        "higher_is_better": True,
+        "scaling": "strong" if strong else "weak",
+        "vs_baseline": None,
+        "dtype": dtype_name,
+        "data": "synthetic (seeded, BASELINE shapes)",
+        "config": {
+            "workload": cfg["workload"],
+            "config": name,
+            "per_gpu_flops_per_step": flops_step,
+            "job_flops_per_step": job_flops_step,
+            "parallelism": (f"one batch sharded over {world} ranks by length-balanced bins" if strong else
+                            f"item-sharded replicas x{world}") if world > 1 else "single GPU",
+            "l2": f"working set {working_set / 2**20:.0f} MiB vs 126 MiB L2, no flush"
+                  if working_set > L2_BYTES else "working set below L2 size: L2-resident between steps",
+        },
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "traffic": traffic, "traffic_source": traffic_source,
+                     "peak_source": peak_source},
+        "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": in_bytes,
+                "d2h_bytes_per_step": out_bytes},
+        "cpu_baseline": cpu,
+        "gpu_launches": launches_per_step * steps,
+        "clocks": clocks,
+    }
+
+
+# Sub-records of the default run: the other BASELINE configurations the metric
+# names (attention at the other shapes; images/s and audio-s/s of the whole
+# encoders), each with its own roofline, cpu_baseline and e2e.
+SUITE = ["c1", "c1_f32", "c3", "c5", "c4_bf16", "c4"]
+ENCODER_MAX_STEPS = 5
+
+
+def run_config(args, name, dist, steps, warmup):
+    cfg = dict(CONFIGS[name])
+    if cfg["kind"] == "encoder":
+        if args.items is not None and name == args.config:
+            cfg["items"] = args.items
+        return run_encoder(args, name, cfg, dist, steps, warmup)
+    return run_ours(args, name, cfg, dist, steps, warmup)
 
 
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
-    ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--config", default=None, choices=sorted(CONFIGS),
+                    help="run one configuration (default: c2 as the headline, the others as sub-records)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=5.0, help="CPU baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sub", action="store_true", help="default run: the headline line only")
     ap.add_argument("--items", type=int, default=None,
                     help="whole-encoder configs: items per step (default: the config's; smaller for profiling)")
     args = ap.parse_args()
-    cfg = dict(CONFIGS[args.config])
-    if args.items is not None:
-        if cfg["kind"] != "encoder" or args.items <= 0:
-            ap.error("--items applies to the whole-encoder configs and must be positive")
-        cfg["items"] = args.items
-    if cfg["kind"] == "encoder":
-        return run_encoder(args, cfg, reference=args.impl == "reference")
+    if args.items is not None and (args.config is None or CONFIGS[args.config]["kind"] != "encoder"
+                                   or args.items <= 0):
+        ap.error("--items applies to an explicit whole-encoder --config and must be positive")
     if args.impl == "reference":
-        return run_reference(args, cfg)
-    return run_ours(args, cfg)
+        cfg = dict(CONFIGS[args.config or "c2"])
+        if cfg["kind"] == "encoder":
+            line = run_encoder_reference(args, cfg)
+        else:
+            line = run_reference(args, cfg)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return 0
+    # This library loads before torch, so that its cuBLAS (the toolkit's, with
+    # fp32 emulation) is the one the process binds rather than torch's older copy.
+    load_package().library()
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    try:
+        if args.config is not None:
+            line = run_config(args, args.config, dist, args.steps, args.warmup)
+        else:
+            line = run_config(args, "c2", dist, args.steps, args.warmup)
+            if not args.no_sub:
+                subs = {}
+                for name in SUITE:
+                    enc = CONFIGS[name]["kind"] == "encoder"
+                    sub = run_config(args, name, dist, min(args.steps, ENCODER_MAX_STEPS) if enc else args.steps,
+                                     min(args.warmup, 3) if enc else args.warmup)
+                    if sub is not None:
+                        subs[name] = sub
+                if line is not None:
+                    line["sub"] = subs
+        if line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+    return 0
 
 
 if __name__ == "__main__":
