@@ -34,10 +34,15 @@ struct FmhaParams {
     int *err;
 };
 
-// Parameters of the fp32 split-precision kernel (fmha_f32_sm100.cu); tensor
-// maps over fp32 (d, token, head, batch) views with 32-column boxes.
+// Parameters of the fp32 split-precision kernel (fmha_f32_sm100.cu): tensor
+// maps of K and V over fp32 (d, token, head, batch) views with 32-column
+// boxes; Q is read row by row (one query row per thread).
 struct FmhaF32Params {
-    CUtensorMap tq, tk, tv;
+    CUtensorMap tk, tv;
+    const float *q;
+    long long q_sb, q_sh, q_st; // Q strides in elements (batch, head, token)
+    int q_d;                    // Q columns present (zero beyond)
+    int q_vec;                  // 16-byte loads allowed
     void *out;
     long long o_sb, o_sh, o_st; // output strides in elements (batch, head, token)
     const int *lengths;         // [batch] valid key counts, or nullptr

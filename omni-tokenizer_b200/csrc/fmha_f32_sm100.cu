@@ -8,24 +8,34 @@
 // src/cpu.cpp:122-172: O = softmax(scale Q K^T + mask) V per head, scale =
 // hd^-1/2, key limit limit(t) = min(L, valid[, (t/block + 1) block]).
 //
-// Split-precision products on the tcgen05 tensor cores.  Every fp32 operand x
-// is written as hi + lo with hi = x rounded to the nearest tf32 value (10
-// explicit mantissa bits) and lo = x - hi, itself rounded to the nearest tf32
-// value.  Then a b = ah bh + ah bl + al bh + al bl, and the three MMAs of kind::tf32
-// this kernel issues per product drop only al bl (at most 2^-22 |a b|) and the
-// rounding of the lo parts (at most 2^-22 |a| and 2^-22 |b| relative), so a
-// product carries a relative error of at most about 3 * 2^-22 = 7e-7, without
-// bias, while the accumulation runs in fp32 in TMEM.
+// Split-precision products on the tcgen05 tensor cores.  An fp32 operand x is
+// written as hi + lo with a tf32 hi and a tf32 lo (10 explicit mantissa bits
+// each), and a b = ah bh + ah bl + al bh + al bl, of which this kernel issues
+// the first three as MMAs of kind::tf32 accumulating in fp32 in TMEM.
+//   * Q (split in registers once per item, stored to TMEM): hi = x rounded
+//     to the nearest tf32 value, lo = x - hi (exact) rounded to the nearest
+//     tf32 value, so |lo| <= 2^-11 |x| with a random sign.
+//   * K, V and P: the tensor cores read an fp32 operand by dropping its low
+//     13 bits (truncation, measured on B200), so the fp32 value itself serves
+//     as hi = trunc(x), and only lo = x - trunc(x) (exact, |lo| < 2^-10 |x|)
+//     rounded to the nearest tf32 value is written beside it: K and V tiles
+//     are read once in shared memory and never rewritten, P is stored to TMEM
+//     as computed plus its lo part.
+// A product then drops al bl (at most 2^-21 |a b| in QK, where Q's lo has a
+// random sign; at most 2^-20 |a b| in PV) and the rounding of the lo parts
+// (at most 2^-21 relative each): a relative error of a few 1e-7 per product.
 //
 // One CTA owns 128 query rows of one (batch, head) per work item and streams
 // the keys in NK-key tiles (persistent grid, one CTA per SM):
-//   warp 8      TMA producer: raw fp32 Q tile per item, K_j / V_j per step
-//               into a ring of STAGES slots;
-//   warps 4-7   converters: split each raw tile in place into its hi part
-//               and write the lo part beside it (identical swizzled layouts,
-//               so the split is position-independent);
+//   warp 8      TMA producer: raw fp32 K_j / V_j into a ring of STAGES slots;
+//   warps 4-7   converters: write the lo part of each raw K / V tile beside
+//               it (identical swizzled layouts, so the split is
+//               position-independent); per item they
+//               also load the 128 query rows (thread = row = TMEM lane),
+//               split them and store Q hi / lo into TMEM;
 //   warp 9      TMEM owner and tcgen05.mma issuer:
-//                 S = Q K^T        (smem x smem, 3 MMAs per 8-wide K step),
+//                 S = Q K^T        (Q from TMEM x K from smem, 3 MMAs per
+//                                   8-wide K step),
 //                 O += P V         (P from TMEM x V from smem, V MN-major as
 //                                   loaded, 3 MMAs per 8-key step);
 //               issue order QK(g+1) before PV(g), so the next scores are
@@ -35,9 +45,12 @@
 //               hi/lo and stores both to TMEM, rescales O in TMEM when its max
 //               grew by more than 2^8 (lazy rescale), and finally normalises
 //               and stores its row of O.
-// S and P are double-buffered in TMEM (by the parity of the global step g);
-// the barriers of each buffer are separate so that every parity wait refers to
-// the barrier's most recent phase.
+// TMEM (512 columns at head_dim 64): Q hi | Q lo | S | P_0 hi, lo | P_1 hi, lo
+// | O.  Keeping Q in TMEM leaves shared memory to the K/V ring (3 stages of
+// 64 keys at head_dim 64), which hides the latency of a tile's load and split.
+// P is double-buffered by the parity of the global step g (single-buffered
+// where TMEM is short, head_dim 128); the barriers of each buffer are separate
+// so that every parity wait refers to the barrier's most recent phase.
 #include "fmha.h"
 #include "sm100.cuh"
 #include "tma.h"
@@ -49,27 +62,28 @@ namespace f32attn {
 
 template <int HDP, int NK> struct Shape {
     static constexpr int CH = HDP / 32;             // 128-byte column chunks (32 fp32)
-    static constexpr int Q_CHUNK = 128 * 128;       // bytes of one Q chunk (128 rows)
-    static constexpr int Q_BYTES = CH * Q_CHUNK;    // one of Q hi / Q lo
     static constexpr int KV_CHUNK = NK * 128;       // bytes of one K or V chunk (NK rows)
     static constexpr int KV_BYTES = CH * KV_CHUNK;  // one of K hi / K lo / V hi / V lo
     static constexpr int STAGE_BYTES = 4 * KV_BYTES;
     static constexpr int BAR_BYTES = 1024;
     static constexpr int BUDGET = 227 * 1024 - BAR_BYTES - 1024;
-    static constexpr int STAGES_RAW = (BUDGET - 2 * Q_BYTES) / STAGE_BYTES;
-    static constexpr int STAGES = STAGES_RAW > 4 ? 4 : STAGES_RAW;
-    static constexpr int SMEM_RAW = 2 * Q_BYTES + STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+    static constexpr int STAGES_RAW = BUDGET / STAGE_BYTES;
+    static constexpr int STAGES = STAGES_RAW > 6 ? 6 : STAGES_RAW;
+    static constexpr int SMEM_RAW = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
     // At least 120 KB so that one CTA (which allocates all 512 TMEM columns)
     // occupies an SM by itself.
     static constexpr int SMEM_BYTES = SMEM_RAW > 120 * 1024 ? SMEM_RAW : 120 * 1024;
-    // TMEM columns: S_b at kS + NK b; P_b hi at kP + 2 NK b, lo at + NK; O at kO.
-    static constexpr uint32_t kS = 0;
-    static constexpr uint32_t kP = 2 * NK;
-    static constexpr uint32_t kO = 6 * NK;
+    // TMEM columns: Q hi at kQ, Q lo at kQ + HDP, S at kS, P_b hi at kP + 2 NK b
+    // (lo at + NK), O at kO.
+    static constexpr int PBUF = 2 * HDP + NK + 4 * NK + HDP <= 512 ? 2 : 1;
+    static constexpr uint32_t kQ = 0;
+    static constexpr uint32_t kS = 2 * HDP;
+    static constexpr uint32_t kP = 2 * HDP + NK;
+    static constexpr uint32_t kO = kP + 2 * NK * PBUF;
     static_assert(HDP % 32 == 0 && HDP <= 128, "head dim padding must be 32, 64, 96 or 128");
     static_assert(NK % 32 == 0 && NK >= 32 && NK <= 128, "key tile must be 32, 64, 96 or 128");
     static_assert(kO + HDP <= 512, "TMEM budget");
-    static_assert(STAGES >= 1, "shared memory budget");
+    static_assert(STAGES >= 2, "shared memory budget");
 };
 
 constexpr int kSoftWarps = 4;
@@ -116,26 +130,31 @@ template <int NK> __device__ __forceinline__ int next_work_item(const FmhaF32Par
 // dropped 13-bit field to the magnitude, then clear it.
 __device__ __forceinline__ uint32_t tf32_round_bits(uint32_t x) { return (x + 0x1000u) & 0xFFFFE000u; }
 
+// x = hi + lo with hi the nearest tf32 value (Q and P, stored to TMEM).
 __device__ __forceinline__ void split_tf32(float x, float &hi, float &lo) {
     hi = __uint_as_float(tf32_round_bits(__float_as_uint(x)));
     lo = __uint_as_float(tf32_round_bits(__float_as_uint(x - hi))); // x - hi is exact
 }
 
-// Splits a raw fp32 tile of `bytes` bytes at `hi` in place and writes the lo
-// parts at the same offsets under `lo`; the 128 converter threads stride over
-// its 16-byte chunks.
-__device__ __forceinline__ void split_tile(uint8_t *hi, uint8_t *lo, int bytes, int tid) {
-    float4 *h4 = reinterpret_cast<float4 *>(hi);
+// The part of x that the tensor cores drop when they read x as tf32
+// (truncation), rounded to the nearest tf32 value.
+__device__ __forceinline__ float tf32_lo_of_trunc(float x) {
+    const float hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+    return __uint_as_float(tf32_round_bits(__float_as_uint(x - hi))); // x - hi is exact
+}
+
+// Writes the lo parts of a raw fp32 tile of `bytes` bytes at `raw` to the same
+// offsets under `lo` (identical swizzled layouts); the raw tile stays as it is
+// and serves as the hi operand.  The 128 converter threads stride over its
+// 16-byte chunks.
+__device__ __forceinline__ void split_tile(const uint8_t *raw, uint8_t *lo, int bytes, int tid) {
+    const float4 *r4 = reinterpret_cast<const float4 *>(raw);
     float4 *l4 = reinterpret_cast<float4 *>(lo);
+#pragma unroll 4
     for (int i = tid; i < bytes / 16; i += 128) {
-        const float4 v = h4[i];
-        float4 h, l;
-        split_tf32(v.x, h.x, l.x);
-        split_tf32(v.y, h.y, l.y);
-        split_tf32(v.z, h.z, l.z);
-        split_tf32(v.w, h.w, l.w);
-        h4[i] = h;
-        l4[i] = l;
+        const float4 v = r4[i];
+        l4[i] = make_float4(tf32_lo_of_trunc(v.x), tf32_lo_of_trunc(v.y), tf32_lo_of_trunc(v.z),
+                            tf32_lo_of_trunc(v.w));
     }
 }
 
@@ -178,23 +197,20 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_f32_kernel(const __grid_cons
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    uint8_t *sQh = smem;                 // Q hi (raw fp32 as loaded, then split in place)
-    uint8_t *sQl = sQh + S::Q_BYTES;     // Q lo
-    uint8_t *sKV = sQl + S::Q_BYTES;     // [STAGES] x (K hi, K lo, V hi, V lo)
+    uint8_t *sKV = smem;                 // [STAGES] x (K hi, K lo, V hi, V lo)
     uint64_t *bars = reinterpret_cast<uint64_t *>(sKV + S::STAGES * S::STAGE_BYTES);
-    uint64_t *q_full = bars;             // Q tile landed
-    uint64_t *q_ready = bars + 1;        // Q split (4 converter warps)
-    uint64_t *q_empty = bars + 2;        // every QK of the item done (commit)
-    uint64_t *k_full = bars + 3;         // [STAGES]
-    uint64_t *k_ready = k_full + 4;      // [STAGES]
-    uint64_t *k_empty = k_ready + 4;     // [STAGES]
-    uint64_t *v_full = k_empty + 4;      // [STAGES]
-    uint64_t *v_ready = v_full + 4;      // [STAGES]
-    uint64_t *v_empty = v_ready + 4;     // [STAGES]
-    uint64_t *s_full = v_empty + 4;      // [2] S_b computed (commit)
-    uint64_t *s_free = s_full + 2;       // [2] softmax read S_b (4 warps)
-    uint64_t *p_full = s_free + 2;       // [2] P_b stored (4 warps)
-    uint64_t *pv_done = p_full + 2;      // [2] O += P_b V complete (commit)
+    uint64_t *q_full = bars;             // Q hi / lo stored in TMEM (4 converter warps)
+    uint64_t *q_free = bars + 1;         // every QK of the item done (commit)
+    uint64_t *k_full = bars + 2;         // [STAGES] K tile landed
+    uint64_t *k_ready = k_full + 6;      // [STAGES] K tile split
+    uint64_t *k_empty = k_ready + 6;     // [STAGES] QK done with the slot (commit)
+    uint64_t *v_full = k_empty + 6;      // [STAGES]
+    uint64_t *v_ready = v_full + 6;      // [STAGES]
+    uint64_t *v_empty = v_ready + 6;     // [STAGES]
+    uint64_t *s_full = v_empty + 6;      // S computed (commit)
+    uint64_t *s_free = s_full + 1;       // softmax read S (4 warps)
+    uint64_t *p_full = s_free + 1;       // [PBUF] P_b stored (4 warps)
+    uint64_t *pv_done = p_full + 2;      // [PBUF] O += P_b V complete (commit)
     uint64_t *drain = pv_done + 2;
     uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(drain + 1);
     auto k_hi = [&](int st) { return sKV + st * S::STAGE_BYTES; };
@@ -207,9 +223,8 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_f32_kernel(const __grid_cons
     int *err = p.err;
 
     if (threadIdx.x == 0) {
-        mbar_init(q_full, 1);
-        mbar_init(q_ready, 4);
-        mbar_init(q_empty, 1);
+        mbar_init(q_full, 4);
+        mbar_init(q_free, 1);
         for (int s = 0; s < S::STAGES; ++s) {
             mbar_init(&k_full[s], 1);
             mbar_init(&k_ready[s], 4);
@@ -218,9 +233,9 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_f32_kernel(const __grid_cons
             mbar_init(&v_ready[s], 4);
             mbar_init(&v_empty[s], 1);
         }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(&s_full[b], 1);
-            mbar_init(&s_free[b], kSoftWarps);
+        mbar_init(s_full, 1);
+        mbar_init(s_free, kSoftWarps);
+        for (int b = 0; b < S::PBUF; ++b) {
             mbar_init(&p_full[b], kSoftWarps);
             mbar_init(&pv_done[b], 1);
         }
@@ -236,7 +251,7 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_f32_kernel(const __grid_cons
     tc_fence_after();
     const uint32_t tmem = *tmem_holder;
     if (tmem != 0) {
-        // The MMA issuer and the softmax address TMEM from column 0 of lane 0.
+        // The MMA issuer, softmax and converters address TMEM from column 0 of lane 0.
         if (threadIdx.x == 0)
             atomicOr(err, kErrWaitDrain);
         __syncthreads();
@@ -244,29 +259,23 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_f32_kernel(const __grid_cons
             tmem_dealloc(tmem, 512);
         return;
     }
+    // O += P_gp V of global step gp is complete: pv_done[gp % PBUF] has
+    // completed once for every earlier step of the same buffer.
+    auto wait_pv = [&](int gp) {
+        return wait_all(&pv_done[gp % S::PBUF], (gp / S::PBUF) & 1, err, kErrWaitO);
+    };
 
     if (warp == kProducerWarp) {
         // ------------------------------------------------------ TMA producer
         if (elect_one()) {
-            tma_prefetch_desc(&p.tq);
             tma_prefetch_desc(&p.tk);
             tma_prefetch_desc(&p.tv);
         }
-        int nq = 0, nk = 0, nv = 0; // Q loads, K loads, V loads issued
+        int nk = 0, nv = 0; // K loads, V loads issued
         bool ok = true;
         for (int u = next_work_item<NK>(p, blockIdx.x, items); ok && u < items;
              u = next_work_item<NK>(p, u + gridDim.x, items)) {
             const Item it = decode_item<NK>(p, u);
-            if (!(ok = wait_all(q_empty, (nq & 1) ^ 1, err, kErrWaitEmpty)))
-                break;
-            if (elect_one()) {
-                mbar_arrive_expect_tx(q_full, S::Q_BYTES);
-#pragma unroll
-                for (int c = 0; c < S::CH; ++c)
-                    tma_load_4d(sQh + c * S::Q_CHUNK, &p.tq, q_full, 32 * c, it.q0, it.h, it.b);
-            }
-            __syncwarp();
-            ++nq;
             for (int j = 0; j < it.T; ++j) {
                 const int st = nk % S::STAGES;
                 const uint32_t ph = (nk / S::STAGES) & 1;
@@ -293,40 +302,84 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_f32_kernel(const __grid_cons
             }
         }
         // Every issued copy must land before the CTA may exit.
-        if (nq > 0)
-            wait_drain(q_full, (nq - 1) & 1, err);
         for (int m = nk - S::STAGES < 0 ? 0 : nk - S::STAGES; m < nk; ++m)
             wait_drain(&k_full[m % S::STAGES], (m / S::STAGES) & 1, err);
         for (int m = nv - S::STAGES < 0 ? 0 : nv - S::STAGES; m < nv; ++m)
             wait_drain(&v_full[m % S::STAGES], (m / S::STAGES) & 1, err);
     } else if (warp >= kConvWarp0 && warp < kConvWarp0 + 4) {
         // -------------------------------------------------------- converters
-        const int tid = threadIdx.x - kConvWarp0 * 32;
+        const int tid = threadIdx.x - kConvWarp0 * 32;  // = query row in the tile = TMEM lane
+        const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
         int nq = 0, n = 0;
         bool ok = true;
+        auto split_k = [&](int g) {
+            const int st = g % S::STAGES;
+            if (!wait_all(&k_full[st], (g / S::STAGES) & 1, err, kErrWaitK))
+                return false;
+            split_tile(k_hi(st), k_lo(st), S::KV_BYTES, tid);
+            fence_proxy_async_smem();
+            warp_arrive(&k_ready[st]);
+            return true;
+        };
+        auto split_v = [&](int g) {
+            const int st = g % S::STAGES;
+            if (!wait_all(&v_full[st], (g / S::STAGES) & 1, err, kErrWaitV))
+                return false;
+            split_tile(v_hi(st), v_lo(st), S::KV_BYTES, tid);
+            fence_proxy_async_smem();
+            warp_arrive(&v_ready[st]);
+            return true;
+        };
         for (int u = next_work_item<NK>(p, blockIdx.x, items); ok && u < items;
              u = next_work_item<NK>(p, u + gridDim.x, items)) {
             const Item it = decode_item<NK>(p, u);
-            if (!(ok = wait_all(q_full, nq & 1, err, kErrWaitQ)))
-                break;
-            split_tile(sQh, sQl, S::Q_BYTES, tid);
-            fence_proxy_async_smem();
-            warp_arrive(q_ready);
-            ++nq;
-            for (int j = 0; j < it.T; ++j, ++n) {
-                const int st = n % S::STAGES;
-                const uint32_t ph = (n / S::STAGES) & 1;
-                if (!(ok = wait_all(&k_full[st], ph, err, kErrWaitK)))
-                    break;
-                split_tile(k_hi(st), k_lo(st), S::KV_BYTES, tid);
-                fence_proxy_async_smem();
-                warp_arrive(&k_ready[st]);
-                if (!(ok = wait_all(&v_full[st], ph, err, kErrWaitV)))
-                    break;
-                split_tile(v_hi(st), v_lo(st), S::KV_BYTES, tid);
-                fence_proxy_async_smem();
-                warp_arrive(&v_ready[st]);
+            // This thread's query row, loaded now so that the global-memory
+            // latency overlaps the split of the item's first K tile.
+            float qraw[HDP];
+            const int t = it.q0 + tid;
+            const float *qrow = p.q + it.b * p.q_sb + it.h * p.q_sh + static_cast<long long>(t) * p.q_st;
+            if (t < p.L && p.q_vec) {
+#pragma unroll
+                for (int e = 0; e < HDP; e += 4) {
+                    const float4 v = e < p.q_d ? *reinterpret_cast<const float4 *>(qrow + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    qraw[e] = v.x;
+                    qraw[e + 1] = v.y;
+                    qraw[e + 2] = v.z;
+                    qraw[e + 3] = v.w;
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < HDP; ++e)
+                    qraw[e] = (t < p.L && e < p.q_d) ? qrow[e] : 0.f;
             }
+            if (!(ok = split_k(n)))
+                break;
+            // Q hi / lo into TMEM once every QK of the previous item is done.
+            if (nq > 0 && !(ok = wait_all(q_free, (nq - 1) & 1, err, kErrWaitQ)))
+                break;
+            tc_fence_after();
+#pragma unroll
+            for (int c = 0; c < HDP / 16; ++c) {
+                uint32_t hi[16], lo[16];
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    float h, lw;
+                    split_tf32(qraw[16 * c + e], h, lw);
+                    hi[e] = __float_as_uint(h);
+                    lo[e] = __float_as_uint(lw);
+                }
+                tmem_st16(tmem + lane_base + S::kQ + 16 * c, hi);
+                tmem_st16(tmem + lane_base + S::kQ + HDP + 16 * c, lo);
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            warp_arrive(q_full);
+            ++nq;
+            if (!(ok = split_v(n)))
+                break;
+            ++n;
+            for (int j = 1; ok && j < it.T; ++j, ++n)
+                ok = split_k(n) && split_v(n);
         }
     } else if (warp == kMmaWarp) {
         // ------------------------------------------------------- MMA issuer
@@ -335,23 +388,18 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_f32_kernel(const __grid_cons
         constexpr uint32_t idesc_qk = make_idesc_tf32(128, NK);
         constexpr uint32_t idesc_pv = make_idesc_tf32(128, HDP, true);
         const uint32_t leader = elect_one() ? 1u : 0u;
-        const uint32_t sqh = smem_u32(sQh), sql = smem_u32(sQl);
         auto commit = [&](uint64_t *bar) { tc_commit_if(leader, bar); };
-        // S_b = Q K_st^T: per 8-wide K step hi*lo, lo*hi, then hi*hi.
-        auto qk = [&](int b, int st) {
-            const uint32_t d = S::kS + NK * b;
+        // S = Q K_st^T: Q hi / lo from TMEM (one column per element), K
+        // K-major in smem; per 8-wide K step hi*lo, lo*hi, then hi*hi.
+        auto qk = [&](int st) {
 #pragma unroll
-            for (int c = 0; c < S::CH; ++c) {
-                const uint64_t ah = make_smem_desc(sqh + c * S::Q_CHUNK, 16, 1024, kLayoutSW128);
-                const uint64_t al = make_smem_desc(sql + c * S::Q_CHUNK, 16, 1024, kLayoutSW128);
-                const uint64_t bh = make_smem_desc(smem_u32(k_hi(st)) + c * S::KV_CHUNK, 16, 1024, kLayoutSW128);
-                const uint64_t bl = make_smem_desc(smem_u32(k_lo(st)) + c * S::KV_CHUNK, 16, 1024, kLayoutSW128);
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk) { // 4 x 8 fp32 = one 128-byte chunk
-                    umma_ss_tf32_if(leader, d, ah + 2 * kk, bl + 2 * kk, idesc_qk, (c > 0 || kk > 0) ? 1u : 0u);
-                    umma_ss_tf32_if(leader, d, al + 2 * kk, bh + 2 * kk, idesc_qk, 1u);
-                    umma_ss_tf32_if(leader, d, ah + 2 * kk, bh + 2 * kk, idesc_qk, 1u);
-                }
+            for (int kk = 0; kk < HDP / 8; ++kk) {
+                const int c = kk >> 2, k4 = kk & 3; // 128-byte chunk, 32-byte step inside it
+                const uint64_t bh = make_smem_desc(smem_u32(k_hi(st)) + c * S::KV_CHUNK, 16, 1024, kLayoutSW128) + 2 * k4;
+                const uint64_t bl = make_smem_desc(smem_u32(k_lo(st)) + c * S::KV_CHUNK, 16, 1024, kLayoutSW128) + 2 * k4;
+                umma_ts_tf32_if(leader, S::kS, S::kQ + 8 * kk, bl, idesc_qk, kk > 0 ? 1u : 0u);
+                umma_ts_tf32_if(leader, S::kS, S::kQ + HDP + 8 * kk, bh, idesc_qk, 1u);
+                umma_ts_tf32_if(leader, S::kS, S::kQ + 8 * kk, bh, idesc_qk, 1u);
             }
         };
         // O (+)= P_b V_st: P hi / lo from TMEM, V MN-major (rows = keys) in the
@@ -374,10 +422,10 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_f32_kernel(const __grid_cons
         bool ok = true;
         bool pending = false; // a PV of step g - 1 still to issue
         bool pending_acc = false;
-        // Issues O += P(g-1) V(g-1).
+        // Issues O += P(gp) V(gp).
         auto issue_pv = [&](int gp, bool acc) {
-            const int b = gp & 1, st = gp % S::STAGES;
-            if (!wait_all(&p_full[b], (gp >> 1) & 1, err, kErrWaitP))
+            const int b = gp % S::PBUF, st = gp % S::STAGES;
+            if (!wait_all(&p_full[b], (gp / S::PBUF) & 1, err, kErrWaitP))
                 return false;
             if (!wait_all(&v_ready[st], (gp / S::STAGES) & 1, err, kErrWaitV))
                 return false;
@@ -390,21 +438,21 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_f32_kernel(const __grid_cons
         for (int u = next_work_item<NK>(p, blockIdx.x, items); ok && u < items;
              u = next_work_item<NK>(p, u + gridDim.x, items)) {
             const Item it = decode_item<NK>(p, u);
-            if (!(ok = wait_all(q_ready, nq & 1, err, kErrWaitQ)))
+            if (!(ok = wait_all(q_full, nq & 1, err, kErrWaitQ)))
                 break;
             ++nq;
             for (int j = 0; j < it.T; ++j, ++g) {
-                const int b = g & 1, st = g % S::STAGES;
-                if (g >= 2 && !(ok = wait_all(&s_free[b], ((g - 2) >> 1) & 1, err, kErrWaitS)))
+                const int st = g % S::STAGES;
+                if (g >= 1 && !(ok = wait_all(s_free, (g - 1) & 1, err, kErrWaitS)))
                     break;
                 if (!(ok = wait_all(&k_ready[st], (g / S::STAGES) & 1, err, kErrWaitK)))
                     break;
                 tc_fence_after();
-                qk(b, st);
-                commit(&s_full[b]);
+                qk(st);
+                commit(s_full);
                 commit(&k_empty[st]);
                 if (j + 1 == it.T)
-                    commit(q_empty); // the item's Q is no longer read
+                    commit(q_free); // the item's Q is no longer read
                 if (pending && !(ok = issue_pv(g - 1, pending_acc)))
                     break;
                 pending = true;
@@ -433,19 +481,18 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_f32_kernel(const __grid_cons
                 limit = min(limit, (t / p.block + 1) * p.block);
             float m = -INFINITY, l = 0.f;
             for (int j = 0; j < it.T; ++j, ++g) {
-                const int b = g & 1;
-                if (!(ok = wait_all(&s_full[b], (g >> 1) & 1, err, kErrWaitS)))
+                const int b = g % S::PBUF;
+                if (!(ok = wait_all(s_full, g & 1, err, kErrWaitS)))
                     break;
                 tc_fence_after();
                 uint32_t sraw[NK];
 #pragma unroll
                 for (int c = 0; c < NK / 32; ++c)
-                    tmem_ld32(tmem + lane_base + S::kS + NK * b + 32 * c,
-                              *reinterpret_cast<uint32_t(*)[32]>(&sraw[32 * c]));
-                float *s = reinterpret_cast<float *>(sraw);
+                    tmem_ld32(tmem + lane_base + S::kS + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&sraw[32 * c]));
                 tmem_wait_ld();
                 tc_fence_before();
-                warp_arrive(&s_free[b]); // S_b may be overwritten by QK(g + 2)
+                warp_arrive(s_free); // S may be overwritten by QK(g + 1)
+                float *s = reinterpret_cast<float *>(sraw);
                 const int kv0 = j * NK;
                 if (kv0 + NK > limit) {
 #pragma unroll
@@ -453,14 +500,16 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_f32_kernel(const __grid_cons
                         if (kv0 + c >= limit)
                             s[c] = -INFINITY;
                 }
+                // Row max: independent 3-input max chains of 16 scores.
                 float mc[NK / 16];
 #pragma unroll
                 for (int q = 0; q < NK / 16; ++q) {
-                    float v = s[16 * q];
+                    const float *sq = s + 16 * q;
+                    float v = fmax3(sq[0], sq[1], sq[2]);
 #pragma unroll
-                    for (int e = 1; e < 16; ++e)
-                        v = fmaxf(v, s[16 * q + e]);
-                    mc[q] = v;
+                    for (int e = 3; e < 15; e += 2)
+                        v = fmax3(v, sq[e], sq[e + 1]);
+                    mc[q] = fmaxf(v, sq[15]);
                 }
 #pragma unroll
                 for (int w = NK / 32; w > 0; w >>= 1)
@@ -475,29 +524,35 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_f32_kernel(const __grid_cons
                     l *= alpha;
                     m = mnew;
                 }
-                float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+                // P = 2^(s scale - m): packed fp32 FMA, MUFU ex2, packed sums; P
+                // overwrites S in place.
+                const float neg_m = -m;
+                float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
 #pragma unroll
                 for (int c = 0; c < NK; c += 4) {
-                    s[c] = ex2_approx(fmaf(s[c], sl2, -m));
-                    s[c + 1] = ex2_approx(fmaf(s[c + 1], sl2, -m));
-                    s[c + 2] = ex2_approx(fmaf(s[c + 2], sl2, -m));
-                    s[c + 3] = ex2_approx(fmaf(s[c + 3], sl2, -m));
-                    a0 += s[c];
-                    a1 += s[c + 1];
-                    a2 += s[c + 2];
-                    a3 += s[c + 3];
+                    float x0, x1, x2, x3;
+                    ffma2(x0, x1, s[c], s[c + 1], sl2, sl2, neg_m, neg_m);
+                    ffma2(x2, x3, s[c + 2], s[c + 3], sl2, sl2, neg_m, neg_m);
+                    x0 = ex2_approx(x0);
+                    x1 = ex2_approx(x1);
+                    x2 = ex2_approx(x2);
+                    x3 = ex2_approx(x3);
+                    fadd2(a0, a1, a0, a1, x0, x1);
+                    fadd2(b0, b1, b0, b1, x2, x3);
+                    s[c] = x0;
+                    s[c + 1] = x1;
+                    s[c + 2] = x2;
+                    s[c + 3] = x3;
                 }
-                l += (a0 + a1) + (a2 + a3);
-                // P_b is free once O += P_b V of step g - 2 is complete.
-                if (g >= 2) {
-                    if (!(ok = wait_all(&pv_done[b], ((g - 2) >> 1) & 1, err, kErrWaitO)))
-                        break;
-                }
+                l += (a0 + a1) + (b0 + b1);
+                // P_b is free once the previous PV that read it is complete.
+                if (g >= S::PBUF && !(ok = wait_pv(g - S::PBUF)))
+                    break;
                 // O rescale: after O += P V of step g - 1, before that of step g.
                 // tcgen05.ld/st are warp-collective, so the warp rescales together
                 // (alpha == 1 for rows whose max did not grow).
                 if (j > 0 && __any_sync(0xffffffffu, grow)) {
-                    if (!(ok = wait_all(&pv_done[b ^ 1], ((g - 1) >> 1) & 1, err, kErrWaitO)))
+                    if (!(ok = wait_pv(g - 1)))
                         break;
                     tc_fence_after();
 #pragma unroll
@@ -512,18 +567,17 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_f32_kernel(const __grid_cons
                     }
                 }
                 tc_fence_after();
+                // P hi = P as computed (the tensor cores truncate it to tf32), P lo =
+                // the truncated part rounded to the nearest tf32 value.
 #pragma unroll
-                for (int c = 0; c < NK / 16; ++c) {
-                    uint32_t hi[16], lo[16];
+                for (int c = 0; c < NK / 32; ++c) {
+                    tmem_st32(tmem + lane_base + S::kP + 2 * NK * b + 32 * c,
+                              *reinterpret_cast<uint32_t(*)[32]>(&sraw[32 * c]));
+                    uint32_t lo[32];
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) {
-                        float h, lw;
-                        split_tf32(s[16 * c + e], h, lw);
-                        hi[e] = __float_as_uint(h);
-                        lo[e] = __float_as_uint(lw);
-                    }
-                    tmem_st16(tmem + lane_base + S::kP + 2 * NK * b + 16 * c, hi);
-                    tmem_st16(tmem + lane_base + S::kP + 2 * NK * b + NK + 16 * c, lo);
+                    for (int e = 0; e < 32; ++e)
+                        lo[e] = __float_as_uint(tf32_lo_of_trunc(s[32 * c + e]));
+                    tmem_st32(tmem + lane_base + S::kP + 2 * NK * b + NK + 32 * c, lo);
                 }
                 tmem_wait_st();
                 tc_fence_before();
@@ -535,7 +589,7 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_f32_kernel(const __grid_cons
             uint32_t oraw[HDP];
             float *o = reinterpret_cast<float *>(oraw);
             if (it.T > 0) {
-                if (!(ok = wait_all(&pv_done[(g - 1) & 1], ((g - 1) >> 1) & 1, err, kErrWaitO)))
+                if (!(ok = wait_pv(g - 1)))
                     break;
                 tc_fence_after();
 #pragma unroll
@@ -607,8 +661,7 @@ template <int HDP, int NK> int launch(const FmhaArgs &a, FmhaF32Params &p, cudaS
     if (attr != cudaSuccess)
         return static_cast<int>(attr);
     int rc = 0;
-    if ((rc = make_map_f32(&p.tq, a.q_ptr, a.q, 128)) || (rc = make_map_f32(&p.tk, a.k_ptr, a.k, NK)) ||
-        (rc = make_map_f32(&p.tv, a.v_ptr, a.v, NK, true)))
+    if ((rc = make_map_f32(&p.tk, a.k_ptr, a.k, NK)) || (rc = make_map_f32(&p.tv, a.v_ptr, a.v, NK, true)))
         return rc;
     static int sms = 0;
     if (!sms) {
@@ -647,6 +700,13 @@ int fmha_f32_launch(const FmhaArgs &a, cudaStream_t stream) {
     if (hdp < 0)
         return -2;
     FmhaF32Params p{};
+    p.q = static_cast<const float *>(a.q_ptr);
+    p.q_sb = a.q.s_batch;
+    p.q_sh = a.q.s_head;
+    p.q_st = a.q.s_token;
+    p.q_d = a.q.d;
+    p.q_vec = (reinterpret_cast<uintptr_t>(a.q_ptr) % 16 == 0) && (a.q.s_token % 4 == 0) && (a.q.s_head % 4 == 0) &&
+              (a.q.batch == 1 || a.q.s_batch % 4 == 0) && (a.q.d % 4 == 0);
     p.out = a.out;
     p.o_sb = a.o_sb;
     p.o_sh = a.o_sh;

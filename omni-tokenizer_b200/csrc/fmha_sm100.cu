@@ -151,29 +151,6 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi, bool bf16) {
     return *reinterpret_cast<uint32_t *>(&v);
 }
 
-// Packed fp32 arithmetic (two lanes per instruction).
-__device__ __forceinline__ void ffma2(float &d0, float &d1, float a0, float a1, float b0, float b1,
-                                      float c0, float c1) {
-    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
-        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
-        "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-        : "=f"(d0), "=f"(d1)
-        : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
-}
-__device__ __forceinline__ void fadd2(float &d0, float &d1, float a0, float a1, float b0,
-                                      float b1) {
-    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
-        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-        "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-        : "=f"(d0), "=f"(d1)
-        : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
-}
-__device__ __forceinline__ float fmax3(float a, float b, float c) {
-    float d;
-    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-    return d;
-}
-
 // 2^x0, 2^x1 with one packed half-precision MUFU ex2; returns the pair as
 // bf16x2 (bf16) or f16x2, low half = x0.
 __device__ __forceinline__ uint32_t ex2_pair(float x0, float x1, bool bf16) {
