@@ -389,17 +389,27 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_f32_kernel(const __grid_cons
         constexpr uint32_t idesc_pv = make_idesc_tf32(128, HDP, true);
         const uint32_t leader = elect_one() ? 1u : 0u;
         auto commit = [&](uint64_t *bar) { tc_commit_if(leader, bar); };
+        // Descriptors of stage 0; a stage is STAGE_BYTES further on, and the
+        // start-address field (bits 0-13, address >> 4) takes the offset by
+        // plain addition (every address stays below 256 KB).  All per-MMA
+        // offsets below are compile-time constants, so the issue path is one
+        // 64-bit add and one tcgen05.mma per MMA.
+        const uint64_t kh0 = make_smem_desc(smem_u32(k_hi(0)), 16, 1024, kLayoutSW128);
+        const uint64_t kl0 = make_smem_desc(smem_u32(k_lo(0)), 16, 1024, kLayoutSW128);
+        const uint64_t vh0 = make_smem_desc(smem_u32(v_hi(0)), S::KV_CHUNK, 512, kLayoutSW128A32);
+        const uint64_t vl0 = make_smem_desc(smem_u32(v_lo(0)), S::KV_CHUNK, 512, kLayoutSW128A32);
+        auto stage_off = [](int st) { return static_cast<uint64_t>((st * S::STAGE_BYTES) >> 4); };
         // S = Q K_st^T: Q hi / lo from TMEM (one column per element), K
         // K-major in smem; per 8-wide K step hi*lo, lo*hi, then hi*hi.
         auto qk = [&](int st) {
+            const uint64_t bh = kh0 + stage_off(st), bl = kl0 + stage_off(st);
 #pragma unroll
             for (int kk = 0; kk < HDP / 8; ++kk) {
-                const int c = kk >> 2, k4 = kk & 3; // 128-byte chunk, 32-byte step inside it
-                const uint64_t bh = make_smem_desc(smem_u32(k_hi(st)) + c * S::KV_CHUNK, 16, 1024, kLayoutSW128) + 2 * k4;
-                const uint64_t bl = make_smem_desc(smem_u32(k_lo(st)) + c * S::KV_CHUNK, 16, 1024, kLayoutSW128) + 2 * k4;
-                umma_ts_tf32_if(leader, S::kS, S::kQ + 8 * kk, bl, idesc_qk, kk > 0 ? 1u : 0u);
-                umma_ts_tf32_if(leader, S::kS, S::kQ + HDP + 8 * kk, bh, idesc_qk, 1u);
-                umma_ts_tf32_if(leader, S::kS, S::kQ + 8 * kk, bh, idesc_qk, 1u);
+                // 128-byte chunk kk / 4, 32-byte step kk % 4 inside it.
+                const uint64_t off = static_cast<uint64_t>(((kk >> 2) * S::KV_CHUNK) >> 4) + 2 * (kk & 3);
+                umma_ts_tf32_if(leader, S::kS, S::kQ + 8 * kk, bl + off, idesc_qk, kk > 0 ? 1u : 0u);
+                umma_ts_tf32_if(leader, S::kS, S::kQ + HDP + 8 * kk, bh + off, idesc_qk, 1u);
+                umma_ts_tf32_if(leader, S::kS, S::kQ + 8 * kk, bh + off, idesc_qk, 1u);
             }
         };
         // O (+)= P_b V_st: P hi / lo from TMEM, V MN-major (rows = keys) in the
@@ -408,8 +418,7 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_f32_kernel(const __grid_cons
         // (SBO); per 8-key step the descriptor moves 8 rows = 1 KB.
         auto pv = [&](int b, int st, bool accumulate) {
             const uint32_t ph = S::kP + 2 * NK * b, pl = ph + NK;
-            const uint64_t vh = make_smem_desc(smem_u32(v_hi(st)), S::KV_CHUNK, 512, kLayoutSW128A32);
-            const uint64_t vl = make_smem_desc(smem_u32(v_lo(st)), S::KV_CHUNK, 512, kLayoutSW128A32);
+            const uint64_t vh = vh0 + stage_off(st), vl = vl0 + stage_off(st);
 #pragma unroll
             for (int kk = 0; kk < NK / 8; ++kk) {
                 const uint64_t off = static_cast<uint64_t>((kk * 8 * 128) >> 4);
