@@ -120,6 +120,29 @@ OMNI_B200_API int omni_b200_vq_argmin_noalloc(const void *x, const void *codeboo
                                               size_t dim, size_t codes, int profile,
                                               int ids_u16, void *stream);
 
+/* ---- Diagnostics (failure detection without a GPU fault) ----------------
+ * Every pipeline wait in this library's kernels is bounded: a wait that has
+ * not completed after 2 s records a bit in the current device's kernel error
+ * word and lets the kernel end, so a broken pipeline shows up as
+ * OMNI_INTERNAL_ERROR from omni_b200_sync_check instead of a hang.  The word
+ * is per device, not per call or context: a check on any stream of the device
+ * reads and clears it.  No counterpart in the reference (its kernels are
+ * library templates without device-side waits).
+ *
+ * omni_b200_wait_selftest runs that bounded wait on a barrier that nothing
+ * completes, with a limit of limit_us microseconds (1 .. 2000000): the kernel
+ * gives up, records bit 0x200 and returns; the next omni_b200_sync_check on
+ * `stream` reports OMNI_INTERNAL_ERROR, and the device stays usable.
+ *
+ * omni_b200_debug_fail_allocations makes the next `count` device allocations
+ * of this library (host-buffer contexts, encoder contexts and model loads)
+ * fail as out of memory without reaching the allocator (0 turns it off).  The
+ * encoder contexts trim their memory pool and retry a failed allocation once,
+ * as the reference's Pool does (src/cuda.cu:515-527), so one injected failure
+ * is absorbed and two surface as OMNI_OUT_OF_MEMORY. */
+OMNI_B200_API int omni_b200_wait_selftest(unsigned limit_us, void *stream);
+OMNI_B200_API void omni_b200_debug_fail_allocations(int count);
+
 /* ---- Host-buffer entry points -------------------------------------------
  * A context owns one CUDA device, one stream and grow-only device buffers
  * (the role of omni_context in omni-tokenizer src/runtime.cpp:200-211).  The

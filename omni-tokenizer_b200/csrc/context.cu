@@ -13,6 +13,7 @@
 
 namespace omni_b200 {
 int ctx_fail(int code, const char *msg);
+bool injected_allocation_failure();
 } // namespace omni_b200
 
 // Batch chunks of the pipelined host-buffer attention call.
@@ -48,6 +49,8 @@ int reserve(omni_b200_context *c, int i, size_t bytes) {
         c->buf[i] = nullptr;
         c->cap[i] = 0;
     }
+    if (omni_b200::injected_allocation_failure())
+        return cuda_status(cudaErrorMemoryAllocation, "device buffer");
     if (int rc = cuda_status(cudaMalloc(&c->buf[i], bytes), "device buffer"))
         return rc;
     c->cap[i] = bytes;

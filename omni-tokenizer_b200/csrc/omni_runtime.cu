@@ -20,6 +20,7 @@
 #include "graph_kernels.h"
 #include "omni_abi.h"
 #include "omni_b200.h"
+#include "vq.h"
 
 #include <algorithm>
 #include <atomic>
@@ -43,6 +44,7 @@
 #include <vector>
 
 namespace omni_b200 {
+bool injected_allocation_failure();
 namespace rt {
 
 struct Fail : std::runtime_error {
@@ -99,7 +101,8 @@ Tensor weight_tensor(size_t rows, size_t cols, bool bf16) {
     t.cols = cols;
     t.bf16 = bf16;
     void *p = nullptr;
-    cuda_ok(cudaMalloc(&p, t.bytes() ? t.bytes() : 1), "weight allocation");
+    cuda_ok(injected_allocation_failure() ? cudaErrorMemoryAllocation : cudaMalloc(&p, t.bytes() ? t.bytes() : 1),
+            "weight allocation");
     t.mem = std::shared_ptr<void>(p, [](void *q) { cudaFree(q); });
     return t;
 }
@@ -372,6 +375,10 @@ struct Context {
     cudaMemPool_t pool = nullptr;
     std::shared_ptr<Memory> memory = std::make_shared<Memory>();
     std::atomic<bool> cancelled{false};
+    // The same flag in mapped pinned host memory, read by the VQ kernels when
+    // they start (cancellation between codebook windows of the VQ pass).
+    int *cancel_host = nullptr;
+    int *cancel_dev = nullptr;
     std::atomic_flag running = ATOMIC_FLAG_INIT;
     Tensor features;
     omni_trace_callback trace = nullptr;
@@ -417,6 +424,8 @@ struct Context {
             cudaStreamDestroy(stream);
         if (pool)
             cudaMemPoolDestroy(pool);
+        if (cancel_host)
+            cudaFreeHost(cancel_host);
     }
     void check() const {
         if (cancelled.load())
@@ -430,7 +439,18 @@ struct Context {
         t.bf16 = bf16;
         const size_t bytes = t.bytes() ? t.bytes() : 1;
         void *p = nullptr;
-        cuda_ok(cudaMallocFromPoolAsync(&p, bytes, pool, stream), "activation allocation");
+        // Out of memory: release the pool's idle memory and retry once (the
+        // reference's Pool trims its cache and retries, src/cuda.cu:515-527).
+        cudaError_t e = injected_allocation_failure() ? cudaErrorMemoryAllocation
+                                                      : cudaMallocFromPoolAsync(&p, bytes, pool, stream);
+        if (e == cudaErrorMemoryAllocation) {
+            cudaGetLastError(); // take the failed call out of the runtime's last-error state
+            cuda_ok(cudaStreamSynchronize(stream), "activation allocation");
+            cuda_ok(cudaMemPoolTrimTo(pool, 0), "activation allocation");
+            e = injected_allocation_failure() ? cudaErrorMemoryAllocation
+                                              : cudaMallocFromPoolAsync(&p, bytes, pool, stream);
+        }
+        cuda_ok(e, "activation allocation");
         memory->add(bytes);
         auto mem = memory;
         cudaStream_t s = stream;
@@ -614,20 +634,25 @@ Tensor attention(Context &c, const Tensor &q, const Tensor *k, const Tensor *v, 
     return y;
 }
 
+// Ops::quantize (src/cuda.cu:934-973).  Cancellation: the reference polls its
+// flag before every codebook tile (:946-948); here the VQ kernels read the
+// context's mapped flag when they start, the wide and fp32 passes run the
+// codebook in windows of kVqCancelWindow codes, and the call reports
+// OMNI_CANCELLED once the stream is drained.
 std::vector<uint16_t> quantize(Context &c, const Tensor &x, const Tensor &cb, const Tensor &cbnorm) {
-    c.check();
     const int profile = x.bf16 ? OMNI_B200_BF16 : OMNI_B200_F32;
     const size_t ws_bytes = omni_b200_vq_workspace(x.rows, x.cols, cb.rows, profile);
     Tensor ws_holder, ids_holder;
     void *ws = c.scratch(ws_bytes, ws_holder);
     void *ids = c.scratch(x.rows * 2, ids_holder);
-    op_ok(omni_b200_vq_argmin(x.data(), cb.data(), cbnorm.data(), ids, x.rows, x.cols, cb.rows, profile,
-                              1, ws, ws_bytes, c.stream),
+    op_ok(vq_argmin(x.data(), cb.data(), cbnorm.data(), ids, x.rows, x.cols, cb.rows, profile, 1, ws, ws_bytes,
+                    c.cancel_dev, c.stream),
           "quantize");
     std::vector<uint16_t> out(x.rows);
     cuda_ok(cudaMemcpyAsync(out.data(), ids, x.rows * 2, cudaMemcpyDeviceToHost, c.stream), "ids");
     cuda_ok(cudaStreamSynchronize(c.stream), "quantize");
     op_ok(omni_b200_sync_check(c.stream), "quantize");
+    c.check();
     return out;
 }
 
@@ -840,7 +865,7 @@ std::vector<uint16_t> encode_audio_batch(Context &c, const float *mel, size_t co
             add_in_place(c, x, mlp);
             trace(c, x, "layer." + std::to_string(cfg.layers - 1));
         }
-        c.check();
+        // The next cancellation point is the VQ pass (src/runtime.cpp:47-66).
         const size_t pooled_rows = (L + cfg.pool_size - 1) / cfg.pool_size;
         Tensor pooled = c.make(items * pooled_rows, W, x.bf16);
         cuda_ok(static_cast<cudaError_t>(graph::pool(x.data(), pooled.data(), x.bf16, x.rows, W, cfg.pool_size,
@@ -1039,6 +1064,13 @@ int omni_context_create(omni_model *m, omni_context **out) {
         omni_b200::rt::blas_ok(cublasCreate(&c->impl.blas), "cuBLAS handle");
         omni_b200::rt::blas_ok(cublasSetStream(c->impl.blas, c->impl.stream), "cuBLAS stream");
         omni_b200::rt::cuda_ok(cudaStreamCreateWithFlags(&c->impl.copy, cudaStreamNonBlocking), "stream create");
+        omni_b200::rt::cuda_ok(cudaHostAlloc(reinterpret_cast<void **>(&c->impl.cancel_host), sizeof(int),
+                                             cudaHostAllocMapped),
+                               "cancel flag");
+        *c->impl.cancel_host = 0;
+        omni_b200::rt::cuda_ok(cudaHostGetDevicePointer(reinterpret_cast<void **>(&c->impl.cancel_dev),
+                                                        c->impl.cancel_host, 0),
+                               "cancel flag");
         cudaMemPoolProps props{};
         props.allocType = cudaMemAllocationTypePinned;
         props.location.type = cudaMemLocationTypeDevice;
@@ -1081,12 +1113,18 @@ int omni_context_create(omni_model *m, omni_context **out) {
 }
 void omni_context_free(omni_context *c) { delete c; }
 void omni_context_cancel(omni_context *c) {
-    if (c)
+    if (c) {
         c->impl.cancelled.store(true);
+        if (c->impl.cancel_host)
+            *reinterpret_cast<volatile int *>(c->impl.cancel_host) = 1;
+    }
 }
 void omni_context_reset_cancel(omni_context *c) {
-    if (c)
+    if (c) {
+        if (c->impl.cancel_host)
+            *reinterpret_cast<volatile int *>(c->impl.cancel_host) = 0;
         c->impl.cancelled.store(false);
+    }
 }
 int omni_context_set_trace(omni_context *c, omni_trace_callback callback, void *user) {
     return guarded([&] {

@@ -4,8 +4,10 @@
 #include "fmha.h"
 #include "norms.h"
 #include "pack.h"
+#include "sm100.cuh"
 #include "vq.h"
 
+#include <atomic>
 #include <cmath>
 #include <cstdio>
 #include <cuda_runtime.h>
@@ -49,6 +51,30 @@ int *kernel_error_word() {
         g_err_ptr[dev] = static_cast<int *>(p);
     }
     return g_err_ptr[dev];
+}
+
+// Test hook: the next g_fail_allocations device allocations made by this
+// library report cudaErrorMemoryAllocation without reaching the allocator.
+std::atomic<int> g_fail_allocations{0};
+bool injected_allocation_failure() {
+    int n = g_fail_allocations.load();
+    while (n > 0 && !g_fail_allocations.compare_exchange_weak(n, n - 1)) {
+    }
+    return n > 0;
+}
+
+// The pipeline kernels' bounded wait on an mbarrier that nothing completes: it
+// gives up after limit_ns, records kErrWaitSelfTest in the error word and
+// returns (no trap, no fault, no hang).
+__global__ void wait_selftest_kernel(int *err, unsigned long long limit_ns) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbarrier_init();
+    }
+    __syncthreads();
+    mbar_wait(&bar, 0, err, kErrWaitSelfTest, limit_ns);
+    __syncthreads();
 }
 
 int ctx_fail(int code, const char *msg) { return fail(code, msg); }
@@ -264,6 +290,20 @@ using namespace omni_b200;
 extern "C" {
 
 const char *omni_b200_last_error(void) { return g_error.c_str(); }
+
+int omni_b200_wait_selftest(unsigned limit_us, void *stream) {
+    g_error.clear();
+    if (limit_us == 0 || limit_us > 2000000u)
+        return fail(1, "wait_selftest: limit_us must be in [1, 2000000]");
+    int *err = kernel_error_word();
+    if (!err)
+        return fail(7, "wait_selftest: no CUDA device");
+    wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(err, 1000ull * limit_us);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_fail(e, "wait_selftest");
+}
+
+void omni_b200_debug_fail_allocations(int count) { g_fail_allocations.store(count < 0 ? 0 : count); }
 const char *omni_b200_version(void) { return "0.1.0+b200"; }
 
 int omni_b200_sync_check(void *stream) {
@@ -377,6 +417,17 @@ size_t omni_b200_vq_workspace(size_t rows, size_t dim, size_t codes, int profile
 int omni_b200_vq_argmin(const void *x, const void *codebook, const void *cbnorm, void *ids,
                         size_t rows, size_t dim, size_t codes, int profile, int ids_u16,
                         void *workspace, size_t workspace_bytes, void *stream) {
+    return vq_argmin(x, codebook, cbnorm, ids, rows, dim, codes, profile, ids_u16, workspace, workspace_bytes,
+                     nullptr, static_cast<cudaStream_t>(stream));
+}
+
+} // extern "C"
+
+namespace omni_b200 {
+
+int vq_argmin(const void *x, const void *codebook, const void *cbnorm, void *ids, size_t rows, size_t dim,
+              size_t codes, int profile, int ids_u16, void *workspace, size_t workspace_bytes,
+              const volatile int *cancel, cudaStream_t stream) {
     g_error.clear();
     if (!x || !codebook || !cbnorm || !ids)
         return fail(1, "vq_argmin: null pointer");
@@ -409,13 +460,13 @@ int omni_b200_vq_argmin(const void *x, const void *codebook, const void *cbnorm,
     a.keys = workspace;
     a.ids = ids;
     a.ids_u16 = ids_u16 ? 1 : 0;
+    a.cancel = cancel;
     a.err = kernel_error_word();
     if (!a.err)
         return fail(7, "vq_argmin: no CUDA device");
     if (fp32 || dim > 128)
-        return launch_status(vq_stream_launch(a, fp32 ? 1 : 0, static_cast<cudaStream_t>(stream)),
-                             "vq_argmin");
-    return launch_status(vq_bf16_launch(a, static_cast<cudaStream_t>(stream)), "vq_argmin");
+        return launch_status(vq_stream_launch(a, fp32 ? 1 : 0, stream), "vq_argmin");
+    return launch_status(vq_bf16_launch(a, stream), "vq_argmin");
 }
 
-} // extern "C"
+} // namespace omni_b200

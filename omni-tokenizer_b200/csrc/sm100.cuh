@@ -31,6 +31,7 @@ enum : int {
     kErrWaitEmpty = 1 << 6,
     kErrWaitAcc = 1 << 7,
     kErrWaitDrain = 1 << 8,
+    kErrWaitSelfTest = 1 << 9, // omni_b200_wait_selftest: a wait that nothing completes
 };
 
 // A wait that has not completed after this long is treated as a deadlock: the
@@ -81,7 +82,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // Waits for the phase with the given parity to complete.  Gives up after
 // kWaitLimitNs (recording `code` in *err) or as soon as another thread of the
 // launch has recorded an error; returns false in both cases.
-static __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int code) {
+static __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int code,
+                                                 uint64_t limit_ns = kWaitLimitNs) {
     const uint32_t a = smem_u32(bar);
     if (mbar_try_wait(a, parity))
         return true;
@@ -92,7 +94,7 @@ static __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
         if ((i & 127u) == 0) {
             if (*reinterpret_cast<volatile int *>(err) != 0)
                 return false;
-            if (globaltimer_ns() - start > kWaitLimitNs) {
+            if (globaltimer_ns() - start > limit_ns) {
                 atomicOr(err, code);
                 return false;
             }

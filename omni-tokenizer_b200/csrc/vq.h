@@ -23,7 +23,15 @@ struct VqArgs {
     void *ids = nullptr;  // output ids
     int ids_u16 = 0;      // 1: uint16 ids, 0: int32 ids
     int *err = nullptr;
+    // Optional cancellation flag the device can read (mapped pinned host memory
+    // or device memory): the streamed kernels run the codebook in windows of
+    // kVqCancelWindow codes, one launch each, and a launch whose CTAs see a
+    // nonzero flag when they start skips its window (the ids are then
+    // incomplete; the caller reports the cancellation).
+    const volatile int *cancel = nullptr;
 };
+
+constexpr int kVqCancelWindow = 4096; // codes per launch when a cancel flag is given
 
 int vq_padded_dim(int dim);
 int vq_bf16_launch(const VqArgs &args, cudaStream_t stream);
@@ -41,10 +49,18 @@ struct VqsParams {
     unsigned *cand_count;         // fp32 profile: [rows]
     unsigned *cand;               // fp32 profile: [rows][kVqCandCap]
     int rows, dim, codes, chunks;
-    int slices, slice_codes;
+    int code_lo, code_hi;         // codebook window of this launch, [code_lo, code_hi)
+    int slices, slice_codes;      // the window split into slices of slice_codes codes
     float win_a, win_b;           // fp32 profile: candidate window a |x||c| + b (|x|^2 + |c|^2)
+    const volatile int *cancel;   // nonzero when the CTA starts: skip the window
     int *err;
 };
+
+// omni_b200_vq_argmin with an optional cancellation flag (see VqArgs::cancel);
+// the encoder graphs pass their context's flag.
+int vq_argmin(const void *x, const void *codebook, const void *cbnorm, void *ids, size_t rows, size_t dim,
+              size_t codes, int profile, int ids_u16, void *workspace, size_t workspace_bytes,
+              const volatile int *cancel, cudaStream_t stream);
 
 // Scratch bytes for vq_stream_launch (VqArgs::keys points at it).
 size_t vq_stream_workspace(size_t rows, int profile_fp32);

@@ -109,6 +109,11 @@ __global__ void __launch_bounds__(kVqsThreads, 1) vq_stream_kernel(const __grid_
     int *err = p.err;
     const int row_tiles = (p.rows + 127) / 128;
     const int units = row_tiles * p.slices;
+    // Cancellation (the reference polls its flag before every codebook tile,
+    // src/cuda.cu:946-948): a CTA that starts after the flag was set skips its
+    // part of this launch's codebook window, before it allocates anything.
+    if (p.cancel && __syncthreads_or(threadIdx.x == 0 ? *p.cancel != 0 : 0))
+        return;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S::STAGES; ++s) {
@@ -141,8 +146,8 @@ __global__ void __launch_bounds__(kVqsThreads, 1) vq_stream_kernel(const __grid_
         bool ok = true;
         for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
             const int rt = u / p.slices, sl = u % p.slices;
-            const int c_begin = sl * p.slice_codes;
-            const int c_end = min(p.codes, c_begin + p.slice_codes);
+            const int c_begin = p.code_lo + sl * p.slice_codes;
+            const int c_end = min(p.code_hi, c_begin + p.slice_codes);
             for (int c = c_begin; ok && c < c_end; c += 256) {
                 for (int kc = 0; kc < p.chunks; ++kc, ++n) {
                     const int st = n % S::STAGES;
@@ -172,8 +177,8 @@ __global__ void __launch_bounds__(kVqsThreads, 1) vq_stream_kernel(const __grid_
         bool ok = true;
         for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
             const int sl = u % p.slices;
-            const int c_begin = sl * p.slice_codes;
-            const int c_end = min(p.codes, c_begin + p.slice_codes);
+            const int c_begin = p.code_lo + sl * p.slice_codes;
+            const int c_end = min(p.code_hi, c_begin + p.slice_codes);
             for (int c = c_begin; ok && c < c_end; c += 256, ++n_acc) {
                 const int buf = n_acc & 1;
                 if (!(ok = __all_sync(0xffffffffu, mbar_wait(&acc_empty[buf], ((n_acc >> 1) & 1) ^ 1,
@@ -215,8 +220,8 @@ __global__ void __launch_bounds__(kVqsThreads, 1) vq_stream_kernel(const __grid_
         bool ok = true;
         for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
             const int rt = u / p.slices, sl = u % p.slices;
-            const int c_begin = sl * p.slice_codes;
-            const int c_end = min(p.codes, c_begin + p.slice_codes);
+            const int c_begin = p.code_lo + sl * p.slice_codes;
+            const int c_end = min(p.code_hi, c_begin + p.slice_codes);
             const int row = rt * 128 + r;
             const bool live = row < p.rows;
             const float xn = live ? p.xn[row] : 0.f;
@@ -496,11 +501,12 @@ int sm_count() {
     return sms;
 }
 
-// Units = 128-row tiles x codebook slices, about 8 units per SM.
+// Units = 128-row tiles x slices of the launch's codebook window, about 8
+// units per SM.
 int plan_units(VqsParams &p) {
     const int sms = sm_count();
     const int row_tiles = (p.rows + 127) / 128;
-    const int code_tiles = (p.codes + 255) / 256;
+    const int code_tiles = (p.code_hi - p.code_lo + 255) / 256;
     int slices = (8 * sms + row_tiles - 1) / row_tiles;
     slices = slices < 1 ? 1 : slices > code_tiles ? code_tiles : slices;
     const int tiles_per_slice = (code_tiles + slices - 1) / slices;
@@ -548,21 +554,34 @@ int vq_stream_launch(const VqArgs &a, int profile_fp32, cudaStream_t stream) {
     p.win_a = static_cast<float>((std::ldexp(1.0, -7) + (a.dim + 1.0) * std::ldexp(1.0, -21)) * 1.0001);
     p.win_b = static_cast<float>((a.dim + 4.0) * std::ldexp(1.0, -22) * 1.0001);
     p.err = a.err;
-    const int grid = plan_units(p);
+    p.cancel = a.cancel;
     const int threads = 256;
     const int kb = (a.rows + threads - 1) / threads;
     vqs_init<<<kb < 4096 ? kb : 4096, threads, 0, stream>>>(p.keys, p.cand_count, a.rows);
     // |x|^2 per row in the profile's arithmetic (bf16 profile: the bf16 value).
     if ((rc = squares_launch(a.x, p.xn, a.rows, a.dim, tf32 ? 0 : 1, 0, stream)))
         return rc;
+    // One launch per codebook window: the whole codebook, or windows of
+    // kVqCancelWindow codes when the caller can cancel.  The keys merge by
+    // atomicMin across launches, so windows compose exactly.
+    const int window = a.cancel ? kVqCancelWindow : a.codes;
+    auto pass = [&](auto launch) {
+        for (int lo = 0; lo < a.codes; lo += window) {
+            p.code_lo = lo;
+            p.code_hi = lo + window < a.codes ? lo + window : a.codes;
+            if (int e = launch(plan_units(p)))
+                return e;
+        }
+        return 0;
+    };
     if (!tf32) {
-        if ((rc = vqs_launch_typed<false, kVqsBf16>(p, grid, stream)))
+        if ((rc = pass([&](int grid) { return vqs_launch_typed<false, kVqsBf16>(p, grid, stream); })))
             return rc;
         vqs_finish<<<kb < 4096 ? kb : 4096, threads, 0, stream>>>(p.keys, a.ids, a.rows, a.ids_u16);
         return static_cast<int>(cudaGetLastError());
     }
-    if ((rc = vqs_launch_typed<true, kVqsApprox>(p, grid, stream)) ||
-        (rc = vqs_launch_typed<true, kVqsCand>(p, grid, stream)))
+    if ((rc = pass([&](int grid) { return vqs_launch_typed<true, kVqsApprox>(p, grid, stream); })) ||
+        (rc = pass([&](int grid) { return vqs_launch_typed<true, kVqsCand>(p, grid, stream); })))
         return rc;
     const int rb = (a.rows * 32 + threads - 1) / threads;
     vq_refine_fp64<<<rb < 8192 ? rb : 8192, threads, 0, stream>>>(

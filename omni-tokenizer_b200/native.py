@@ -32,6 +32,8 @@ SIGNATURES = {
     "omni_b200_last_error": (C.c_char_p, []),
     "omni_b200_version": (C.c_char_p, []),
     "omni_b200_sync_check": (C.c_int, [_P]),
+    "omni_b200_wait_selftest": (C.c_int, [C.c_uint, _P]),
+    "omni_b200_debug_fail_allocations": (None, [C.c_int]),
     "omni_b200_attention_bhld": (
         C.c_int,
         [_P, _P, _P, _P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _P, C.c_int, C.c_int, C.c_float, _P],
