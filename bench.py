@@ -12,9 +12,9 @@ pass over that batch; FLOPs per step = 4*B*H*L^2*D (D = 72, not the padded 80).
 The same line carries, under "sub", one record per other configuration the
 metric names, each with its own roofline, cpu_baseline and e2e: c1 (Whisper
 shape, bf16), c1_f32 (the same shape in fp32, the reference's audio profile),
-c3 (variable-length audio batch), c5 (images/s of the whole image encoder),
-c4_bf16 and c4 (audio-s/s of the whole audio encoder, bf16 mode and the fp32
-profile).  --config NAME runs one configuration alone.
+c3 (variable-length audio batch), vq_audio and vq_image (the VQ argmin ops),
+c5 (images/s of the whole image encoder), c4_bf16 and c4 (audio-s/s of the
+whole audio encoder, bf16 mode and the fp32 profile).  --config NAME runs one configuration alone.
 
 * value  -- device-resident inputs, K steps timed with CUDA events between a
             barrier + synchronize on both sides, max over ranks, whole job.
@@ -827,7 +827,7 @@ def run_ours(args, name, cfg, dist, steps, warmup):
 # Sub-records of the default run: the other BASELINE configurations the metric
 # names (attention at the other shapes; images/s and audio-s/s of the whole
 # encoders), each with its own roofline, cpu_baseline and e2e.
-SUITE = ["c1", "c1_f32", "c3", "c5", "c4_bf16", "c4"]
+SUITE = ["c1", "c1_f32", "c3", "vq_audio", "vq_image", "c5", "c4_bf16", "c4"]
 ENCODER_MAX_STEPS = 5
 
 

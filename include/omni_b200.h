@@ -101,6 +101,23 @@ OMNI_B200_API int omni_b200_vq_argmin(const void *x, const void *codebook, const
                                       int profile, int ids_u16, void *workspace,
                                       size_t workspace_bytes, void *stream);
 
+/* omni_b200_vq_argmin with the reference's cancellation contract
+ * (Ops::quantize(x, cb, cbnorm, std::atomic<bool>& cancel), omni-tokenizer
+ * src/internal.h:87-88; its CUDA backend polls the flag before every 1024-code
+ * tile, src/cuda.cu:946-948).  cancel points at an int the device can read --
+ * mapped pinned host memory (cudaHostAlloc with cudaHostAllocMapped; pass the
+ * device pointer from cudaHostGetDevicePointer) or device memory -- that the
+ * caller sets to nonzero to cancel; NULL behaves as omni_b200_vq_argmin.  With
+ * a flag, the wide (dim > 128) and fp32 passes run the codebook in windows of
+ * 4096 codes, one launch each, and a launch that starts after the flag is set
+ * skips its window.  The call is asynchronous like the others: after
+ * synchronising, a caller that set the flag discards ids and reports
+ * OMNI_CANCELLED, as Ops::quantize throws Error(OMNI_CANCELLED). */
+OMNI_B200_API int omni_b200_vq_argmin_cancellable(const void *x, const void *codebook, const void *cbnorm,
+                                                  void *ids, size_t rows, size_t dim, size_t codes,
+                                                  int profile, int ids_u16, void *workspace,
+                                                  size_t workspace_bytes, const int *cancel, void *stream);
+
 /* omni_b200_vq_argmin without caller-provided scratch.  No counterpart in the
  * reference (its Ops::quantize allocates from the context's Pool).  For callers
  * that cannot allocate device memory: processes whose HBM is owned by another

@@ -421,6 +421,13 @@ int omni_b200_vq_argmin(const void *x, const void *codebook, const void *cbnorm,
                      nullptr, static_cast<cudaStream_t>(stream));
 }
 
+int omni_b200_vq_argmin_cancellable(const void *x, const void *codebook, const void *cbnorm, void *ids,
+                                    size_t rows, size_t dim, size_t codes, int profile, int ids_u16,
+                                    void *workspace, size_t workspace_bytes, const int *cancel, void *stream) {
+    return vq_argmin(x, codebook, cbnorm, ids, rows, dim, codes, profile, ids_u16, workspace, workspace_bytes,
+                     cancel, static_cast<cudaStream_t>(stream));
+}
+
 } // extern "C"
 
 namespace omni_b200 {

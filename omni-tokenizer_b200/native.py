@@ -49,6 +49,10 @@ SIGNATURES = {
         C.c_int,
         [_P, _P, _P, _P, C.c_size_t, C.c_size_t, C.c_size_t, C.c_int, C.c_int, _P, C.c_size_t, _P],
     ),
+    "omni_b200_vq_argmin_cancellable": (
+        C.c_int,
+        [_P, _P, _P, _P, C.c_size_t, C.c_size_t, C.c_size_t, C.c_int, C.c_int, _P, C.c_size_t, _P, _P],
+    ),
     "omni_b200_vq_workspace": (C.c_size_t, [C.c_size_t, C.c_size_t, C.c_size_t, C.c_int]),
     "omni_b200_context_create": (C.c_int, [C.c_int, C.POINTER(_P)]),
     "omni_b200_context_free": (None, [_P]),

@@ -223,3 +223,41 @@ def test_vq_fp32_candidate_overflow_scores_every_code(ob):
     want = O.quantize(x, cb, bf16=False).astype(np.int64)
     assert got[1] == tied[0]
     assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("profile,dim", [(0, 1280), (1, 2048)])
+def test_vq_cancellable_windows_and_cancel(ob, profile, dim):
+    """omni_b200_vq_argmin_cancellable (Ops::quantize's cancel contract): with a
+    clear flag the 4096-code windows compose to exactly the ids of
+    omni_b200_vq_argmin; with the flag set before the call every window is
+    skipped, so the ids are incomplete and the caller reports the cancellation."""
+    lib = ob.library()
+    rows, codes = 200, 9000  # three windows of at most 4096 codes
+    rng = np.random.default_rng(dim + profile)
+    x = rng.standard_normal((rows, dim)).astype(np.float32)
+    cb = rng.standard_normal((codes, dim)).astype(np.float32)
+    cb[4100] = x[3]  # an exact match in the second window
+    if profile == 1:
+        x, cb = O.round_bf16(x), O.round_bf16(cb)
+    want, _ = _gpu_quantize(ob, x, cb, ids_u16=False, profile=profile)
+    dt = torch.bfloat16 if profile == 1 else torch.float32
+    tx, tc = torch.from_numpy(x).to(dt).cuda(), torch.from_numpy(cb).to(dt).cuda()
+    norms = torch.empty(codes, dtype=dt, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    lib.check(lib.lib.omni_b200_squares(tc.data_ptr(), norms.data_ptr(), codes, dim, profile, profile, stream))
+    ws_bytes = lib.lib.omni_b200_vq_workspace(rows, dim, codes, profile)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+    flag = torch.zeros(1, dtype=torch.int32, device="cuda")
+    for value in (0, 1):
+        flag.fill_(value)
+        ids = torch.full((rows,), -7, dtype=torch.int32, device="cuda")
+        lib.check(lib.lib.omni_b200_vq_argmin_cancellable(tx.data_ptr(), tc.data_ptr(), norms.data_ptr(),
+                                                          ids.data_ptr(), rows, dim, codes, profile, 0,
+                                                          ws.data_ptr(), ws_bytes, flag.data_ptr(), stream))
+        lib.sync_check(stream)
+        got = ids.cpu().numpy().astype(np.int64)
+        if value == 0:
+            assert np.array_equal(got, want)
+            assert got[3] == 4100
+        else:
+            assert (got != want).mean() > 0.9  # the windows were skipped
