@@ -25,9 +25,10 @@ struct VqArgs {
     int *err = nullptr;
     // Optional cancellation flag the device can read (mapped pinned host memory
     // or device memory): the streamed kernels run the codebook in windows of
-    // kVqCancelWindow codes, one launch each, and a launch whose CTAs see a
-    // nonzero flag when they start skips its window (the ids are then
-    // incomplete; the caller reports the cancellation).
+    // kVqCancelWindow codes (a multiple of it when the rows are too few to fill
+    // the GPU), one launch each, and a launch whose CTAs see a nonzero flag
+    // when they start skips its window (the ids are then incomplete; the caller
+    // reports the cancellation).
     const volatile int *cancel = nullptr;
 };
 

@@ -561,10 +561,18 @@ int vq_stream_launch(const VqArgs &a, int profile_fp32, cudaStream_t stream) {
     // |x|^2 per row in the profile's arithmetic (bf16 profile: the bf16 value).
     if ((rc = squares_launch(a.x, p.xn, a.rows, a.dim, tf32 ? 0 : 1, 0, stream)))
         return rc;
-    // One launch per codebook window: the whole codebook, or windows of
-    // kVqCancelWindow codes when the caller can cancel.  The keys merge by
-    // atomicMin across launches, so windows compose exactly.
-    const int window = a.cancel ? kVqCancelWindow : a.codes;
+    // One launch per codebook window: the whole codebook, or (when the caller
+    // can cancel) windows of kVqCancelWindow codes, widened in multiples of it
+    // until one window gives two units per SM (few rows: a 4096-code window of
+    // three row tiles would occupy 48 SMs).  The keys merge by atomicMin across
+    // launches, so windows compose exactly.
+    int window = a.codes;
+    if (a.cancel) {
+        const long long row_tiles = (a.rows + 127) / 128;
+        const long long tiles = (2LL * sm_count() + row_tiles - 1) / row_tiles;
+        const long long w = (tiles * 256 + kVqCancelWindow - 1) / kVqCancelWindow * kVqCancelWindow;
+        window = w < a.codes ? static_cast<int>(w) : a.codes;
+    }
     auto pass = [&](auto launch) {
         for (int lo = 0; lo < a.codes; lo += window) {
             p.code_lo = lo;

@@ -232,7 +232,7 @@ def test_vq_cancellable_windows_and_cancel(ob, profile, dim):
     omni_b200_vq_argmin; with the flag set before the call every window is
     skipped, so the ids are incomplete and the caller reports the cancellation."""
     lib = ob.library()
-    rows, codes = 200, 9000  # three windows of at most 4096 codes
+    rows, codes = 4000, 9000  # 32 row tiles: three windows of at most 4096 codes
     rng = np.random.default_rng(dim + profile)
     x = rng.standard_normal((rows, dim)).astype(np.float32)
     cb = rng.standard_normal((codes, dim)).astype(np.float32)
