@@ -146,6 +146,10 @@ struct Model {
         auto it = w16.find(name);
         return it == w16.end() ? nullptr : &it->second;
     }
+    // Tensors that are views into another tensor of `w` (the audio layers'
+    // q/k/v projections inside their stacked qkv weight); not converted for
+    // the bf16 audio mode.
+    std::set<std::string> views;
 };
 
 // ------------------------------------------------------------------ loader
@@ -346,6 +350,38 @@ std::shared_ptr<Model> load_model(const char *path, int backend, int device) {
         cuda_ok(cudaMemcpy(t.data(), raw.data(), t.bytes(), cudaMemcpyHostToDevice), "weight upload");
         m->weight_bytes += t.bytes();
         m->w.emplace(e.name, std::move(t));
+    }
+    if (c.kind == OMNI_AUDIO) {
+        // The three attention projections of an audio layer read the same
+        // input: stack them as one [3 width, width] weight (and a [3 width]
+        // bias with zeros where a projection has none) so that the graph runs
+        // one GEMM whose output is the fused Q|K|V layout.  The separate
+        // tensors stay available as views into the stacked ones.
+        const size_t W = c.width;
+        for (uint32_t i = 0; i < c.layers; ++i) {
+            const std::string p = "layers." + std::to_string(i) + ".self_attn.";
+            Tensor qkv = weight_tensor(3 * W, W, false), bias = weight_tensor(3 * W, 1, false);
+            cuda_ok(cudaMemset(bias.data(), 0, bias.bytes()), "qkv bias");
+            const char *proj[3] = {"q_proj", "k_proj", "v_proj"};
+            for (int j = 0; j < 3; ++j) {
+                const std::string wn = p + proj[j] + ".weight", bn = p + proj[j] + ".bias";
+                Tensor &wt = m->w.at(wn);
+                char *dst = static_cast<char *>(qkv.data()) + j * W * W * 4;
+                cuda_ok(cudaMemcpy(dst, wt.data(), W * W * 4, cudaMemcpyDeviceToDevice), "qkv weight");
+                wt.mem = std::shared_ptr<void>(qkv.mem, dst);
+                m->views.insert(wn);
+                auto b = m->w.find(bn);
+                if (b != m->w.end()) {
+                    char *bdst = static_cast<char *>(bias.data()) + j * W * 4;
+                    cuda_ok(cudaMemcpy(bdst, b->second.data(), W * 4, cudaMemcpyDeviceToDevice), "qkv bias");
+                    b->second.mem = std::shared_ptr<void>(bias.mem, bdst);
+                    m->views.insert(bn);
+                }
+            }
+            m->weight_bytes += bias.bytes();
+            m->w.emplace(p + "qkv.weight", std::move(qkv));
+            m->w.emplace(p + "qkv.bias", std::move(bias));
+        }
     }
     const char *cb_name = c.kind == OMNI_AUDIO ? "codebook.weight" : "quantize.embedding.weight";
     Tensor &cb = m->w.at(cb_name);
@@ -593,19 +629,22 @@ Tensor attention(Context &c, const Tensor &q, const Tensor *k, const Tensor *v, 
         // S = scale Q K^T for all heads (one strided batched fp32 GEMM), masked
         // softmax in place, O = P V.  Head dims up to 128 take the fused
         // split-precision kernel through attention_rows below.
-        require(!fused, "fp32 fused attention is not used by the graphs", OMNI_INTERNAL_ERROR);
+        // Q, K, V rows are `ld` floats apart (d, or 3 d in the fused layout).
+        const size_t ld = fused ? 3 * d : d;
         const long long nn = static_cast<long long>(n) * n;
         Tensor scores = c.make(batch * heads * n, n, false);
         float *S = static_cast<float *>(scores.data());
         const float scale = 1.f / std::sqrt(static_cast<float>(hd)), one = 1.f, zero = 0.f;
-        const float *Q = static_cast<const float *>(q.data()), *K = static_cast<const float *>(k->data()),
-                    *V = static_cast<const float *>(v->data());
+        const float *Q = static_cast<const float *>(q.data());
+        const float *K = fused ? Q + d : static_cast<const float *>(k->data());
+        const float *V = fused ? Q + 2 * d : static_cast<const float *>(v->data());
         float *O = static_cast<float *>(y.data());
-        const int ni = static_cast<int>(n), di = static_cast<int>(d), hi = static_cast<int>(hd);
+        const int ni = static_cast<int>(n), di = static_cast<int>(d), li = static_cast<int>(ld),
+                  hi = static_cast<int>(hd);
         for (size_t b = 0; b < batch; ++b)
             blas_ok(cublasGemmStridedBatchedEx(c.blas, CUBLAS_OP_T, CUBLAS_OP_N, ni, ni, hi, &scale,
-                                               K + b * n * d, CUDA_R_32F, di, static_cast<long long>(hd),
-                                               Q + b * n * d, CUDA_R_32F, di, static_cast<long long>(hd), &zero,
+                                               K + b * n * ld, CUDA_R_32F, li, static_cast<long long>(hd),
+                                               Q + b * n * ld, CUDA_R_32F, li, static_cast<long long>(hd), &zero,
                                                S + b * heads * nn, CUDA_R_32F, ni, nn, static_cast<int>(heads),
                                                c.fp32_compute(), CUBLAS_GEMM_DEFAULT),
                     "attention scores");
@@ -613,8 +652,8 @@ Tensor attention(Context &c, const Tensor &q, const Tensor *k, const Tensor *v, 
                                                              static_cast<size_t>(valid[0]), block, c.stream)),
                 "attention softmax");
         for (size_t b = 0; b < batch; ++b)
-            blas_ok(cublasGemmStridedBatchedEx(c.blas, CUBLAS_OP_N, CUBLAS_OP_N, hi, ni, ni, &one, V + b * n * d,
-                                               CUDA_R_32F, di, static_cast<long long>(hd), S + b * heads * nn,
+            blas_ok(cublasGemmStridedBatchedEx(c.blas, CUBLAS_OP_N, CUBLAS_OP_N, hi, ni, ni, &one, V + b * n * ld,
+                                               CUDA_R_32F, li, static_cast<long long>(hd), S + b * heads * nn,
                                                CUDA_R_32F, ni, nn, &zero, O + b * n * d, CUDA_R_32F, di,
                                                static_cast<long long>(hd), static_cast<int>(heads),
                                                c.fp32_compute(), CUBLAS_GEMM_DEFAULT),
@@ -778,7 +817,7 @@ std::vector<uint16_t> encode_audio_batch(Context &c, const float *mel, size_t co
     if (bf)
         std::call_once(model.w16_once, [&] {
             for (const auto &kv : model.w) {
-                if (kv.first == "codebook.weight" || kv.second.bf16)
+                if (kv.first == "codebook.weight" || kv.second.bf16 || model.views.count(kv.first))
                     continue;
                 Tensor t = weight_tensor(kv.second.rows, kv.second.cols, true);
                 cuda_ok(static_cast<cudaError_t>(graph::convert(static_cast<const float *>(kv.second.data()),
@@ -849,11 +888,12 @@ std::vector<uint16_t> encode_audio_batch(Context &c, const float *mel, size_t co
             auto proj = [&](const Tensor &in, const std::string &name) {
                 return linear(c, in, m.get(name + ".weight", bf), m.opt(name + ".bias", bf));
             };
-            Tensor q = proj(z, p + "self_attn.q_proj"), k = proj(z, p + "self_attn.k_proj"),
-                   v = proj(z, p + "self_attn.v_proj");
-            z = attention(c, q, &k, &v, cfg.heads, cfg.block_size, false, items, chunk_keys,
+            // Q|K|V from one GEMM (the stacked projections), attended in the
+            // fused layout with the unfused scale hd^-1/2.
+            Tensor qkv = proj(z, p + "self_attn.qkv");
+            z = attention(c, qkv, nullptr, nullptr, cfg.heads, cfg.block_size, true, items, chunk_keys,
                           static_cast<const int *>(keys_dev.data()));
-            q = {}, k = {}, v = {};
+            qkv = {};
             z = proj(z, p + "self_attn.out_proj");
             z = add_norm(c, x, &z, m.get(p + "final_layer_norm.weight", bf), m.get(p + "final_layer_norm.bias", bf),
                          1e-5f);
