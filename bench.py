@@ -2,7 +2,7 @@
 """Benchmark of the omni-tokenizer hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config NAME] [--items N]
-                    [--impl ours|reference]
+                    [--rows N] [--impl ours|reference]
 
 Default run: the headline is BASELINE config 2, the SigLIP-shaped encoder
 self-attention op -- batch 32, 16 heads, L=729, head_dim 72, fp16 Q/K/V drawn
@@ -12,7 +12,8 @@ pass over that batch; FLOPs per step = 4*B*H*L^2*D (D = 72, not the padded 80).
 The same line carries, under "sub", one record per other configuration the
 metric names, each with its own roofline, cpu_baseline and e2e: c1 (Whisper
 shape, bf16), c1_f32 (the same shape in fp32, the reference's audio profile),
-c3 (variable-length audio batch), vq_audio and vq_image (the VQ argmin ops),
+c3 (variable-length audio batch), vq_audio and vq_image (the VQ argmin ops,
+bf16 profile), vq_audio_f32 (the fp32-profile VQ at config 4's graph shape),
 c5 (images/s of the whole image encoder), c4_bf16 and c4 (audio-s/s of the
 whole audio encoder, bf16 mode and the fp32 profile).  --config NAME runs one configuration alone.
 
@@ -78,6 +79,11 @@ CONFIGS = {
                      workload="VQ argmin op, audio-shaped (x 24000x64 vs codebook 16384x64, bf16)"),
     "vq_image": dict(kind="vq", N=373248, K=16384, dim=32, seed=1011,
                      workload="VQ argmin op, image-shaped (x 373248x32 vs codebook 16384x32, bf16)"),
+    # The fp32-profile VQ of BASELINE config 4's graph: 16 segments pool to
+    # 16 x 188 rows of width 1024, searched against the 16384 x 1024 codebook.
+    "vq_audio_f32": dict(kind="vq", N=3008, K=16384, dim=1024, profile="f32", seed=1012,
+                         workload="VQ argmin op, fp32 profile at BASELINE config 4's graph shape (x 3008x1024 "
+                                  "vs codebook 16384x1024: tf32 search, fp64 re-scoring of the candidates)"),
     # Whole encoders through the reference's omni_* C ABI (libomni_b200.so), on
     # randomly initialised OMNIVQ01 models of production shape.
     "c4": dict(kind="encoder", modality="audio", items=16, mel=80, frames=3000, width=1024, layers=24, heads=16,
@@ -243,8 +249,9 @@ def vq_inputs(cfg, rank):
     import torch
 
     g = torch.Generator().manual_seed(cfg["seed"] + 7919 * rank)
-    x = torch.randn(cfg["N"], cfg["dim"], generator=g).to(torch.bfloat16).pin_memory()
-    cb = torch.randn(cfg["K"], cfg["dim"], generator=g).to(torch.bfloat16).pin_memory()
+    dt = torch.float32 if cfg.get("profile") == "f32" else torch.bfloat16
+    x = torch.randn(cfg["N"], cfg["dim"], generator=g).to(dt).pin_memory()
+    cb = torch.randn(cfg["K"], cfg["dim"], generator=g).to(dt).pin_memory()
     return x, cb
 
 
@@ -282,19 +289,22 @@ def cpu_reference_sample(cfg, budget_s, items=None):
         return flops, t_total, threads, kind, sample
     # VQ: a slice of rows against the full codebook.
     dim, K = cfg["dim"], cfg["K"]
-    cb = O.round_bf16(rng.standard_normal((K, dim)).astype(np.float32))
-    norms = O.squares(cb, bf16=True)
-    rows, t_total, work = 64, 0.0, 0.0
+    bf = cfg.get("profile") != "f32"
+    rnd = O.round_bf16 if bf else (lambda a: a)
+    cb = rnd(rng.standard_normal((K, dim)).astype(np.float32))
+    norms = O.squares(cb, bf16=bf)
+    rows, t_total, work = 64 if bf else 8, 0.0, 0.0
     done = chunks = 0
     while done < cfg["N"] and (chunks < items if items is not None else (t_total < budget_s or chunks == 0)):
-        x = O.round_bf16(rng.standard_normal((rows, dim)).astype(np.float32))
+        x = rnd(rng.standard_normal((rows, dim)).astype(np.float32))
         t0 = time.perf_counter()
-        O.quantize(x, cb, norms, bf16=True, impl=impl)
+        O.quantize(x, cb, norms, bf16=bf, impl=impl)
         t_total += time.perf_counter() - t0
         work += 2.0 * rows * K * dim
         done += rows
         chunks += 1
-    return work, t_total, threads, kind, f"{done} rows x {K} codes, bf16 profile, src/cpu.cpp Ops::quantize"
+    return work, t_total, threads, kind, (f"{done} rows x {K} codes, {'bf16' if bf else 'fp32'} profile, "
+                                          "src/cpu.cpp Ops::quantize")
 
 
 # ------------------------------------------------------------------ whole encoders
@@ -503,7 +513,10 @@ def run_encoder(args, name, cfg, dist, steps, warmup):
         t_clock1 = time.perf_counter()
         sampler.stop()
         # e2e: host buffers through the same call (host-to-device copies inside),
-        # after one untimed call that sizes the host path's staging buffers.
+        # after two untimed calls: the first sizes the host path's staging
+        # buffers, the second (the same key again) captures the call's CUDA graph,
+        # which the timed calls replay (copies from the pinned inputs included).
+        encode_batch(session, cfg, host)
         encode_batch(session, cfg, host)
         e2e_steps = max(1, min(steps, 3))
         e2e_elapsed, codes_bytes = timed(lambda: encode_batch(session, cfg, host), e2e_steps)
@@ -612,7 +625,8 @@ def run_reference(args, cfg):
     probe_work, probe_t, threads, kind, _ = cpu_reference_sample(cfg, 0.0, items=1)
     per_unit = max(probe_t, 1e-4)
     budget = 120.0 / max(1, args.steps + args.warmup)
-    total_units = cfg["B"] * cfg["H"] if cfg["kind"] == "attn" else (cfg["N"] + 63) // 64
+    vq_rows = 64 if cfg.get("profile") != "f32" else 8
+    total_units = cfg["B"] * cfg["H"] if cfg["kind"] == "attn" else (cfg["N"] + vq_rows - 1) // vq_rows
     units = max(1, min(total_units, int(budget / per_unit)))
     for _ in range(args.warmup):
         cpu_reference_sample(cfg, 0.0, items=units)
@@ -685,27 +699,30 @@ def run_ours(args, name, cfg, dist, steps, warmup):
         hx, hcb = vq_inputs(cfg, rank)
         x, cb = hx.cuda(), hcb.cuda()
         N, K, dim = cfg["N"], cfg["K"], cfg["dim"]
-        norms = torch.empty(K, dtype=torch.bfloat16, device="cuda")
-        lib.check(lib.lib.omni_b200_squares(cb.data_ptr(), norms.data_ptr(), K, dim, 1, 1, sp))
-        ws_bytes = lib.lib.omni_b200_vq_workspace(N, dim, K, 1)
+        prof = 0 if cfg.get("profile") == "f32" else 1  # OMNI_B200_F32 / OMNI_B200_BF16
+        norms = torch.empty(K, dtype=x.dtype, device="cuda")
+        lib.check(lib.lib.omni_b200_squares(cb.data_ptr(), norms.data_ptr(), K, dim, prof, prof, sp))
+        ws_bytes = lib.lib.omni_b200_vq_workspace(N, dim, K, prof)
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
         ids = torch.empty(N, dtype=torch.int32, device="cuda")
         flops_step = 2.0 * N * K * dim
         job_flops_step = flops_step * world
-        launches_per_step = 3
+        # bf16 dim <= 128: init, fused kernel, finish; wide or fp32: init, row
+        # norms, one launch per pass, refinement (fp32).
+        launches_per_step = 3 if (prof == 1 and dim <= 128) else (4 if prof == 1 else 6)
 
         def step():
             lib.check(lib.lib.omni_b200_vq_argmin(x.data_ptr(), cb.data_ptr(), norms.data_ptr(), ids.data_ptr(),
-                                                  N, dim, K, 1, 0, ws.data_ptr(), ws_bytes, sp))
+                                                  N, dim, K, prof, 0, ws.data_ptr(), ws_bytes, sp))
 
         hids = torch.empty(N, dtype=torch.int32).pin_memory()
-        in_bytes = hx.numel() * 2 + hcb.numel() * 2
+        in_bytes = hx.numel() * hx.element_size() + hcb.numel() * hcb.element_size()
         out_bytes = N * 4
 
         def e2e_step(ctx):
-            ctx.vq_argmin(hx, hcb, hids, N, dim, K, profile=1, ids_u16=False)
+            ctx.vq_argmin(hx, hcb, hids, N, dim, K, profile=prof, ids_u16=False)
 
-        dtype_name = "bf16"
+        dtype_name = "f32" if prof == 0 else "bf16"
         working_set = in_bytes + out_bytes
 
     # ---- warm-up
@@ -772,6 +789,10 @@ def run_ours(args, name, cfg, dist, steps, warmup):
         # Three tf32 MMAs per fp32 product, tf32 at half the bf16 rate.
         peak /= 6.0
         peak_source = f"{pk_kind} bf16_tflops (burst) / 6: three tf32 products per fp32 product at half the bf16 rate"
+    elif cfg.get("profile") == "f32":
+        # The fp32 VQ's distance GEMM runs as kind::tf32 (half the bf16 rate).
+        peak /= 2.0
+        peak_source = f"{pk_kind} bf16_tflops (burst) / 2: the tf32 tensor rate of the distance search"
     achieved = flops_step / launch_s / 1e12
     traffic, traffic_source = None, None
     tf = ROOT / "profiles" / "traffic.json"
@@ -827,12 +848,14 @@ def run_ours(args, name, cfg, dist, steps, warmup):
 # Sub-records of the default run: the other BASELINE configurations the metric
 # names (attention at the other shapes; images/s and audio-s/s of the whole
 # encoders), each with its own roofline, cpu_baseline and e2e.
-SUITE = ["c1", "c1_f32", "c3", "vq_audio", "vq_image", "c5", "c4_bf16", "c4"]
+SUITE = ["c1", "c1_f32", "c3", "vq_audio", "vq_image", "vq_audio_f32", "c5", "c4_bf16", "c4"]
 ENCODER_MAX_STEPS = 5
 
 
 def run_config(args, name, dist, steps, warmup):
     cfg = dict(CONFIGS[name])
+    if cfg["kind"] == "vq" and args.rows is not None and name == args.config:
+        cfg["N"] = args.rows
     if cfg["kind"] == "encoder":
         if args.items is not None and name == args.config:
             cfg["items"] = args.items
@@ -853,7 +876,11 @@ def main():
     ap.add_argument("--no-sub", action="store_true", help="default run: the headline line only")
     ap.add_argument("--items", type=int, default=None,
                     help="whole-encoder configs: items per step (default: the config's; smaller for profiling)")
+    ap.add_argument("--rows", type=int, default=None,
+                    help="VQ configs: rows of x (default: the config's; smaller for profiling)")
     args = ap.parse_args()
+    if args.rows is not None and (args.config is None or CONFIGS[args.config]["kind"] != "vq" or args.rows <= 0):
+        ap.error("--rows applies to an explicit VQ --config and must be positive")
     if args.items is not None and (args.config is None or CONFIGS[args.config]["kind"] != "encoder"
                                    or args.items <= 0):
         ap.error("--items applies to an explicit whole-encoder --config and must be positive")

@@ -106,6 +106,17 @@ OMNI_ABI_API int omni_b200_encode_images(omni_context *context, const float *pix
                                          uint32_t height, uint32_t width, uint16_t *codes,
                                          size_t capacity, size_t *count);
 
+/* Repeated batched calls run as a CUDA graph: when a call has the same entry
+ * point, shapes, valid lengths and input address as the previous call, and
+ * its input is device memory or page-locked host memory, and no trace
+ * callback is set, the context captures the call's device work into a graph
+ * (outputs in buffers the graph keeps) and replays that graph for later calls
+ * with the same key -- the whole graph is recomputed from the input each time.
+ * Cancellation is checked before a replay starts and by the VQ kernels inside
+ * it.  OMNI_B200_GRAPHS=0 (read when the context is created) keeps every call
+ * eager.  This counter is the number of graph launches of the context. */
+OMNI_ABI_API uint64_t omni_b200_context_graph_launches(const omni_context *context);
+
 #ifdef __cplusplus
 }
 #endif

@@ -57,6 +57,7 @@ _EXT_SIGS = {
                                                C.POINTER(C.c_size_t)]),
     "omni_b200_encode_images": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32,
                                           C.POINTER(C.c_uint16), C.c_size_t, C.POINTER(C.c_size_t)]),
+    "omni_b200_context_graph_launches": (C.c_uint64, [C.c_void_p]),
 }
 EXTENSION_SYMBOLS = tuple(_EXT_SIGS)
 
@@ -192,6 +193,11 @@ class Session:
     @property
     def peak_workspace(self):
         return int(self.lib.lib.omni_context_peak_workspace(self.handle))
+
+    @property
+    def graph_launches(self):
+        """CUDA-graph launches of repeated batched calls (captures and replays)."""
+        return int(self.lib.lib.omni_b200_context_graph_launches(self.handle))
 
     def close(self):
         if self.handle:

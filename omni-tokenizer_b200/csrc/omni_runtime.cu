@@ -436,6 +436,27 @@ struct Context {
     void *lt_ws = nullptr;
     size_t lt_ws_bytes = 0;
     std::map<std::array<long long, 5>, std::pair<bool, cublasLtMatmulAlgo_t>> lt_algos;
+    // cuBLAS workspace, set explicitly so that captured GEMMs allocate nothing.
+    void *blas_ws = nullptr;
+    // CUDA-graph replay of repeated batched calls: the second call with the
+    // same key (entry point, shapes, valid lengths, input address) is captured
+    // into a graph whose outputs live in persistent buffers, and later calls
+    // with that key replay it.
+    struct Replay {
+        std::vector<uint64_t> key;
+        cudaGraphExec_t exec = nullptr;
+        Tensor flag, features, ids, keys;
+    };
+    Replay replay;
+    std::vector<uint64_t> last_key;
+    uint64_t graph_launches = 0;
+    bool capturing = false; // inside a stream capture: no synchronising retries
+    bool graphs = true;     // OMNI_B200_GRAPHS=0 turns replay off
+    void drop_replay() {
+        if (replay.exec)
+            cudaGraphExecDestroy(replay.exec);
+        replay = Replay{};
+    }
 
     ~Context() {
         features = {};
@@ -443,6 +464,7 @@ struct Context {
             cudaSetDevice(model ? model->device : 0);
             cudaStreamSynchronize(stream);
         }
+        drop_replay();
         if (copy)
             cudaStreamSynchronize(copy);
         for (cudaEvent_t e : {ready[0], ready[1], done[0], done[1], start})
@@ -454,6 +476,8 @@ struct Context {
             cublasLtDestroy(lt);
         if (lt_ws)
             cudaFree(lt_ws);
+        if (blas_ws)
+            cudaFree(blas_ws);
         if (copy)
             cudaStreamDestroy(copy);
         if (stream)
@@ -479,7 +503,7 @@ struct Context {
         // reference's Pool trims its cache and retries, src/cuda.cu:515-527).
         cudaError_t e = injected_allocation_failure() ? cudaErrorMemoryAllocation
                                                       : cudaMallocFromPoolAsync(&p, bytes, pool, stream);
-        if (e == cudaErrorMemoryAllocation) {
+        if (e == cudaErrorMemoryAllocation && !capturing) {
             cudaGetLastError(); // take the failed call out of the runtime's last-error state
             cuda_ok(cudaStreamSynchronize(stream), "activation allocation");
             cuda_ok(cudaMemPoolTrimTo(pool, 0), "activation allocation");
@@ -678,17 +702,23 @@ Tensor attention(Context &c, const Tensor &q, const Tensor *k, const Tensor *v, 
 // context's mapped flag when they start, the wide and fp32 passes run the
 // codebook in windows of kVqCancelWindow codes, and the call reports
 // OMNI_CANCELLED once the stream is drained.
-std::vector<uint16_t> quantize(Context &c, const Tensor &x, const Tensor &cb, const Tensor &cbnorm) {
+// Launch part: uint16 ids of x's rows into `ids` (device), asynchronously.
+void quantize_launch(Context &c, const Tensor &x, const Tensor &cb, const Tensor &cbnorm, void *ids) {
     const int profile = x.bf16 ? OMNI_B200_BF16 : OMNI_B200_F32;
     const size_t ws_bytes = omni_b200_vq_workspace(x.rows, x.cols, cb.rows, profile);
-    Tensor ws_holder, ids_holder;
+    Tensor ws_holder;
     void *ws = c.scratch(ws_bytes, ws_holder);
-    void *ids = c.scratch(x.rows * 2, ids_holder);
     op_ok(vq_argmin(x.data(), cb.data(), cbnorm.data(), ids, x.rows, x.cols, cb.rows, profile, 1, ws, ws_bytes,
                     c.cancel_dev, c.stream),
           "quantize");
-    std::vector<uint16_t> out(x.rows);
-    cuda_ok(cudaMemcpyAsync(out.data(), ids, x.rows * 2, cudaMemcpyDeviceToHost, c.stream), "ids");
+}
+
+// Reads `rows` uint16 ids back once the stream has drained; kernel errors and
+// a cancellation that arrived meanwhile are reported here.
+std::vector<uint16_t> read_ids(Context &c, const Tensor &ids, size_t rows) {
+    std::vector<uint16_t> out(rows);
+    if (rows)
+        cuda_ok(cudaMemcpyAsync(out.data(), ids.data(), rows * 2, cudaMemcpyDeviceToHost, c.stream), "ids");
     cuda_ok(cudaStreamSynchronize(c.stream), "quantize");
     op_ok(omni_b200_sync_check(c.stream), "quantize");
     c.check();
@@ -796,6 +826,106 @@ void finite_or_fail(Context &c, const Tensor &flag) {
     cuda_ok(cudaStreamSynchronize(c.stream), "input check");
     require(v == 0, "Input contains a non-finite value");
 }
+
+// Inputs a captured graph can read again at replay: device memory, or host
+// memory that is page-locked (copies from pageable memory cannot be captured).
+bool replayable_input(const void *p) {
+    cudaPointerAttributes at{};
+    if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged || at.type == cudaMemoryTypeHost;
+}
+
+// Buffers that outlive one batched call's device work: the non-finite flag,
+// the features (what omni_context_copy_features returns), the uint16 ids and
+// per-item key limits.
+struct Bufs {
+    Tensor flag, features, ids, keys;
+};
+
+// Captures work(b) on the context's stream into a graph, instantiates and
+// launches it, and keeps it as the context's replay.  Returns false (nothing
+// launched) when the work cannot be captured; a cancellation propagates.
+template <class Work> bool capture_and_launch(Context &c, const std::vector<uint64_t> &key, const Bufs &b, Work &work) {
+    if (cudaStreamBeginCapture(c.stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    c.capturing = true;
+    cudaGraph_t g = nullptr;
+    try {
+        work(b);
+    } catch (const Fail &f) {
+        c.capturing = false;
+        if (cudaStreamEndCapture(c.stream, &g) == cudaSuccess && g)
+            cudaGraphDestroy(g);
+        cudaGetLastError();
+        if (f.code == OMNI_CANCELLED)
+            throw;
+        c.graphs = false; // this context runs its calls eagerly from now on
+        return false;
+    }
+    c.capturing = false;
+    cudaError_t e = cudaStreamEndCapture(c.stream, &g);
+    cudaGraphExec_t exec = nullptr;
+    if (e == cudaSuccess)
+        e = cudaGraphInstantiate(&exec, g, 0);
+    if (g)
+        cudaGraphDestroy(g);
+    if (e == cudaSuccess)
+        e = cudaGraphLaunch(exec, c.stream);
+    if (e != cudaSuccess) {
+        if (exec)
+            cudaGraphExecDestroy(exec);
+        cudaGetLastError();
+        c.graphs = false;
+        return false;
+    }
+    ++c.graph_launches;
+    c.replay.key = key;
+    c.replay.exec = exec;
+    c.replay.flag = b.flag;
+    c.replay.features = b.features;
+    c.replay.ids = b.ids;
+    c.replay.keys = b.keys;
+    return true;
+}
+
+// One batched call: work(b) (all device work, writing b.flag, b.features and
+// b.ids) runs eagerly, or as a CUDA graph when the call repeats -- inputs in
+// device or page-locked host memory, no trace callback, the same key as the
+// previous call (captured then) or as the captured graph (replayed).  A replay
+// checks cancellation before its launch; inside it, the VQ kernels read the
+// context's mapped flag as in the eager graph.  Then the ids are read back.
+template <class Alloc, class Work>
+std::vector<uint16_t> run_batch(Context &c, const std::vector<uint64_t> &key, bool eligible, size_t id_rows,
+                                Alloc alloc, Work work) {
+    eligible = eligible && c.graphs && !c.trace;
+    Bufs b;
+    if (eligible && c.replay.exec && c.replay.key == key) {
+        c.check();
+        cuda_ok(cudaGraphLaunch(c.replay.exec, c.stream), "graph launch");
+        ++c.graph_launches;
+        b.flag = c.replay.flag;
+        b.features = c.replay.features;
+        b.ids = c.replay.ids;
+        b.keys = c.replay.keys;
+    } else {
+        if (eligible && key == c.last_key)
+            c.drop_replay(); // its buffers go back to the pool before the new ones are made
+        b = alloc();
+        const bool captured = eligible && key == c.last_key && capture_and_launch(c, key, b, work);
+        if (!captured)
+            work(b);
+    }
+    c.last_key = eligible ? key : std::vector<uint64_t>{};
+    auto ids = read_ids(c, b.ids, id_rows);
+    finite_or_fail(c, b.flag);
+    c.features = b.features;
+    return ids;
+}
 } // namespace
 
 // Audio graph (src/runtime.cpp:30-75) over `count` log-mel segments
@@ -831,108 +961,117 @@ std::vector<uint16_t> encode_audio_batch(Context &c, const float *mel, size_t co
     std::vector<size_t> offset(count + 1, 0);
     for (size_t i = 0; i < count; ++i)
         offset[i + 1] = offset[i] + (valid[i] + 7) / 8;
-    Tensor flag = c.make(1, 1, false);
-    cuda_ok(cudaMemsetAsync(flag.data(), 0, 4, c.stream), "input check");
-    Tensor features = c.make(offset[count], W, bf);
     std::vector<int> keys(count);
     for (size_t i = 0; i < count; ++i)
         keys[i] = static_cast<int>((valid[i] + 1) / 2);
     const size_t chunk = chunk_items(count, T);
-    for_chunks(c, mel, count, C * T, chunk, [&](size_t i0, size_t items, const float *src) {
-        cuda_ok(static_cast<cudaError_t>(graph::finite_check(src, items * C * T, static_cast<int *>(flag.data()),
-                                                             c.stream)),
-                "input check");
-        Tensor x = c.make(items * T, C, false);
-        cuda_ok(static_cast<cudaError_t>(graph::frames_major(src, static_cast<float *>(x.data()), items, C, T,
-                                                             c.stream)),
-                "frames");
-        if (bf) {
-            Tensor x16 = c.make(items * T, C, true);
-            cuda_ok(static_cast<cudaError_t>(graph::convert(static_cast<const float *>(x.data()), x16.data(), true,
-                                                            x.size(), c.stream)),
-                    "frames");
-            x = x16;
-        }
-        auto conv = [&](const Tensor &in, size_t rows, size_t stride, const char *name) {
-            const size_t out_rows = (rows + stride - 1) / stride;
-            Tensor g = c.make(items * out_rows, in.cols * 3, in.bf16);
-            cuda_ok(static_cast<cudaError_t>(graph::conv_gather(in.data(), g.data(), in.bf16, items, rows,
-                                                                in.cols, stride, c.stream)),
-                    "conv gather");
-            Tensor y = linear(c, g, m.get(std::string(name) + ".weight", bf),
-                              m.opt(std::string(name) + ".bias", bf));
-            gelu_in_place(c, y);
-            return y;
-        };
-        x = conv(x, T, 1, "conv1");
-        x = conv(x, T, 2, "conv2");
-        const Tensor &pos = m.get("embed_positions.weight", bf);
-        cuda_ok(static_cast<cudaError_t>(graph::add_periodic(x.data(), pos.data(), x.bf16, x.size(), L * W,
-                                                             c.stream)),
-                "positions");
-        trace(c, x, "embedding");
-        const std::vector<int> chunk_keys(keys.begin() + i0, keys.begin() + i0 + items);
-        Tensor keys_dev = c.make(items, 1, false);
-        cuda_ok(cudaMemcpyAsync(keys_dev.data(), chunk_keys.data(), items * 4, cudaMemcpyHostToDevice, c.stream),
+    // Persistent buffers: flag, fp32 features (the VQ input and what
+    // omni_context_copy_features returns), ids, per-segment key limits.
+    auto alloc = [&] {
+        Bufs b;
+        b.flag = c.make(1, 1, false);
+        b.features = c.make(offset[count], W, false);
+        b.ids = c.make((offset[count] + 1) / 2, 1, false);
+        b.keys = c.make(count, 1, false);
+        cuda_ok(cudaMemcpyAsync(b.keys.data(), keys.data(), count * 4, cudaMemcpyHostToDevice, c.stream),
                 "key counts");
-        // Each residual add runs fused with the layer norm that follows it; the
-        // MLP output `mlp` of layer i joins x at the start of layer i + 1.
-        Tensor mlp;
-        for (uint32_t i = 0; i < cfg.layers; ++i) {
-            c.check();
-            const std::string p = "layers." + std::to_string(i) + ".";
-            Tensor z = add_norm(c, x, i ? &mlp : nullptr, m.get(p + "self_attn_layer_norm.weight", bf),
-                                m.get(p + "self_attn_layer_norm.bias", bf), 1e-5f);
-            if (i)
-                trace(c, x, "layer." + std::to_string(i - 1));
-            auto proj = [&](const Tensor &in, const std::string &name) {
-                return linear(c, in, m.get(name + ".weight", bf), m.opt(name + ".bias", bf));
+        return b;
+    };
+    auto work = [&](const Bufs &b) {
+        cuda_ok(cudaMemsetAsync(b.flag.data(), 0, 4, c.stream), "input check");
+        Tensor flag = b.flag;
+        // bf16 mode: the pooled features stay bf16 until the fp32 copy for the VQ.
+        Tensor features = bf ? c.make(offset[count], W, true) : b.features;
+        for_chunks(c, mel, count, C * T, chunk, [&](size_t i0, size_t items, const float *src) {
+            cuda_ok(static_cast<cudaError_t>(graph::finite_check(src, items * C * T, static_cast<int *>(flag.data()),
+                                                                 c.stream)),
+                    "input check");
+            Tensor x = c.make(items * T, C, false);
+            cuda_ok(static_cast<cudaError_t>(graph::frames_major(src, static_cast<float *>(x.data()), items, C, T,
+                                                                 c.stream)),
+                    "frames");
+            if (bf) {
+                Tensor x16 = c.make(items * T, C, true);
+                cuda_ok(static_cast<cudaError_t>(graph::convert(static_cast<const float *>(x.data()), x16.data(), true,
+                                                                x.size(), c.stream)),
+                        "frames");
+                x = x16;
+            }
+            auto conv = [&](const Tensor &in, size_t rows, size_t stride, const char *name) {
+                const size_t out_rows = (rows + stride - 1) / stride;
+                Tensor g = c.make(items * out_rows, in.cols * 3, in.bf16);
+                cuda_ok(static_cast<cudaError_t>(graph::conv_gather(in.data(), g.data(), in.bf16, items, rows,
+                                                                    in.cols, stride, c.stream)),
+                        "conv gather");
+                Tensor y = linear(c, g, m.get(std::string(name) + ".weight", bf),
+                                  m.opt(std::string(name) + ".bias", bf));
+                gelu_in_place(c, y);
+                return y;
             };
-            // Q|K|V from one GEMM (the stacked projections), attended in the
-            // fused layout with the unfused scale hd^-1/2.
-            Tensor qkv = proj(z, p + "self_attn.qkv");
-            z = attention(c, qkv, nullptr, nullptr, cfg.heads, cfg.block_size, true, items, chunk_keys,
-                          static_cast<const int *>(keys_dev.data()));
-            qkv = {};
-            z = proj(z, p + "self_attn.out_proj");
-            z = add_norm(c, x, &z, m.get(p + "final_layer_norm.weight", bf), m.get(p + "final_layer_norm.bias", bf),
-                         1e-5f);
-            z = proj(z, p + "fc1");
-            gelu_in_place(c, z);
-            mlp = proj(z, p + "fc2");
-        }
-        if (cfg.layers) {
-            add_in_place(c, x, mlp);
-            trace(c, x, "layer." + std::to_string(cfg.layers - 1));
-        }
-        // The next cancellation point is the VQ pass (src/runtime.cpp:47-66).
-        const size_t pooled_rows = (L + cfg.pool_size - 1) / cfg.pool_size;
-        Tensor pooled = c.make(items * pooled_rows, W, x.bf16);
-        cuda_ok(static_cast<cudaError_t>(graph::pool(x.data(), pooled.data(), x.bf16, x.rows, W, cfg.pool_size,
-                                                     c.stream)),
-                "pool");
-        // pool over the stacked rows equals pool per segment: L is a multiple of
-        // the pool size (frames % 8 == 0), so no group straddles two segments.
-        const size_t es = bf ? 2 : 4;
-        for (size_t b = 0; b < items; ++b) {
-            const size_t rows = offset[i0 + b + 1] - offset[i0 + b];
-            cuda_ok(cudaMemcpyAsync(static_cast<char *>(features.data()) + offset[i0 + b] * W * es,
-                                    static_cast<const char *>(pooled.data()) + b * pooled_rows * W * es,
-                                    rows * W * es, cudaMemcpyDeviceToDevice, c.stream),
+            x = conv(x, T, 1, "conv1");
+            x = conv(x, T, 2, "conv2");
+            const Tensor &pos = m.get("embed_positions.weight", bf);
+            cuda_ok(static_cast<cudaError_t>(graph::add_periodic(x.data(), pos.data(), x.bf16, x.size(), L * W,
+                                                                 c.stream)),
+                    "positions");
+            trace(c, x, "embedding");
+            const std::vector<int> chunk_keys(keys.begin() + i0, keys.begin() + i0 + items);
+            const int *keys_dev = static_cast<const int *>(b.keys.data()) + i0;
+            // Each residual add runs fused with the layer norm that follows it; the
+            // MLP output `mlp` of layer i joins x at the start of layer i + 1.
+            Tensor mlp;
+            for (uint32_t i = 0; i < cfg.layers; ++i) {
+                c.check();
+                const std::string p = "layers." + std::to_string(i) + ".";
+                Tensor z = add_norm(c, x, i ? &mlp : nullptr, m.get(p + "self_attn_layer_norm.weight", bf),
+                                    m.get(p + "self_attn_layer_norm.bias", bf), 1e-5f);
+                if (i)
+                    trace(c, x, "layer." + std::to_string(i - 1));
+                auto proj = [&](const Tensor &in, const std::string &name) {
+                    return linear(c, in, m.get(name + ".weight", bf), m.opt(name + ".bias", bf));
+                };
+                // Q|K|V from one GEMM (the stacked projections), attended in the
+                // fused layout with the unfused scale hd^-1/2.
+                Tensor qkv = proj(z, p + "self_attn.qkv");
+                z = attention(c, qkv, nullptr, nullptr, cfg.heads, cfg.block_size, true, items, chunk_keys, keys_dev);
+                qkv = {};
+                z = proj(z, p + "self_attn.out_proj");
+                z = add_norm(c, x, &z, m.get(p + "final_layer_norm.weight", bf), m.get(p + "final_layer_norm.bias", bf),
+                             1e-5f);
+                z = proj(z, p + "fc1");
+                gelu_in_place(c, z);
+                mlp = proj(z, p + "fc2");
+            }
+            if (cfg.layers) {
+                add_in_place(c, x, mlp);
+                trace(c, x, "layer." + std::to_string(cfg.layers - 1));
+            }
+            // The next cancellation point is the VQ pass (src/runtime.cpp:47-66).
+            const size_t pooled_rows = (L + cfg.pool_size - 1) / cfg.pool_size;
+            Tensor pooled = c.make(items * pooled_rows, W, x.bf16);
+            cuda_ok(static_cast<cudaError_t>(graph::pool(x.data(), pooled.data(), x.bf16, x.rows, W, cfg.pool_size,
+                                                         c.stream)),
+                    "pool");
+            // pool over the stacked rows equals pool per segment: L is a multiple of
+            // the pool size (frames % 8 == 0), so no group straddles two segments.
+            const size_t es = bf ? 2 : 4;
+            for (size_t b = 0; b < items; ++b) {
+                const size_t rows = offset[i0 + b + 1] - offset[i0 + b];
+                cuda_ok(cudaMemcpyAsync(static_cast<char *>(features.data()) + offset[i0 + b] * W * es,
+                                        static_cast<const char *>(pooled.data()) + b * pooled_rows * W * es,
+                                        rows * W * es, cudaMemcpyDeviceToDevice, c.stream),
+                        "features");
+            }
+        });
+        if (bf) // fp32 VQ on the bf16 features
+            cuda_ok(static_cast<cudaError_t>(graph::to_float(features.data(), static_cast<float *>(b.features.data()),
+                                                             true, features.size(), c.stream)),
                     "features");
-        }
-    });
-    if (bf) { // fp32 VQ on the bf16 features
-        Tensor f32 = c.make(features.rows, features.cols, false);
-        cuda_ok(static_cast<cudaError_t>(graph::to_float(features.data(), static_cast<float *>(f32.data()), true,
-                                                         features.size(), c.stream)),
-                "features");
-        features = f32;
-    }
-    auto ids = quantize(c, features, m.get("codebook.weight"), m.cbnorm);
-    finite_or_fail(c, flag);
-    c.features = features;
-    return ids;
+        quantize_launch(c, b.features, m.get("codebook.weight"), m.cbnorm, b.ids.data());
+    };
+    std::vector<uint64_t> key{1, reinterpret_cast<uintptr_t>(mel), count, frames, bf ? 1u : 0u};
+    key.insert(key.end(), valid, valid + count);
+    return run_batch(c, key, replayable_input(mel), offset[count], alloc, work);
 }
 
 // Image graph (src/runtime.cpp:76-130) over `count` CHW images of one size
@@ -946,81 +1085,89 @@ std::vector<uint16_t> encode_images(Context &c, const float *pixels, size_t coun
     c.check();
     const size_t P = cfg.patch_size, gh = height / P, gw = width / P, n = gh * gw;
     const size_t item_floats = size_t(3) * height * width;
-    Tensor flag = c.make(1, 1, false);
-    cuda_ok(cudaMemsetAsync(flag.data(), 0, 4, c.stream), "input check");
-    Tensor pos = c.make(n, cfg.width, true);
-    cuda_ok(static_cast<cudaError_t>(graph::interpolate(m.get("pos_embed").data(), pos.data(), true,
-                                                        cfg.pos_height, gh, gw, cfg.width, c.stream)),
-            "interpolate");
-    Tensor features = c.make(count * n, cfg.code_dim, true);
-    const std::vector<int> all_keys(1, static_cast<int>(n));
-    const size_t chunk = chunk_items(count, n);
-    for_chunks(c, pixels, count, item_floats, chunk, [&](size_t i0, size_t items, const float *src) {
-        cuda_ok(static_cast<cudaError_t>(graph::finite_check(src, items * item_floats,
-                                                             static_cast<int *>(flag.data()), c.stream)),
-                "input check");
-        Tensor patches = c.make(items * n, 8 * P * P, true);
-        cuda_ok(static_cast<cudaError_t>(graph::image_patches(src, patches.data(), items, height, width, P,
-                                                              c.stream)),
-                "patches");
-        Tensor x = linear(c, patches, m.get("patch_embed.proj.weight"), &m.get("patch_embed.proj.bias"), true);
-        patches = {};
-        trace(c, x, "patch");
-        if (i0 == 0)
-            trace(c, pos, "position");
-        cuda_ok(static_cast<cudaError_t>(graph::add_periodic(x.data(), pos.data(), true, x.size(), pos.size(),
-                                                             c.stream)),
-                "positions");
-        trace(c, x, "embedding");
-        // Residual adds fused with the following norm, as in the audio graph.
-        Tensor mlp;
-        for (uint32_t i = 0; i < cfg.layers; ++i) {
+    auto alloc = [&] {
+        Bufs b;
+        b.flag = c.make(1, 1, false);
+        b.features = c.make(count * n, cfg.code_dim, true);
+        b.ids = c.make((count * n + 1) / 2, 1, false);
+        return b;
+    };
+    auto work = [&](const Bufs &b) {
+        cuda_ok(cudaMemsetAsync(b.flag.data(), 0, 4, c.stream), "input check");
+        const Tensor &flag = b.flag, &features = b.features;
+        Tensor pos = c.make(n, cfg.width, true);
+        cuda_ok(static_cast<cudaError_t>(graph::interpolate(m.get("pos_embed").data(), pos.data(), true,
+                                                            cfg.pos_height, gh, gw, cfg.width, c.stream)),
+                "interpolate");
+        const std::vector<int> all_keys(1, static_cast<int>(n));
+        const size_t chunk = chunk_items(count, n);
+        for_chunks(c, pixels, count, item_floats, chunk, [&](size_t i0, size_t items, const float *src) {
+            cuda_ok(static_cast<cudaError_t>(graph::finite_check(src, items * item_floats,
+                                                                 static_cast<int *>(flag.data()), c.stream)),
+                    "input check");
+            Tensor patches = c.make(items * n, 8 * P * P, true);
+            cuda_ok(static_cast<cudaError_t>(graph::image_patches(src, patches.data(), items, height, width, P,
+                                                                  c.stream)),
+                    "patches");
+            Tensor x = linear(c, patches, m.get("patch_embed.proj.weight"), &m.get("patch_embed.proj.bias"), true);
+            patches = {};
+            trace(c, x, "patch");
+            if (i0 == 0)
+                trace(c, pos, "position");
+            cuda_ok(static_cast<cudaError_t>(graph::add_periodic(x.data(), pos.data(), true, x.size(), pos.size(),
+                                                                 c.stream)),
+                    "positions");
+            trace(c, x, "embedding");
+            // Residual adds fused with the following norm, as in the audio graph.
+            Tensor mlp;
+            for (uint32_t i = 0; i < cfg.layers; ++i) {
+                c.check();
+                const std::string p = "blocks." + std::to_string(i) + ".";
+                auto proj = [&](const Tensor &in, const std::string &name) {
+                    return linear(c, in, m.get(name + ".weight"), m.opt(name + ".bias"));
+                };
+                Tensor z = add_norm(c, x, i ? &mlp : nullptr, m.get(p + "norm1.weight"), m.get(p + "norm1.bias"),
+                                    1e-6f);
+                if (i)
+                    trace(c, x, "layer." + std::to_string(i - 1));
+                if (i == 0)
+                    trace(c, z, "norm1.0");
+                z = proj(z, p + "attn.qkv");
+                if (i == 0)
+                    trace(c, z, "qkv.0");
+                z = attention(c, z, nullptr, nullptr, cfg.heads, 0, true, items, all_keys, nullptr);
+                if (i == 0)
+                    trace(c, z, "attention.0");
+                z = proj(z, p + "attn.proj");
+                z = add_norm(c, x, &z, m.get(p + "norm2.weight"), m.get(p + "norm2.bias"), 1e-6f);
+                if (i == 0)
+                    trace(c, x, "residual1.0");
+                z = proj(z, p + "mlp.fc1");
+                if (i == 0)
+                    trace(c, z, "fc1.0");
+                gelu_in_place(c, z);
+                if (i == 0)
+                    trace(c, z, "gelu.0");
+                mlp = proj(z, p + "mlp.fc2");
+                if (i == 0)
+                    trace(c, mlp, "fc2.0");
+            }
+            if (cfg.layers) {
+                add_in_place(c, x, mlp);
+                trace(c, x, "layer." + std::to_string(cfg.layers - 1));
+            }
             c.check();
-            const std::string p = "blocks." + std::to_string(i) + ".";
-            auto proj = [&](const Tensor &in, const std::string &name) {
-                return linear(c, in, m.get(name + ".weight"), m.opt(name + ".bias"));
-            };
-            Tensor z = add_norm(c, x, i ? &mlp : nullptr, m.get(p + "norm1.weight"), m.get(p + "norm1.bias"), 1e-6f);
-            if (i)
-                trace(c, x, "layer." + std::to_string(i - 1));
-            if (i == 0)
-                trace(c, z, "norm1.0");
-            z = proj(z, p + "attn.qkv");
-            if (i == 0)
-                trace(c, z, "qkv.0");
-            z = attention(c, z, nullptr, nullptr, cfg.heads, 0, true, items, all_keys, nullptr);
-            if (i == 0)
-                trace(c, z, "attention.0");
-            z = proj(z, p + "attn.proj");
-            z = add_norm(c, x, &z, m.get(p + "norm2.weight"), m.get(p + "norm2.bias"), 1e-6f);
-            if (i == 0)
-                trace(c, x, "residual1.0");
-            z = proj(z, p + "mlp.fc1");
-            if (i == 0)
-                trace(c, z, "fc1.0");
-            gelu_in_place(c, z);
-            if (i == 0)
-                trace(c, z, "gelu.0");
-            mlp = proj(z, p + "mlp.fc2");
-            if (i == 0)
-                trace(c, mlp, "fc2.0");
-        }
-        if (cfg.layers) {
-            add_in_place(c, x, mlp);
-            trace(c, x, "layer." + std::to_string(cfg.layers - 1));
-        }
-        c.check();
-        x = linear(c, x, m.get("quant_conv.weight"), &m.get("quant_conv.bias"), true);
-        trace(c, x, "projected");
-        cuda_ok(static_cast<cudaError_t>(graph::normalize(
-                    x.data(), static_cast<__nv_bfloat16 *>(features.data()) + i0 * n * cfg.code_dim, true, x.rows,
-                    x.cols, c.stream)),
-                "normalize");
-    });
-    auto ids = quantize(c, features, m.get("quantize.embedding.weight"), m.cbnorm);
-    finite_or_fail(c, flag);
-    c.features = features;
-    return ids;
+            x = linear(c, x, m.get("quant_conv.weight"), &m.get("quant_conv.bias"), true);
+            trace(c, x, "projected");
+            cuda_ok(static_cast<cudaError_t>(graph::normalize(
+                        x.data(), static_cast<__nv_bfloat16 *>(features.data()) + i0 * n * cfg.code_dim, true, x.rows,
+                        x.cols, c.stream)),
+                    "normalize");
+        });
+        quantize_launch(c, features, m.get("quantize.embedding.weight"), m.cbnorm, b.ids.data());
+    };
+    const std::vector<uint64_t> key{2, reinterpret_cast<uintptr_t>(pixels), count, height, width};
+    return run_batch(c, key, replayable_input(pixels), count * n, alloc, work);
 }
 
 } // namespace rt
@@ -1103,6 +1250,10 @@ int omni_context_create(omni_model *m, omni_context **out) {
                                "stream create");
         omni_b200::rt::blas_ok(cublasCreate(&c->impl.blas), "cuBLAS handle");
         omni_b200::rt::blas_ok(cublasSetStream(c->impl.blas, c->impl.stream), "cuBLAS stream");
+        omni_b200::rt::cuda_ok(cudaMalloc(&c->impl.blas_ws, size_t(32) << 20), "cuBLAS workspace");
+        omni_b200::rt::blas_ok(cublasSetWorkspace(c->impl.blas, c->impl.blas_ws, size_t(32) << 20), "cuBLAS workspace");
+        const char *graphs = std::getenv("OMNI_B200_GRAPHS");
+        c->impl.graphs = !(graphs && *graphs == '0');
         omni_b200::rt::cuda_ok(cudaStreamCreateWithFlags(&c->impl.copy, cudaStreamNonBlocking), "stream create");
         omni_b200::rt::cuda_ok(cudaHostAlloc(reinterpret_cast<void **>(&c->impl.cancel_host), sizeof(int),
                                              cudaHostAllocMapped),
@@ -1250,4 +1401,5 @@ int omni_context_copy_features(omni_context *c, float *out, size_t capacity, siz
 uint64_t omni_context_peak_workspace(const omni_context *c) {
     return c ? c->impl.memory->peak.load() : 0;
 }
+uint64_t omni_b200_context_graph_launches(const omni_context *c) { return c ? c->impl.graph_launches : 0; }
 } // extern "C"

@@ -421,3 +421,68 @@ def test_multi_device_encoder_matches_one_session(abi, ours, golden):
     with MultiDeviceEncoder(devices, lib=ours, model_path=GOLDEN / "audio.omni") as enc:
         for got, want in zip(enc.encode_audio(mels, valid), want_audio):
             np.testing.assert_array_equal(got, want)
+
+
+def test_repeated_batches_replay_a_cuda_graph(abi, ours, golden, monkeypatch):
+    """A batched call that repeats (same key, device or page-locked host input,
+    no trace callback) is captured on its second call and replayed afterwards.
+    The replay recomputes everything from the input: new data in the same
+    buffer gives that data's codes, bit-identical to an eager context's."""
+    monkeypatch.setenv("OMNI_B200_GRAPHS", "0")
+    with ours.load(GOLDEN / "audio.omni") as m:
+        eager = m.context()
+        monkeypatch.setenv("OMNI_B200_GRAPHS", "1")
+        s = m.context()
+        mels, valid = golden["audio_batch_mel"], golden["audio_batch_valid"]
+        dev = torch.from_numpy(mels).cuda()
+        want = eager.encode_audio_batch(mels, valid)
+        want_f = eager.features(len(want))
+        for i in range(4):
+            got = s.encode_audio_batch(tuple(dev.shape), valid, device_ptr=dev.data_ptr())
+            np.testing.assert_array_equal(got, want)
+            np.testing.assert_array_equal(s.features(len(got)), want_f)
+        assert s.graph_launches == 3  # captured on the second call, replayed twice
+        assert eager.graph_launches == 0
+        # Other data in the same buffer: the replay follows the input.
+        other = np.ascontiguousarray(mels[::-1])
+        dev.copy_(torch.from_numpy(other))
+        got = s.encode_audio_batch(tuple(dev.shape), valid, device_ptr=dev.data_ptr())
+        assert s.graph_launches == 4
+        np.testing.assert_array_equal(got, eager.encode_audio_batch(other, valid))
+        np.testing.assert_array_equal(s.features(len(got)), eager.features(len(got)))
+        # A cancellation before a replay: OMNI_CANCELLED, then the replay works again.
+        s.cancel()
+        with pytest.raises(abi.OmniError) as e:
+            s.encode_audio_batch(tuple(dev.shape), valid, device_ptr=dev.data_ptr())
+        assert e.value.status == 6
+        s.reset_cancel()
+        np.testing.assert_array_equal(s.encode_audio_batch(tuple(dev.shape), valid, device_ptr=dev.data_ptr()),
+                                      got)
+        # Page-locked host input is captured too; pageable host input stays eager.
+        pinned = torch.from_numpy(mels).pin_memory()
+        before = s.graph_launches
+        for _ in range(3):
+            np.testing.assert_array_equal(s.encode_audio_batch(pinned.numpy(), valid), want)
+        assert s.graph_launches == before + 2
+        before = s.graph_launches
+        for _ in range(3):
+            np.testing.assert_array_equal(s.encode_audio_batch(mels, valid), want)
+        assert s.graph_launches == before
+        s.close()
+        eager.close()
+    with ours.load(GOLDEN / "image.omni") as m:
+        monkeypatch.setenv("OMNI_B200_GRAPHS", "0")
+        eager = m.context()
+        monkeypatch.setenv("OMNI_B200_GRAPHS", "1")
+        s = m.context()
+        pxs = golden["image_batch_pixels"]
+        dev = torch.from_numpy(pxs).cuda()
+        want = eager.encode_images(pxs, patch=8)
+        want_f = eager.features(len(want))
+        for _ in range(3):
+            got = s.encode_images(tuple(dev.shape), patch=8, device_ptr=dev.data_ptr())
+            np.testing.assert_array_equal(got, want)
+            np.testing.assert_array_equal(s.features(len(got)), want_f)
+        assert s.graph_launches == 2
+        s.close()
+        eager.close()
