@@ -12,6 +12,7 @@
 #include <stdint.h>
 
 #include <atomic>
+#include <algorithm>
 #include <mutex>
 
 namespace omni_b200 {
@@ -436,6 +437,84 @@ __global__ void k_normalize(const void *x, void *y, bool bf16, size_t rows, size
     }
 }
 
+// One warp per pooled row; per step each lane reads `FACTOR` 16-byte vectors
+// (unconditional loads from valid rows, so that all of a step's loads are in
+// flight together), forms VEC pooled values (the group's rows added in order,
+// then / factor, rounded in the bf16 profile) and stores them as fp32.  The
+// squared norm is a warp reduction of the lanes' partial sums: the fp32 VQ
+// uses it only in its approximate search, whose candidate window bounds the
+// fp32 rounding of a sum of squares in any order.
+template <bool BF16, int FACTOR>
+__global__ void __launch_bounds__(128) k_pool_features(const void *x, size_t items, size_t rows_per_item,
+                                                       size_t cols, const int *out_offset, float *features,
+                                                       float *xn) {
+    constexpr int VEC = kVec<BF16>, TW = 32 * VEC;
+    const int lane = threadIdx.x & 31, warps = blockDim.x >> 5;
+    const size_t pooled = (rows_per_item + FACTOR - 1) / FACTOR;
+    for (size_t w = static_cast<size_t>(blockIdx.x) * warps + (threadIdx.x >> 5); w < items * pooled;
+         w += static_cast<size_t>(gridDim.x) * warps) {
+        const size_t b = w / pooled, t = w % pooled;
+        if (t >= static_cast<size_t>(out_offset[b + 1] - out_offset[b]))
+            continue;
+        const size_t out_row = static_cast<size_t>(out_offset[b]) + t, r0 = b * rows_per_item + t * FACTOR;
+        float part = 0.f;
+#pragma unroll 2
+        for (size_t c = static_cast<size_t>(lane) * VEC; c < cols; c += TW) {
+            float v[VEC];
+#pragma unroll
+            for (int e = 0; e < VEC; ++e)
+                v[e] = 0.f;
+            float a[FACTOR][VEC];
+#pragma unroll
+            for (int k = 0; k < FACTOR; ++k) {
+                const bool ok = t * FACTOR + k < rows_per_item;
+                vload<BF16>(x, (ok ? r0 + k : r0) * cols + c, a[k]);
+                if (!ok)
+#pragma unroll
+                    for (int e = 0; e < VEC; ++e)
+                        a[k][e] = 0.f;
+            }
+#pragma unroll
+            for (int k = 0; k < FACTOR; ++k)
+#pragma unroll
+                for (int e = 0; e < VEC; ++e)
+                    v[e] = __fadd_rn(v[e], a[k][e]);
+            float *dst = features + out_row * cols + c;
+#pragma unroll
+            for (int e = 0; e < VEC; e += 4) {
+                float4 q;
+                q.x = rnd(v[e] / static_cast<float>(FACTOR), BF16);
+                q.y = rnd(v[e + 1] / static_cast<float>(FACTOR), BF16);
+                q.z = rnd(v[e + 2] / static_cast<float>(FACTOR), BF16);
+                q.w = rnd(v[e + 3] / static_cast<float>(FACTOR), BF16);
+                *reinterpret_cast<float4 *>(dst + e) = q;
+                part = fmaf(q.x, q.x, fmaf(q.y, q.y, fmaf(q.z, q.z, fmaf(q.w, q.w, part))));
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+            part += __shfl_xor_sync(0xffffffffu, part, o);
+        if (lane == 0)
+            xn[out_row] = part;
+    }
+}
+
+__global__ void k_bias_normalize(const __nv_bfloat16 *x, const __nv_bfloat16 *bias, __nv_bfloat16 *y,
+                                 size_t rows, size_t cols) {
+    GRID_STRIDE(r, rows) {
+        float n = 0.f;
+        for (size_t j = 0; j < cols; ++j) {
+            const float v = rnd(__fadd_rn(__bfloat162float(x[r * cols + j]), __bfloat162float(bias[j])), true);
+            n = __fadd_rn(n, __fmul_rn(v, v));
+        }
+        n = fmaxf(rnd(sqrtf(n), true), rnd(1e-12f, true));
+        for (size_t j = 0; j < cols; ++j) {
+            const float v = rnd(__fadd_rn(__bfloat162float(x[r * cols + j]), __bfloat162float(bias[j])), true);
+            y[r * cols + j] = __float2bfloat16_rn(v / n);
+        }
+    }
+}
+
 __global__ void k_image_patches(const float *px, __nv_bfloat16 *y, size_t count, size_t height,
                                 size_t width, size_t patch) {
     const size_t gw = width / patch, pd = 8 * patch * patch, cells = (height / patch) * gw;
@@ -754,6 +833,29 @@ int interpolate(const void *x, void *y, bool bf16, size_t source, size_t height,
 }
 int normalize(const void *x, void *y, bool bf16, size_t rows, size_t cols, cudaStream_t s) {
     k_normalize<<<blocks_for(rows, 128), 128, 0, s>>>(x, y, bf16, rows, cols);
+    return status();
+}
+int pool_features(const void *x, bool bf16, size_t items, size_t rows_per_item, size_t cols, size_t factor,
+                  const int *out_offset, float *features, float *xn, cudaStream_t s) {
+    if (items == 0 || cols == 0)
+        return 0;
+    // 16-byte vectors of x and of the fp32 feature rows; the reference's pool
+    // factor (4; src/model.cpp:43) is compiled in.
+    if (reinterpret_cast<uintptr_t>(x) % 16 != 0 || reinterpret_cast<uintptr_t>(features) % 16 != 0 ||
+        cols % (bf16 ? 8 : 4) != 0 || factor != 4)
+        return static_cast<int>(cudaErrorInvalidValue);
+    const size_t rows = items * ((rows_per_item + factor - 1) / factor);
+    const unsigned blocks = static_cast<unsigned>(std::min<size_t>((rows + 3) / 4, 148 * 32));
+    if (bf16)
+        k_pool_features<true, 4><<<blocks, 128, 0, s>>>(x, items, rows_per_item, cols, out_offset, features, xn);
+    else
+        k_pool_features<false, 4><<<blocks, 128, 0, s>>>(x, items, rows_per_item, cols, out_offset, features, xn);
+    return status();
+}
+int bias_normalize(const void *x, const void *b, void *y, size_t rows, size_t cols, cudaStream_t s) {
+    k_bias_normalize<<<blocks_for(rows, 128), 128, 0, s>>>(static_cast<const __nv_bfloat16 *>(x),
+                                                            static_cast<const __nv_bfloat16 *>(b),
+                                                            static_cast<__nv_bfloat16 *>(y), rows, cols);
     return status();
 }
 int image_patches(const float *pixels, void *y, size_t count, size_t height, size_t width, size_t patch,

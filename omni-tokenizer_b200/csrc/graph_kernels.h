@@ -47,6 +47,21 @@ int interpolate(const void *x, void *y, bool bf16, size_t source, size_t height,
                 size_t cols, cudaStream_t s);
 // Row-wise L2 normalisation with the reference's max(r(sqrt(n)), r(1e-12)) guard.
 int normalize(const void *x, void *y, bool bf16, size_t rows, size_t cols, cudaStream_t s);
+// Audio graph tail (pre-VQ epilogue in one pass): mean-pool `factor` rows of
+// each of `items` stacked sequences of `rows_per_item` rows of x (bf16 or
+// fp32), keep the first out_offset[b+1] - out_offset[b] pooled rows of item b
+// and write them as fp32 rows out_offset[b] + t of `features` (what pool, the
+// per-item row copies and the fp32 conversion wrote one after another), and
+// their squared norms xn for the fp32 VQ's approximate search (a warp
+// reduction: any fp32 summation order is within that search's window).
+// Needs factor 4, 16-byte aligned x and features and cols a multiple of 8
+// (bf16) or 4 (fp32); else cudaErrorInvalidValue.
+int pool_features(const void *x, bool bf16, size_t items, size_t rows_per_item, size_t cols, size_t factor,
+                  const int *out_offset, float *features, float *xn, cudaStream_t s);
+// Image graph tail (pre-VQ epilogue in one pass, bf16): per row v = r(x + b),
+// then y = r(v / max(r(sqrt(sum v^2)), r(1e-12))) -- image_conv's bias added
+// after the rounded GEMM, followed by normalize.
+int bias_normalize(const void *x, const void *b, void *y, size_t rows, size_t cols, cudaStream_t s);
 // `count` CHW fp32 images -> bf16 patches [count*gh*gw, 8*p*p] (channel-padded to 8
 // per pixel).
 int image_patches(const float *pixels, void *y, size_t count, size_t height, size_t width, size_t patch,

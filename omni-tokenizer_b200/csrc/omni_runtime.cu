@@ -703,13 +703,14 @@ Tensor attention(Context &c, const Tensor &q, const Tensor *k, const Tensor *v, 
 // codebook in windows of kVqCancelWindow codes, and the call reports
 // OMNI_CANCELLED once the stream is drained.
 // Launch part: uint16 ids of x's rows into `ids` (device), asynchronously.
-void quantize_launch(Context &c, const Tensor &x, const Tensor &cb, const Tensor &cbnorm, void *ids) {
+void quantize_launch(Context &c, const Tensor &x, const Tensor &cb, const Tensor &cbnorm, void *ids,
+                     const float *xnorm = nullptr) {
     const int profile = x.bf16 ? OMNI_B200_BF16 : OMNI_B200_F32;
     const size_t ws_bytes = omni_b200_vq_workspace(x.rows, x.cols, cb.rows, profile);
     Tensor ws_holder;
     void *ws = c.scratch(ws_bytes, ws_holder);
     op_ok(vq_argmin(x.data(), cb.data(), cbnorm.data(), ids, x.rows, x.cols, cb.rows, profile, 1, ws, ws_bytes,
-                    c.cancel_dev, c.stream),
+                    c.cancel_dev, c.stream, xnorm),
           "quantize");
 }
 
@@ -966,22 +967,27 @@ std::vector<uint16_t> encode_audio_batch(Context &c, const float *mel, size_t co
         keys[i] = static_cast<int>((valid[i] + 1) / 2);
     const size_t chunk = chunk_items(count, T);
     // Persistent buffers: flag, fp32 features (the VQ input and what
-    // omni_context_copy_features returns), ids, per-segment key limits.
+    // omni_context_copy_features returns), ids, and per segment the key limit
+    // followed by the first feature row (count + 1 offsets).
+    std::vector<int> limits(keys);
+    for (size_t i = 0; i <= count; ++i)
+        limits.push_back(static_cast<int>(offset[i]));
     auto alloc = [&] {
         Bufs b;
         b.flag = c.make(1, 1, false);
         b.features = c.make(offset[count], W, false);
         b.ids = c.make((offset[count] + 1) / 2, 1, false);
-        b.keys = c.make(count, 1, false);
-        cuda_ok(cudaMemcpyAsync(b.keys.data(), keys.data(), count * 4, cudaMemcpyHostToDevice, c.stream),
+        b.keys = c.make(limits.size(), 1, false);
+        cuda_ok(cudaMemcpyAsync(b.keys.data(), limits.data(), limits.size() * 4, cudaMemcpyHostToDevice, c.stream),
                 "key counts");
         return b;
     };
     auto work = [&](const Bufs &b) {
         cuda_ok(cudaMemsetAsync(b.flag.data(), 0, 4, c.stream), "input check");
         Tensor flag = b.flag;
-        // bf16 mode: the pooled features stay bf16 until the fp32 copy for the VQ.
-        Tensor features = bf ? c.make(offset[count], W, true) : b.features;
+        // Squared norms of the feature rows, written with them for the VQ.
+        Tensor xn = c.make(offset[count], 1, false);
+        const int *row_offsets = static_cast<const int *>(b.keys.data()) + count;
         for_chunks(c, mel, count, C * T, chunk, [&](size_t i0, size_t items, const float *src) {
             cuda_ok(static_cast<cudaError_t>(graph::finite_check(src, items * C * T, static_cast<int *>(flag.data()),
                                                                  c.stream)),
@@ -1047,27 +1053,19 @@ std::vector<uint16_t> encode_audio_batch(Context &c, const float *mel, size_t co
                 trace(c, x, "layer." + std::to_string(cfg.layers - 1));
             }
             // The next cancellation point is the VQ pass (src/runtime.cpp:47-66).
-            const size_t pooled_rows = (L + cfg.pool_size - 1) / cfg.pool_size;
-            Tensor pooled = c.make(items * pooled_rows, W, x.bf16);
-            cuda_ok(static_cast<cudaError_t>(graph::pool(x.data(), pooled.data(), x.bf16, x.rows, W, cfg.pool_size,
-                                                         c.stream)),
+            // Pre-VQ epilogue in one pass (src/runtime.cpp:64-66): mean-pool by
+            // pool_size per segment, keep each segment's ceil(valid / 8) rows as
+            // fp32 features (bf16 mode: the bf16 pooled values), and write their
+            // squared norms for the fp32 VQ.  Pooling the stacked rows equals
+            // pooling per segment: L is a multiple of the pool size (frames % 8
+            // == 0), so no group straddles two segments.
+            cuda_ok(static_cast<cudaError_t>(graph::pool_features(
+                        x.data(), x.bf16, items, L, W, cfg.pool_size, row_offsets + i0,
+                        static_cast<float *>(b.features.data()), static_cast<float *>(xn.data()), c.stream)),
                     "pool");
-            // pool over the stacked rows equals pool per segment: L is a multiple of
-            // the pool size (frames % 8 == 0), so no group straddles two segments.
-            const size_t es = bf ? 2 : 4;
-            for (size_t b = 0; b < items; ++b) {
-                const size_t rows = offset[i0 + b + 1] - offset[i0 + b];
-                cuda_ok(cudaMemcpyAsync(static_cast<char *>(features.data()) + offset[i0 + b] * W * es,
-                                        static_cast<const char *>(pooled.data()) + b * pooled_rows * W * es,
-                                        rows * W * es, cudaMemcpyDeviceToDevice, c.stream),
-                        "features");
-            }
         });
-        if (bf) // fp32 VQ on the bf16 features
-            cuda_ok(static_cast<cudaError_t>(graph::to_float(features.data(), static_cast<float *>(b.features.data()),
-                                                             true, features.size(), c.stream)),
-                    "features");
-        quantize_launch(c, b.features, m.get("codebook.weight"), m.cbnorm, b.ids.data());
+        quantize_launch(c, b.features, m.get("codebook.weight"), m.cbnorm, b.ids.data(),
+                        static_cast<const float *>(xn.data()));
     };
     std::vector<uint64_t> key{1, reinterpret_cast<uintptr_t>(mel), count, frames, bf ? 1u : 0u};
     key.insert(key.end(), valid, valid + count);
@@ -1157,12 +1155,20 @@ std::vector<uint16_t> encode_images(Context &c, const float *pixels, size_t coun
                 trace(c, x, "layer." + std::to_string(cfg.layers - 1));
             }
             c.check();
-            x = linear(c, x, m.get("quant_conv.weight"), &m.get("quant_conv.bias"), true);
-            trace(c, x, "projected");
-            cuda_ok(static_cast<cudaError_t>(graph::normalize(
-                        x.data(), static_cast<__nv_bfloat16 *>(features.data()) + i0 * n * cfg.code_dim, true, x.rows,
-                        x.cols, c.stream)),
-                    "normalize");
+            void *feat = static_cast<__nv_bfloat16 *>(features.data()) + i0 * n * cfg.code_dim;
+            if (c.trace) { // the "projected" stage needs image_conv's output on its own
+                x = linear(c, x, m.get("quant_conv.weight"), &m.get("quant_conv.bias"), true);
+                trace(c, x, "projected");
+                cuda_ok(static_cast<cudaError_t>(graph::normalize(x.data(), feat, true, x.rows, x.cols, c.stream)),
+                        "normalize");
+            } else {
+                // image_conv's bias (added after the rounded GEMM) and the L2
+                // normalisation in one pass over the projected rows.
+                x = linear(c, x, m.get("quant_conv.weight"), nullptr);
+                cuda_ok(static_cast<cudaError_t>(graph::bias_normalize(x.data(), m.get("quant_conv.bias").data(), feat,
+                                                                       x.rows, x.cols, c.stream)),
+                        "normalize");
+            }
         });
         quantize_launch(c, features, m.get("quantize.embedding.weight"), m.cbnorm, b.ids.data());
     };

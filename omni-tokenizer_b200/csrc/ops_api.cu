@@ -434,7 +434,7 @@ namespace omni_b200 {
 
 int vq_argmin(const void *x, const void *codebook, const void *cbnorm, void *ids, size_t rows, size_t dim,
               size_t codes, int profile, int ids_u16, void *workspace, size_t workspace_bytes,
-              const volatile int *cancel, cudaStream_t stream) {
+              const volatile int *cancel, cudaStream_t stream, const float *xnorm) {
     g_error.clear();
     if (!x || !codebook || !cbnorm || !ids)
         return fail(1, "vq_argmin: null pointer");
@@ -468,6 +468,7 @@ int vq_argmin(const void *x, const void *codebook, const void *cbnorm, void *ids
     a.ids = ids;
     a.ids_u16 = ids_u16 ? 1 : 0;
     a.cancel = cancel;
+    a.xnorm = fp32 ? xnorm : nullptr;
     a.err = kernel_error_word();
     if (!a.err)
         return fail(7, "vq_argmin: no CUDA device");

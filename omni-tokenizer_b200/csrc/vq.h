@@ -30,6 +30,11 @@ struct VqArgs {
     // when they start skips its window (the ids are then incomplete; the caller
     // reports the cancellation).
     const volatile int *cancel = nullptr;
+    // fp32 profile: the rows' squared norms when the caller produced them with
+    // x (any fp32 summation order: they enter only the approximate search,
+    // whose window bounds fp32 rounding of the sum); the squares pass is then
+    // skipped.
+    const float *xnorm = nullptr;
 };
 
 constexpr int kVqCancelWindow = 4096; // codes per launch when a cancel flag is given
@@ -44,7 +49,7 @@ enum VqsMode { kVqsBf16 = 0, kVqsApprox = 1, kVqsCand = 2 };
 
 struct VqsParams {
     CUtensorMap tx, tc;           // x / codebook maps, 128-byte column chunks
-    float *xn;                    // [rows] |x|^2 (bf16 profile: the bf16 value)
+    const float *xn;              // [rows] |x|^2 (bf16 profile: the bf16 value)
     const void *cbnorm;           // bf16 [codes] (bf16 profile) or f32 [codes]
     unsigned long long *keys;     // [rows] (order bits of dist) << 32 | id
     unsigned *cand_count;         // fp32 profile: [rows]
@@ -61,7 +66,7 @@ struct VqsParams {
 // the encoder graphs pass their context's flag.
 int vq_argmin(const void *x, const void *codebook, const void *cbnorm, void *ids, size_t rows, size_t dim,
               size_t codes, int profile, int ids_u16, void *workspace, size_t workspace_bytes,
-              const volatile int *cancel, cudaStream_t stream);
+              const volatile int *cancel, cudaStream_t stream, const float *xnorm = nullptr);
 
 // Scratch bytes for vq_stream_launch (VqArgs::keys points at it).
 size_t vq_stream_workspace(size_t rows, int profile_fp32);

@@ -539,7 +539,8 @@ int vq_stream_launch(const VqArgs &a, int profile_fp32, cudaStream_t stream) {
     uint8_t *ws = static_cast<uint8_t *>(a.keys);
     const size_t rows = static_cast<size_t>(a.rows);
     p.keys = reinterpret_cast<unsigned long long *>(ws);
-    p.xn = reinterpret_cast<float *>(ws + 8 * rows);
+    float *xn_ws = reinterpret_cast<float *>(ws + 8 * rows);
+    p.xn = xn_ws;
     if (tf32) {
         p.cand_count = reinterpret_cast<unsigned *>(ws + 12 * rows);
         p.cand = reinterpret_cast<unsigned *>(ws + 16 * rows);
@@ -558,8 +559,11 @@ int vq_stream_launch(const VqArgs &a, int profile_fp32, cudaStream_t stream) {
     const int threads = 256;
     const int kb = (a.rows + threads - 1) / threads;
     vqs_init<<<kb < 4096 ? kb : 4096, threads, 0, stream>>>(p.keys, p.cand_count, a.rows);
-    // |x|^2 per row in the profile's arithmetic (bf16 profile: the bf16 value).
-    if ((rc = squares_launch(a.x, p.xn, a.rows, a.dim, tf32 ? 0 : 1, 0, stream)))
+    // |x|^2 per row in the profile's arithmetic (bf16 profile: the bf16 value),
+    // unless the caller wrote the fp32 norms alongside x.
+    if (tf32 && a.xnorm)
+        p.xn = a.xnorm;
+    else if ((rc = squares_launch(a.x, xn_ws, a.rows, a.dim, tf32 ? 0 : 1, 0, stream)))
         return rc;
     // One launch per codebook window: the whole codebook, or (when the caller
     // can cancel) windows of kVqCancelWindow codes, widened in multiples of it
