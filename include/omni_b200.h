@@ -110,8 +110,9 @@ OMNI_B200_API int omni_b200_vq_argmin(const void *x, const void *codebook, const
  * caller sets to nonzero to cancel; NULL behaves as omni_b200_vq_argmin.  With
  * a flag, the wide (dim > 128) and fp32 passes run the codebook in windows of
  * 4096 codes (a multiple of 4096 when the rows are too few for one window to
- * give every SM two units of work), one launch each, and a launch that starts
- * after the flag is set skips its window.  The call is asynchronous like the others: after
+ * give every SM two units of work), one launch each; the flag is copied to the
+ * workspace in stream order before each window, and a window whose copy is
+ * nonzero is skipped.  The call is asynchronous like the others: after
  * synchronising, a caller that set the flag discards ids and reports
  * OMNI_CANCELLED, as Ops::quantize throws Error(OMNI_CANCELLED). */
 OMNI_B200_API int omni_b200_vq_argmin_cancellable(const void *x, const void *codebook, const void *cbnorm,

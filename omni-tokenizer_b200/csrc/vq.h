@@ -26,9 +26,10 @@ struct VqArgs {
     // Optional cancellation flag the device can read (mapped pinned host memory
     // or device memory): the streamed kernels run the codebook in windows of
     // kVqCancelWindow codes (a multiple of it when the rows are too few to fill
-    // the GPU), one launch each, and a launch whose CTAs see a nonzero flag
-    // when they start skips its window (the ids are then incomplete; the caller
-    // reports the cancellation).
+    // the GPU), one launch each; the flag is copied to device memory in stream
+    // order just before each window's launch, and a launch whose copy is
+    // nonzero skips its window (the ids are then incomplete; the caller reports
+    // the cancellation).
     const volatile int *cancel = nullptr;
     // fp32 profile: the rows' squared norms when the caller produced them with
     // x (any fp32 summation order: they enter only the approximate search,
@@ -57,8 +58,8 @@ struct VqsParams {
     int rows, dim, codes, chunks;
     int code_lo, code_hi;         // codebook window of this launch, [code_lo, code_hi)
     int slices, slice_codes;      // the window split into slices of slice_codes codes
-    float win_a, win_b;           // fp32 profile: candidate window a |x||c| + b (|x|^2 + |c|^2)
-    const volatile int *cancel;   // nonzero when the CTA starts: skip the window
+    float win_a, win_c, win_s;    // fp32 profile: window a |x||c| + c |c|^2 + s (|x|^2 + |c|^2)
+    const volatile int *cancel;   // device copy of the flag: nonzero skips the window
     int *err;
 };
 

@@ -16,17 +16,26 @@
 // fp32 profile on B200.  The tensor cores have no fp32 MMA, so the
 // approximate distances come from kind::tf32 (inputs truncated to 10 mantissa
 // bits).  The candidate window is therefore a bound written for this kernel,
-// not the reference's fp32 gamma: for every code
-//   |approx(c) - exact(c)| <= w(c) = a |x| |c| + b (|x|^2 + |c|^2),
-//   a = 2^-7 + (dim + 1) 2^-21,   b = (dim + 4) 2^-22
+// not the reference's fp32 gamma.  approx(c) = fma(-2, dot(c), xn + cn(c)) uses
+// the same fp32 row norm xn for every code of the row, so the error of xn is
+// a common offset d: approx(c) = exact(c) + d + e(c), and only the per-code
+// part needs a bound:
+//   |e(c)| <= w(c) = a |x| |c| + bc |c|^2 + bs (|x|^2 + |c|^2),
+//   a = 2^-7 + (dim + 1) 2^-21,   bc = dim 2^-22,   bs = 2^-20
 // The dot product carries the tf32 truncation, at most 2^-10 per factor, so
 // 2|x.c - tf32 dot| <= (2^-8 + 2^-19) sum_k |x_k c_k| <= (2^-8 + 2^-19)|x||c|
 // (Cauchy-Schwarz), plus the fp32 accumulation, at most dim 2^-23 per unit of
-// sum |x_k c_k|; the fp32 norms and the final fma add at most (dim + 2) 2^-24
-// (|x|^2 + |c|^2).  a and b carry a factor of two of slack over these, and
-// |x| |c| is taken as sqrt(|x|^2) sqrt(|c|^2) of the fp32 norms.  With b* the
-// code of the smallest approximate distance, the exact nearest code c* satisfies
-//   approx(c*) - w(c*) <= approx(b*) + w(b*),
+// sum |x_k c_k|; the codebook norm cn (fp32, in column order) is within
+// (dim - 1) 2^-24 |c|^2; the sum xn + cn and the final fma round twice, at most
+// 3 2^-24 (|x|^2 + |c|^2) together, and evaluating the test below rounds lo(c)
+// and the threshold once each (distances are at most 2 (|x|^2 + |c|^2), so at
+// most 2 2^-24 (|x|^2 + |c|^2) each).  a, bc and bs carry a factor of two of
+// slack over these, and |x| |c| is taken as sqrt(|x|^2) sqrt(|c|^2) of the fp32
+// norms.
+// (The row norm may come from any fp32 summation order: its error is the common
+// d.)  With b* the code of the smallest approximate distance, the exact nearest
+// code c* satisfies approx(c*) - w(c*) <= exact(c*) + d <= exact(b*) + d <=
+// approx(b*) + w(b*),
 // so the candidate set {c : approx(c) - w(c) <= approx(b*) + w(b*)} contains c*
 // and every code whose direct distance ties with it.  The reference's own
 // candidate set also contains c* (its gamma bound), and both pick the smallest
@@ -233,7 +242,7 @@ __global__ void __launch_bounds__(kVqsThreads, 1) vq_stream_kernel(const __grid_
                     const int b = static_cast<int>(key & 0xffffffffu);
                     const float best = vqs_from_order_bits(static_cast<uint32_t>(key >> 32));
                     const float cb = static_cast<const float *>(p.cbnorm)[b];
-                    thr = best + p.win_a * sqrtf(xn) * sqrtf(cb) + p.win_b * (xn + cb);
+                    thr = best + p.win_a * sqrtf(xn) * sqrtf(cb) + p.win_c * cb + p.win_s * (xn + cb);
                 }
                 if (!(thr < INFINITY)) // non-finite: every code is a candidate
                     thr = INFINITY;
@@ -245,6 +254,45 @@ __global__ void __launch_bounds__(kVqsThreads, 1) vq_stream_kernel(const __grid_
             int best_id = 0;
             for (int c = c_begin; c < c_end; c += 256, ++n_acc) {
                 const int buf = n_acc & 1;
+                // The code tile's norms: lane l holds codes c + 8 l .. c + 8 l + 7
+                // (one coalesced 16- or 32-byte load per lane, issued before the
+                // accumulator wait), handed to every row thread by shuffles.
+                // Codes past the end hold +inf (bf16 profile: 0, masked below).
+                const int kl = c + 8 * lane;
+                uint4 cw = make_uint4(0u, 0u, 0u, 0u);
+                float cf[8];
+                if constexpr (MODE == kVqsBf16) {
+                    const unsigned short *cs = static_cast<const unsigned short *>(p.cbnorm);
+                    if (kl + 8 <= p.codes) {
+                        cw = *reinterpret_cast<const uint4 *>(cs + kl);
+                    } else {
+                        unsigned short h[8];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e)
+                            h[e] = kl + e < p.codes ? cs[kl + e] : 0;
+                        cw = make_uint4(h[0] | (uint32_t(h[1]) << 16), h[2] | (uint32_t(h[3]) << 16),
+                                        h[4] | (uint32_t(h[5]) << 16), h[6] | (uint32_t(h[7]) << 16));
+                    }
+                } else {
+                    const float *cn = static_cast<const float *>(p.cbnorm);
+                    if (kl + 8 <= p.codes) {
+                        const float4 a = *reinterpret_cast<const float4 *>(cn + kl);
+                        const float4 b = *reinterpret_cast<const float4 *>(cn + kl + 4);
+                        cf[0] = a.x, cf[1] = a.y, cf[2] = a.z, cf[3] = a.w;
+                        cf[4] = b.x, cf[5] = b.y, cf[6] = b.z, cf[7] = b.w;
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 8; ++e)
+                            cf[e] = kl + e < p.codes ? cn[kl + e] : INFINITY;
+                    }
+                }
+                // kVqsCand: sqrt(|c|^2) once per code, by the lane that holds it.
+                float cr[8];
+                if constexpr (MODE == kVqsCand) {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e)
+                        cr[e] = sqrtf(cf[e]);
+                }
                 ok = __all_sync(0xffffffffu,
                                 mbar_wait(&acc_full[buf], (n_acc >> 1) & 1, err, kErrWaitS));
                 if (!ok)
@@ -256,19 +304,18 @@ __global__ void __launch_bounds__(kVqsThreads, 1) vq_stream_kernel(const __grid_
                     tmem_ld32(tmem + lane_base + buf * 256 + ch * 32, dv);
                     const int code0 = c + ch * 32;
                     tmem_wait_ld();
-                    if (!live || code0 >= p.codes)
+                    if (code0 >= p.codes) // warp-uniform
                         continue;
                     if constexpr (MODE == kVqsBf16) {
-                        const unsigned short *cs = static_cast<const unsigned short *>(p.cbnorm);
                         float cmin = INFINITY;
                         float dist[32];
 #pragma unroll
                         for (int q = 0; q < 16; ++q) {
+                            // Codes code0 + 2q, 2q + 1: lane 4 ch + q / 4, word q % 4.
+                            const uint32_t w = q % 4 == 0 ? cw.x : q % 4 == 1 ? cw.y : q % 4 == 2 ? cw.z : cw.w;
+                            const uint32_t cwq = __shfl_sync(0xffffffffu, w, 4 * ch + q / 4);
                             const int k0 = code0 + 2 * q;
-                            const unsigned short h0 = k0 < p.codes ? cs[k0] : 0;
-                            const unsigned short h1 = k0 + 1 < p.codes ? cs[k0 + 1] : 0;
-                            const uint32_t cw = h0 | (static_cast<uint32_t>(h1) << 16);
-                            const __nv_bfloat162 c2 = *reinterpret_cast<const __nv_bfloat162 *>(&cw);
+                            const __nv_bfloat162 c2 = *reinterpret_cast<const __nv_bfloat162 *>(&cwq);
                             const __nv_bfloat162 dd = __floats2bfloat162_rn(__uint_as_float(dv[2 * q]),
                                                                             __uint_as_float(dv[2 * q + 1]));
                             const __nv_bfloat162 s2 = __hadd2(x2, c2);
@@ -277,7 +324,7 @@ __global__ void __launch_bounds__(kVqsThreads, 1) vq_stream_kernel(const __grid_
                             dist[2 * q + 1] = k0 + 1 < p.codes ? __bfloat162float(t.y) : INFINITY;
                             cmin = fminf(cmin, fminf(dist[2 * q], dist[2 * q + 1]));
                         }
-                        if (cmin < best) {
+                        if (live && cmin < best) {
                             best = cmin;
 #pragma unroll
                             for (int e = 31; e >= 0; --e)
@@ -285,22 +332,23 @@ __global__ void __launch_bounds__(kVqsThreads, 1) vq_stream_kernel(const __grid_
                                     best_id = code0 + e;
                         }
                     } else {
-                        const float *cn = static_cast<const float *>(p.cbnorm);
 #pragma unroll
                         for (int e = 0; e < 32; ++e) {
                             const int k = code0 + e;
-                            if (k >= p.codes)
-                                break;
-                            const float cnk = cn[k];
+                            // Code code0 + e: lane 4 ch + e / 8, element e % 8.
+                            const float cnk = __shfl_sync(0xffffffffu, cf[e % 8], 4 * ch + e / 8);
                             const float dist = fmaf(-2.f, __uint_as_float(dv[e]), xn + cnk);
                             if constexpr (MODE == kVqsApprox) {
-                                if (dist < best) {
+                                if (k < p.codes && dist < best) {
                                     best = dist;
                                     best_id = k;
                                 }
                             } else {
+                                const float crk = __shfl_sync(0xffffffffu, cr[e % 8], 4 * ch + e / 8);
+                                if (!live || k >= p.codes)
+                                    continue;
                                 // Candidate unless provably outside the window.
-                                const float lo = dist - (sx * sqrtf(cnk) + p.win_b * (xn + cnk));
+                                const float lo = dist - (sx * crk + p.win_c * cnk + p.win_s * (xn + cnk));
                                 if (!(lo <= thr) && isfinite(lo) && thr < INFINITY)
                                     continue;
                                 const unsigned slot = atomicAdd(p.cand_count + row, 1u);
@@ -518,9 +566,10 @@ int plan_units(VqsParams &p) {
 } // namespace
 
 size_t vq_stream_workspace(size_t rows, int profile_fp32) {
-    // keys (8) + xn (4) [+ candidate count (4) + candidate list] per row.
+    // keys (8) + xn (4) [+ candidate count (4) + candidate list] per row, then
+    // 256 bytes for the device copy of a cancellation flag.
     const size_t per_row = profile_fp32 ? 16 + 4 * static_cast<size_t>(kVqCandCap) : 12;
-    return (rows * per_row + 255) / 256 * 256;
+    return (rows * per_row + 255) / 256 * 256 + 256;
 }
 
 int vq_stream_launch(const VqArgs &a, int profile_fp32, cudaStream_t stream) {
@@ -545,6 +594,12 @@ int vq_stream_launch(const VqArgs &a, int profile_fp32, cudaStream_t stream) {
         p.cand_count = reinterpret_cast<unsigned *>(ws + 12 * rows);
         p.cand = reinterpret_cast<unsigned *>(ws + 16 * rows);
     }
+    // The cancellation flag is copied to device memory before each window's
+    // launch and the CTAs read that copy: the flag usually lives in mapped
+    // pinned host memory, and 148 CTAs reading host memory as they start made
+    // each launch about four times slower (44 -> 179 us at 750 x 1024 fp32).
+    int *flag_dev = reinterpret_cast<int *>(ws + (rows * (tf32 ? 16 + 4 * static_cast<size_t>(kVqCandCap) : 12) + 255) /
+                                                     256 * 256);
     p.cbnorm = a.cbnorm;
     p.rows = a.rows;
     p.dim = a.dim;
@@ -553,9 +608,10 @@ int vq_stream_launch(const VqArgs &a, int profile_fp32, cudaStream_t stream) {
     // Window coefficients (see the top of this file), rounded up by 1e-4 for
     // the fp32 evaluation of the window itself.
     p.win_a = static_cast<float>((std::ldexp(1.0, -7) + (a.dim + 1.0) * std::ldexp(1.0, -21)) * 1.0001);
-    p.win_b = static_cast<float>((a.dim + 4.0) * std::ldexp(1.0, -22) * 1.0001);
+    p.win_c = static_cast<float>(a.dim * std::ldexp(1.0, -22) * 1.0001);
+    p.win_s = static_cast<float>(std::ldexp(1.0, -20) * 1.0001);
     p.err = a.err;
-    p.cancel = a.cancel;
+    p.cancel = a.cancel ? flag_dev : nullptr;
     const int threads = 256;
     const int kb = (a.rows + threads - 1) / threads;
     vqs_init<<<kb < 4096 ? kb : 4096, threads, 0, stream>>>(p.keys, p.cand_count, a.rows);
@@ -579,6 +635,12 @@ int vq_stream_launch(const VqArgs &a, int profile_fp32, cudaStream_t stream) {
     }
     auto pass = [&](auto launch) {
         for (int lo = 0; lo < a.codes; lo += window) {
+            if (a.cancel) {
+                const cudaError_t e = cudaMemcpyAsync(flag_dev, const_cast<const int *>(a.cancel), sizeof(int),
+                                                      cudaMemcpyDefault, stream);
+                if (e != cudaSuccess)
+                    return static_cast<int>(e);
+            }
             p.code_lo = lo;
             p.code_hi = lo + window < a.codes ? lo + window : a.codes;
             if (int e = launch(plan_units(p)))

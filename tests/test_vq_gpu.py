@@ -209,6 +209,22 @@ def test_vq_fp32_large_feature_norms(ob):
     assert np.array_equal(got, want), f"{int((got != want).sum())} rows differ"
 
 
+@pytest.mark.parametrize("x_scale,c_scale", [(1.0, 0.02), (30.0, 0.02), (30.0, 1.0)])
+def test_vq_fp32_rows_much_longer_than_codes(ob, x_scale, c_scale):
+    """|x| from 50 to 1500 times |c| (encoder features against a codebook of
+    small rows): the row norm's error is common to all codes of the row and
+    leaves the window, whose remaining terms must still hold the exact nearest
+    code and every code tied with it."""
+    rng = np.random.default_rng(int(x_scale * 100 + c_scale * 1000))
+    rows, dim, codes = 96, 512, 4099
+    x = (rng.standard_normal((rows, dim)) * x_scale).astype(np.float32)
+    cb = (rng.standard_normal((codes, dim)) * c_scale).astype(np.float32)
+    cb[17] = cb[4000]  # an exact tie across tiles: the smaller id wins
+    got, _ = _gpu_quantize(ob, x, cb, profile=0, ids_u16=False)
+    want = O.quantize(x, cb, bf16=False).astype(np.int64)
+    assert np.array_equal(got, want), f"{int((got != want).sum())} rows differ"
+
+
 def test_vq_fp32_candidate_overflow_scores_every_code(ob):
     """More than kVqCandCap (32) exact ties: the row falls back to scoring every
     code in fp64, and the smallest tied id wins."""
