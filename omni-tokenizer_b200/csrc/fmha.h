@@ -30,6 +30,7 @@ struct FmhaParams {
     int ones_col; // >= 0: V column holding 1.0 so that O[:, ones_col] = row sum of P
     int o_tma;    // 1: the output is staged in shared memory and written by TMA
     int v1_width; // columns of V's second chunk loaded by TMA (0: none)
+    int sorted;   // 1: items of long sequences first, dealt to the CTAs in snake order
     float scale_log2;
     int *err;
 };

@@ -93,13 +93,13 @@ template <int HDP> struct FmhaShape {
     static constexpr uint32_t O_STRIDE = SEP ? 64 : 128; // O_1 - O_0 in columns
     __host__ __device__ static constexpr uint32_t p_col(int i) { return 384 + 64 * i; }
     static constexpr int QBUF = OMNI_FMHA_QBUF; // Q buffers (2: next item prefetch)
-    static constexpr int BUDGET = 226 * 1024 - 8 * 1024;
+    static constexpr int BUDGET = 226 * 1024 - 12 * 1024;
     static constexpr int STAGES_RAW = (BUDGET - QBUF * 2 * TILE_BYTES) / (TILE_BYTES + V_BYTES);
     static constexpr int STAGES = STAGES_RAW > 4 ? 4 : STAGES_RAW;
     static constexpr int KSTEPS = HDP / 16;
-    // Barriers, TMEM handle and (two warps per row) the row-max / row-sum
-    // exchange buffers.
-    static constexpr int BAR_BYTES = 1024 + 8192;
+    // Barriers, TMEM handle, (two warps per row) the row-max / row-sum
+    // exchange buffers and the sorted item table (kSortMaxBatch sequences).
+    static constexpr int BAR_BYTES = 1024 + 8192 + 4096;
     // At least 120 KB so that one CTA (which allocates all 512 TMEM columns)
     // occupies an SM by itself.
     static constexpr int SMEM_RAW =
@@ -108,7 +108,18 @@ template <int HDP> struct FmhaShape {
     static_assert(C1 == 0 || C1 == 16 || C1 == 32 || C1 == 64, "unsupported head dim padding");
     static_assert(HDP % 16 == 0, "head dim padding must be a multiple of 16");
     static_assert(STAGES >= 2, "K/V ring needs two stages");
+    static_assert(SMEM_BYTES <= 227 * 1024, "shared memory of one CTA");
 };
+
+// Sorted item order (variable-length batches without a block window): the
+// sequences ordered by KV tiles, longest first (ties: lower index), their
+// items enumerated in that order (head-major, then query block), and rank r
+// dealt to CTA c in snake order -- round k covers ranks [kG, kG + G) and
+// goes c = 0..G-1 on even k, G-1..0 on odd k -- so every CTA's work is nearly
+// the same (a static round-robin over the batch order left one CTA with about
+// 25 % more work than the mean on a 64-sequence batch of lengths 100..1500).
+// Table in shared memory: seq[rank] = batch index, pre[rank] = items before it.
+constexpr int kSortMaxBatch = 496;
 
 // 12 warps: 0-3 softmax tile 0, 4-7 softmax tile 1 (warp w serves TMEM lane
 // quarter w % 4; each thread owns one query row, all 128 score columns), 8 TMA
@@ -230,13 +241,38 @@ struct Item {
     bool skip;              // nothing to do (rows past the end / padded-query skip)
 };
 
-__device__ __forceinline__ Item decode_item(const FmhaParams &p, int u) {
+__device__ __forceinline__ Item decode_item(const FmhaParams &p, const int *tab, int u) {
     const int qblocks = (p.L + 255) / 256;
     Item it;
-    const int bh = u / qblocks;
-    it.q0 = (u - bh * qblocks) * 256;
-    it.b = bh / p.heads;
-    it.h = bh - it.b * p.heads;
+    if (tab) {
+        // Slot u = round k, position c of the snake deal.
+        const int G = gridDim.x, k = u / G, c = u - k * G;
+        const int r = k * G + ((k & 1) ? G - 1 - c : c);
+        const int *seq = tab, *pre = tab + kSortMaxBatch;
+        if (r >= pre[p.batch]) {
+            it.b = it.h = it.q0 = it.valid = it.T = 0;
+            it.skip = true;
+            return it;
+        }
+        int lo = 0, hi = p.batch - 1; // last rank with pre[rank] <= r
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (pre[mid] <= r)
+                lo = mid;
+            else
+                hi = mid - 1;
+        }
+        const int nq = (pre[lo + 1] - pre[lo]) / p.heads;
+        const int off = r - pre[lo];
+        it.b = seq[lo];
+        it.h = off / nq;
+        it.q0 = (off - it.h * nq) * 256;
+    } else {
+        const int bh = u / qblocks;
+        it.q0 = (u - bh * qblocks) * 256;
+        it.b = bh / p.heads;
+        it.h = bh - it.b * p.heads;
+    }
     int valid = p.lengths ? p.lengths[it.b] : p.valid;
     valid = valid < p.L ? valid : p.L;
     it.valid = valid < 0 ? 0 : valid;
@@ -252,9 +288,9 @@ __device__ __forceinline__ Item decode_item(const FmhaParams &p, int u) {
 // The first item at or after u (in steps of the grid) that has KV work, or
 // `items` when there is none: the items whose Q, K and V are loaded and whose
 // MMAs are issued.
-__device__ __forceinline__ int next_work_item(const FmhaParams &p, int u, int items) {
+__device__ __forceinline__ int next_work_item(const FmhaParams &p, const int *tab, int u, int items) {
     for (; u < items; u += gridDim.x) {
-        const Item it = decode_item(p, u);
+        const Item it = decode_item(p, tab, u);
         if (!it.skip && it.T > 0)
             break;
     }
@@ -263,10 +299,10 @@ __device__ __forceinline__ int next_work_item(const FmhaParams &p, int u, int it
 
 // Loads the two Q tiles of item u into Q slot nq % QBUF once the slot is free.
 template <int HDP>
-__device__ __forceinline__ bool load_q_tiles(const FmhaParams &p, int u, int nq, uint8_t *sQ,
+__device__ __forceinline__ bool load_q_tiles(const FmhaParams &p, const int *tab, int u, int nq, uint8_t *sQ,
                                              uint64_t *q_full, uint64_t *q_empty, int *err) {
     using S = FmhaShape<HDP>;
-    const Item it = decode_item(p, u);
+    const Item it = decode_item(p, tab, u);
     const int qs = nq % S::QBUF;
     if (!__all_sync(0xffffffffu,
                     mbar_wait(&q_empty[qs], ((nq / S::QBUF) & 1) ^ 1, err, kErrWaitEmpty)))
@@ -325,8 +361,43 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
     [[maybe_unused]] float *xsum = xmax + 2 * 2 * 4 * 2 * 32;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int items = p.batch * p.heads * ((p.L + 255) / 256);
     int *err = p.err;
+    // Sorted item table (after the exchange buffers).
+    int *tab = p.sorted ? reinterpret_cast<int *>(xsum + 2 * 2 * 4 * 2 * 32) : nullptr;
+    if (p.sorted) {
+        int *seq = tab, *pre = tab + kSortMaxBatch;
+        const int qblocks = (p.L + 255) / 256;
+        auto kv_tiles = [&](int b) {
+            int v = p.lengths[b];
+            v = v < p.L ? v : p.L;
+            return v < 0 ? 0 : (v + 127) / 128;
+        };
+        for (int b = threadIdx.x; b < p.batch; b += blockDim.x) {
+            const int tb = kv_tiles(b);
+            int r = 0;
+            for (int b2 = 0; b2 < p.batch; ++b2) {
+                const int t2 = kv_tiles(b2);
+                r += (t2 > tb || (t2 == tb && b2 < b)) ? 1 : 0;
+            }
+            seq[r] = b;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            int acc = 0;
+            for (int r = 0; r < p.batch; ++r) {
+                pre[r] = acc;
+                int v = p.lengths[seq[r]];
+                v = v < p.L ? v : p.L;
+                v = v < 0 ? 0 : v;
+                const int nq = p.skip_padded_q ? (v + 255) / 256 : qblocks;
+                acc += p.heads * nq;
+            }
+            pre[p.batch] = acc;
+        }
+        __syncthreads();
+    }
+    const int items = p.sorted ? (tab[kSortMaxBatch + p.batch] + gridDim.x - 1) / gridDim.x * gridDim.x
+                               : p.batch * p.heads * ((p.L + 255) / 256);
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < 2; ++i) {
@@ -401,9 +472,9 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
             // K and V loads issued by this CTA (Q tiles are loaded by warp 10).
             int nk = 0, nv = 0;
             bool ok = true;
-            for (int u = next_work_item(p, blockIdx.x, items); ok && u < items;
-                 u = next_work_item(p, u + gridDim.x, items)) {
-                const Item it = decode_item(p, u);
+            for (int u = next_work_item(p, tab, blockIdx.x, items); ok && u < items;
+                 u = next_work_item(p, tab, u + gridDim.x, items)) {
+                const Item it = decode_item(p, tab, u);
                 for (int j = 0; j < it.T; ++j) {
                     const int st = nk % S::STAGES;
                     const uint32_t ph = (nk / S::STAGES) & 1;
@@ -525,9 +596,9 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                     commit(&k_empty[st]);
                     return true;
                 };
-                for (int u = next_work_item(p, blockIdx.x, items); ok && u < items;) {
-                    const Item it = decode_item(p, u);
-                    const int u_next = next_work_item(p, u + gridDim.x, items);
+                for (int u = next_work_item(p, tab, blockIdx.x, items); ok && u < items;) {
+                    const Item it = decode_item(p, tab, u);
+                    const int u_next = next_work_item(p, tab, u + gridDim.x, items);
                     const int qs = nq % S::QBUF;
                     const uint32_t qbase = sq + qs * 2 * S::TILE_BYTES;
                     if (!first_s_issued) { // S_i(g0) for the item's first KV tile g0 = kv
@@ -584,7 +655,7 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                 int nq = 0, kv = 0, n_items = 0;
                 bool ok = true;
                 for (int u = blockIdx.x; ok && u < items; u += gridDim.x) {
-                    const Item it = decode_item(p, u);
+                    const Item it = decode_item(p, tab, u);
                     if (it.skip || it.T == 0)
                         continue;
                     const int qs = nq % S::QBUF;
@@ -655,19 +726,19 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
             // the K/V producer never waits for a Q slot.
             const int i = warp - (kMmaWarp + 1);
             int n_items = 0, nq = 0;
-            int uq = next_work_item(p, blockIdx.x, items); // next item whose Q is due
+            int uq = next_work_item(p, tab, blockIdx.x, items); // next item whose Q is due
             bool ok = true;
             if (i == 0) {
                 for (int k = 0; ok && k < S::QBUF && uq < items; ++k) {
-                    ok = load_q_tiles<HDP>(p, uq, nq, sQ, q_full, q_empty, err);
+                    ok = load_q_tiles<HDP>(p, tab, uq, nq, sQ, q_full, q_empty, err);
                     ++nq;
-                    uq = next_work_item(p, uq + gridDim.x, items);
+                    uq = next_work_item(p, tab, uq + gridDim.x, items);
                 }
             }
-            for (int u = next_work_item(p, blockIdx.x, items); ok && u < items;
-                 u = next_work_item(p, u + gridDim.x, items)) {
+            for (int u = next_work_item(p, tab, blockIdx.x, items); ok && u < items;
+                 u = next_work_item(p, tab, u + gridDim.x, items)) {
                 if (p.o_tma) {
-                    const Item it = decode_item(p, u);
+                    const Item it = decode_item(p, tab, u);
                     const int qs_out = n_items % S::QBUF;
                     ok = __all_sync(0xffffffffu, mbar_wait(&ebar[i], n_items & 1, err, kErrWaitO));
                     if (!ok)
@@ -689,10 +760,10 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                     __syncwarp();
                 }
                 if (i == 0 && uq < items) {
-                    if (!(ok = load_q_tiles<HDP>(p, uq, nq, sQ, q_full, q_empty, err)))
+                    if (!(ok = load_q_tiles<HDP>(p, tab, uq, nq, sQ, q_full, q_empty, err)))
                         break;
                     ++nq;
-                    uq = next_work_item(p, uq + gridDim.x, items);
+                    uq = next_work_item(p, tab, uq + gridDim.x, items);
                 }
             }
             if (i == 0) {
@@ -728,7 +799,7 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
         [[maybe_unused]] int n_sum = 0;
         bool ok = true;
         for (int u = blockIdx.x; ok && u < items; u += gridDim.x) {
-            const Item it = decode_item(p, u);
+            const Item it = decode_item(p, tab, u);
             if (it.skip)
                 continue;
             const int t = it.q0 + i * 128 + r; // query token
@@ -1222,6 +1293,7 @@ int fmha_launch(const FmhaArgs &a, cudaStream_t stream) {
     const double scale = a.scale > 0 ? a.scale : 1.0 / std::sqrt(static_cast<double>(p.hd));
     p.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
     p.err = a.err;
+    p.sorted = (a.lengths != nullptr && a.block == 0 && a.q.batch > 1 && a.q.batch <= kSortMaxBatch) ? 1 : 0;
     // Persistent grid: one CTA per SM, each looping over (batch, head, 256-row) items.
     static int sms = 0;
     if (!sms) {
