@@ -648,6 +648,51 @@ def run_reference(args, cfg):
     }
 
 
+def e2e_timeline(ctx, e2e_step, in_bytes, out_bytes):
+    """--e2e-timeline: the PCIe rates of this box for the step's byte counts
+    (pinned buffers) and the CUDA activity of one end-to-end call, on stderr."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    def timed(fn, reps=10):
+        fn()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            fn()
+        torch.cuda.synchronize()
+        return (time.perf_counter() - t0) / reps
+
+    hi, di = torch.empty(in_bytes, dtype=torch.uint8).pin_memory(), torch.empty(in_bytes, dtype=torch.uint8,
+                                                                                   device="cuda")
+    ho, do = torch.empty(out_bytes, dtype=torch.uint8).pin_memory(), torch.empty(out_bytes, dtype=torch.uint8,
+                                                                                    device="cuda")
+    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+
+    def both():
+        with torch.cuda.stream(s_in):
+            di.copy_(hi, non_blocking=True)
+        with torch.cuda.stream(s_out):
+            ho.copy_(do, non_blocking=True)
+
+    t_in = timed(lambda: di.copy_(hi, non_blocking=True))
+    t_out = timed(lambda: ho.copy_(do, non_blocking=True))
+    t_both = timed(both)
+    print(f"[e2e-timeline] H2D {in_bytes / 1e6:.1f} MB {t_in * 1e3:.3f} ms ({in_bytes / t_in / 1e9:.1f} GB/s); "
+          f"D2H {out_bytes / 1e6:.1f} MB {t_out * 1e3:.3f} ms ({out_bytes / t_out / 1e9:.1f} GB/s); "
+          f"both concurrently {t_both * 1e3:.3f} ms", file=sys.stderr)
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        e2e_step(ctx)
+        torch.cuda.synchronize()
+    ev = sorted((e for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA),
+                key=lambda e: e.time_range.start)
+    if ev:
+        t0 = ev[0].time_range.start
+        for e in ev:
+            print(f"[e2e-timeline] {e.time_range.start - t0:9.1f} .. {e.time_range.end - t0:9.1f} us  "
+                  f"{e.name[:60]}", file=sys.stderr)
+
+
 def run_ours(args, name, cfg, dist, steps, warmup):
     """One op config (attention or VQ).  Returns the JSON line on rank 0."""
     import torch
@@ -771,6 +816,8 @@ def run_ours(args, name, cfg, dist, steps, warmup):
         for _ in range(e2e_steps):
             e2e_step(ctx)
         e2e_elapsed = time.perf_counter() - t0
+        if args.e2e_timeline and rank == 0:
+            e2e_timeline(ctx, e2e_step, in_bytes, out_bytes)
     barrier()
 
     if dist is not None:
@@ -876,6 +923,8 @@ def main():
     ap.add_argument("--no-sub", action="store_true", help="default run: the headline line only")
     ap.add_argument("--items", type=int, default=None,
                     help="whole-encoder configs: items per step (default: the config's; smaller for profiling)")
+    ap.add_argument("--e2e-timeline", action="store_true",
+                    help="op configs: print the PCIe rates and the CUDA timeline of one end-to-end call (stderr)")
     ap.add_argument("--rows", type=int, default=None,
                     help="VQ configs: rows of x (default: the config's; smaller for profiling)")
     args = ap.parse_args()
