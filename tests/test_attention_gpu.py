@@ -75,6 +75,36 @@ def test_bhld_key_padding_lengths(ob):
         _close(got[b, :, :n], want[b, :, :n], f"segment {b} (valid {n})")
 
 
+@pytest.mark.parametrize("skip", [False, True])
+def test_bhld_ragged_lengths_sorted_order(ob, skip):
+    """Variable lengths (empty, one key, ragged, full) take the longest-first
+    item order across the persistent CTAs: every item is computed exactly once,
+    rows of empty sequences are zeros (when computed), padded query rows are
+    left untouched when skipped."""
+    B, H, L, D = 23, 3, 900, 64
+    q, k, v = _bhld_inputs(B, H, L, D, torch.bfloat16, seed=29)
+    rng = np.random.default_rng(29)
+    lens = rng.integers(1, L + 1, size=B)
+    lens[[0, 5]] = 0
+    lens[[1, 9]] = 1
+    lens[[2, 17]] = L
+    lengths = torch.tensor(lens, dtype=torch.int32)
+    out = torch.full((B, H, L, D), 7.0, dtype=torch.float32, device="cuda")
+    ob.attention_bhld(q.cuda(), k.cuda(), v.cuda(), out=out, lengths=lengths.cuda(), skip_padded_queries=skip)
+    ob.library().sync_check()
+    want = O.attention_bhld(q.float().numpy(), k.float().numpy(), v.float().numpy(), lengths=lens)
+    got = out.cpu().numpy()
+    for b, n in enumerate(lens.tolist()):
+        if n == 0:
+            rows = got[b, :, : (0 if skip else L)]
+            assert np.all(rows == 0.0), f"segment {b}: an empty sequence gives zeros"
+        else:
+            _close(got[b, :, :n], want[b, :, :n], f"segment {b} (valid {n})")
+        if skip:
+            first_untouched = -(-n // 256) * 256  # whole 256-row items past the length are skipped
+            assert np.all(got[b, :, first_untouched:] == 7.0), f"segment {b}: skipped rows written"
+
+
 def test_bhld_block_causal(ob):
     B, H, L, D = 1, 2, 601, 64
     q, k, v = _bhld_inputs(B, H, L, D, torch.bfloat16, seed=11)
