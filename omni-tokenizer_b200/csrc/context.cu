@@ -165,6 +165,15 @@ int omni_b200_attention_bhld_host(omni_b200_context *c, const void *q, const voi
     // on `s_out` (host-to-device and device-to-host copies use separate copy
     // engines), so the call costs about one pass over the inputs at PCIe rate.
     const int chunks = batch < kMaxChunks ? batch : kMaxChunks;
+    // The last chunk is small: after the last input copy only its attention and
+    // output copy remain (the tail of the call).  The other chunks share the
+    // rest evenly.
+    const int last = chunks > 1 ? (batch / (4 * chunks) > 1 ? batch / (4 * chunks) : 1) : batch;
+    auto bound = [&](int ck) { // first item of chunk ck (ck <= chunks)
+        if (ck >= chunks)
+            return batch;
+        return static_cast<int>(static_cast<long long>(batch - last) * ck / (chunks - 1 > 0 ? chunks - 1 : 1));
+    };
     const size_t item_elems = static_cast<size_t>(heads) * L * head_dim;
     const size_t in_es = elem_size(dtype), out_es = elem_size(out_dtype);
     if (lengths)
@@ -175,8 +184,7 @@ int omni_b200_attention_bhld_host(omni_b200_context *c, const void *q, const voi
     const void *src[3] = {q, k, v};
     int rc = 0;
     for (int ck = 0; ck < chunks && !rc; ++ck) {
-        const int b0 = static_cast<int>(static_cast<long long>(batch) * ck / chunks);
-        const int b1 = static_cast<int>(static_cast<long long>(batch) * (ck + 1) / chunks);
+        const int b0 = bound(ck), b1 = bound(ck + 1);
         const size_t off_in = b0 * item_elems * in_es, len_in = (b1 - b0) * item_elems * in_es;
         const size_t off_out = b0 * item_elems * out_es, len_out = (b1 - b0) * item_elems * out_es;
         for (int i = 0; i < 3 && !rc; ++i)
