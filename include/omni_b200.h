@@ -65,8 +65,12 @@ OMNI_B200_API int omni_b200_attention_bhld(const void *q, const void *k, const v
  *   fused:   q is [n, 3*heads*head_dim] holding Q|K|V column blocks, k = v = NULL.
  * out is [n, heads*head_dim] of out_dtype.  dtype F32 inputs (the audio fp32
  * profile) and layouts that TMA cannot address directly are repacked into
- * `workspace` first; omni_b200_attention_rows_workspace() gives the bytes
- * needed (0 when no repacking is needed). */
+ * `workspace` first.  With 16-bit operands and fewer (query block, head)
+ * items than fill the last round of SMs, the kernel also splits
+ * that round's items along the keys and merges the parts in a second pass,
+ * using scratch after the repacked operands.  omni_b200_attention_rows_workspace()
+ * gives the bytes for both (0 when neither is needed); a smaller workspace,
+ * or none, runs without the split and with the same results up to rounding. */
 OMNI_B200_API size_t omni_b200_attention_rows_workspace(size_t n, int heads, int head_dim,
                                                         int dtype, int fused);
 OMNI_B200_API int omni_b200_attention_rows(const void *q, const void *k, const void *v, void *out,
@@ -74,6 +78,20 @@ OMNI_B200_API int omni_b200_attention_rows(const void *q, const void *k, const v
                                            size_t valid, int fused, int dtype, int out_dtype,
                                            void *workspace, size_t workspace_bytes,
                                            void *stream);
+
+/* `batch` sequences of n tokens stacked as batch*n rows (the layout above per
+ * sequence), the keys of sequence b limited to lengths[b] (device int32; NULL:
+ * `valid` for every sequence) and to the block window: what the encoder graphs
+ * run for a batch of audio segments or images.  Workspace as above, from
+ * omni_b200_attention_rows_batch_workspace(). */
+OMNI_B200_API size_t omni_b200_attention_rows_batch_workspace(size_t n, int batch, int heads,
+                                                              int head_dim, int dtype, int fused);
+OMNI_B200_API int omni_b200_attention_rows_batch(const void *q, const void *k, const void *v,
+                                                 void *out, size_t n, int batch, int heads,
+                                                 int head_dim, size_t block, size_t valid,
+                                                 const int32_t *lengths, int fused, int dtype,
+                                                 int out_dtype, void *workspace,
+                                                 size_t workspace_bytes, void *stream);
 
 /* Ops::squares (omni-tokenizer src/internal.h:86, semantics of
  * src/cpu.cpp:216-226): out[r] = sum over columns in order of x[r,j]^2, with

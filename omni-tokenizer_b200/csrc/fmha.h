@@ -31,6 +31,16 @@ struct FmhaParams {
     int o_tma;    // 1: the output is staged in shared memory and written by TMA
     int v1_width; // columns of V's second chunk loaded by TMA (0: none)
     int sorted;   // 1: items of long sequences first, dealt to the CTAs in snake order
+    // Split keys: the `split_tail` items of the last, partial
+    // round are cut into `split_s` ranges of KV tiles, one CTA each; part v of
+    // slot split_first + v writes its unnormalised O rows, row max and row sum
+    // to split_o / split_m / split_l and fmha_split_combine merges them.
+    int split_s;     // parts per split item (0 or 1: no split)
+    int split_first; // first split slot (full rounds x grid)
+    int split_tail;  // items that are split
+    int split_items; // slots: split_first + split_tail * split_s
+    int4 *split_hdr; // [split_tail] (batch, head, first query row, skip)
+    float *split_m, *split_l, *split_o; // [part][256], [part][256], [part][256][HDP]
     float scale_log2;
     int *err;
 };
@@ -71,11 +81,22 @@ struct FmhaArgs {
     double scale = 0; // 0: out_d^-1/2
     int out_d = 0;    // output columns per head (0: q.d); the operands may be zero-padded wider
     int *err = nullptr;
+    // Scratch for the key split of a partial last round (fmha_split_workspace
+    // bytes, 256-byte aligned), or nullptr: no split.
+    void *split_ws = nullptr;
+    size_t split_ws_bytes = 0;
 };
 
 // Returns 0 on success, a CUDA error code, or a negative/1000+ code for an
 // unsupported shape / tensor-map failure.
 int fmha_launch(const FmhaArgs &args, cudaStream_t stream);
+
+// Bytes of split scratch that fmha_launch uses for `batch` sequences of L
+// tokens (keys limited to at most `valid`), `heads` heads of head_dim (16-bit
+// operands), or 0 when it would not split (padded-query skip, or a last round
+// that is full or too short to gain).
+size_t fmha_split_workspace(int batch, int heads, int L, int head_dim, int valid, int block,
+                            int skip_padded_q);
 
 // Attention on row-major [batch*n, heads*hd] (fused: [batch*n, 3*heads*hd])
 // rows: `batch` sequences of n tokens, keys of sequence b limited to
@@ -85,7 +106,10 @@ size_t attention_rows_workspace(size_t rows, int heads, int head_dim, int dtype,
 int attention_rows(const void *q, const void *k, const void *v, void *out, size_t n, int batch,
                    int heads, int head_dim, size_t block, size_t valid, const int *lengths,
                    int fused, int dtype, int out_dtype, void *workspace, size_t workspace_bytes,
-                   cudaStream_t stream);
+                   cudaStream_t stream, void *split_ws = nullptr, size_t split_ws_bytes = 0);
+// Split scratch for attention_rows on 16-bit rows (0 for fp32 or no split).
+size_t attention_rows_split_workspace(size_t n, int batch, int heads, int head_dim, size_t block,
+                                      size_t valid, int dtype);
 bool tma_view_ok(const void *base, const TensorView &v);
 int padded_head_dim(int hd);
 

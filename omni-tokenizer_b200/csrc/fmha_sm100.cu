@@ -120,6 +120,11 @@ template <int HDP> struct FmhaShape {
 // 25 % more work than the mean on a 64-sequence batch of lengths 100..1500).
 // Table in shared memory: seq[rank] = batch index, pre[rank] = items before it.
 constexpr int kSortMaxBatch = 496;
+// After the table (seq[496], pre[497]): this CTA's split part.  A CTA's slots
+// are u = blockIdx.x + k * grid, so its only split slot is v = blockIdx.x,
+// decoded once in the prologue: (b, h, q0, valid), (T, kb, skip, 0).
+constexpr int kSplitSlot = 1000; // 16-byte aligned (int4 reads)
+constexpr int kSplitMaxParts = 8;
 
 // 12 warps: 0-3 softmax tile 0, 4-7 softmax tile 1 (warp w serves TMEM lane
 // quarter w % 4; each thread owns one query row, all 128 score columns), 8 TMA
@@ -235,19 +240,23 @@ __device__ __forceinline__ void wait_drain(uint64_t *bar, uint32_t parity, int *
     }
 }
 
-// One work item = 256 query rows of one (batch, head).
+// One work item = 256 query rows of one (batch, head), or (split keys) one
+// part of such an item: KV tiles [kb, kb + T) of the item's T_item tiles.
 struct Item {
-    int b, h, q0, valid, T; // T = KV tiles the item needs (0: write zeros)
+    int b, h, q0, valid, T; // T = KV tiles the item (part) needs (0: write zeros)
+    int kb;                 // first KV tile
+    int part;               // split part slot v (>= 0), or -1: a whole item
     bool skip;              // nothing to do (rows past the end / padded-query skip)
 };
 
-__device__ __forceinline__ Item decode_item(const FmhaParams &p, const int *tab, int u) {
+// Item of rank r (sorted order or batch order), all its KV tiles.
+// `tab` is null unless the launch uses the sorted order or split slots.
+template <bool SPLIT> __device__ __forceinline__ Item decode_rank(const FmhaParams &p, const int *tab, int r) {
     const int qblocks = (p.L + 255) / 256;
     Item it;
-    if (tab) {
-        // Slot u = round k, position c of the snake deal.
-        const int G = gridDim.x, k = u / G, c = u - k * G;
-        const int r = k * G + ((k & 1) ? G - 1 - c : c);
+    it.kb = 0;
+    it.part = -1;
+    if (SPLIT ? p.sorted != 0 : tab != nullptr) {
         const int *seq = tab, *pre = tab + kSortMaxBatch;
         if (r >= pre[p.batch]) {
             it.b = it.h = it.q0 = it.valid = it.T = 0;
@@ -268,8 +277,8 @@ __device__ __forceinline__ Item decode_item(const FmhaParams &p, const int *tab,
         it.h = off / nq;
         it.q0 = (off - it.h * nq) * 256;
     } else {
-        const int bh = u / qblocks;
-        it.q0 = (u - bh * qblocks) * 256;
+        const int bh = r / qblocks;
+        it.q0 = (r - bh * qblocks) * 256;
         it.b = bh / p.heads;
         it.h = bh - it.b * p.heads;
     }
@@ -285,12 +294,41 @@ __device__ __forceinline__ Item decode_item(const FmhaParams &p, const int *tab,
     return it;
 }
 
+// Slot u of this CTA.  Whole items: round k = u / grid, position c; sorted
+// order deals rank k*G + c (even k) or k*G + G-1-c (odd k).  Split slots
+// (u >= split_first): the CTA's one part, decoded in the prologue into
+// tab[kSplitSlot..] as (b, h, q0, valid, T, kb, skip).
+template <bool SPLIT> __device__ __forceinline__ Item decode_item(const FmhaParams &p, const int *tab, int u) {
+    if (SPLIT && u >= p.split_first) {
+        Item it;
+        const int v = u - p.split_first;
+        const int4 a = *reinterpret_cast<const int4 *>(tab + kSplitSlot);
+        const int4 b = *reinterpret_cast<const int4 *>(tab + kSplitSlot + 4);
+        it.b = a.x;
+        it.h = a.y;
+        it.q0 = a.z;
+        it.valid = a.w;
+        it.T = b.x;
+        it.kb = b.y;
+        it.skip = v >= p.split_tail * p.split_s || b.z != 0;
+        it.part = v;
+        return it;
+    }
+    int r = u;
+    if (SPLIT ? p.sorted != 0 : tab != nullptr) {
+        const int G = gridDim.x, k = u / G, c = u - k * G;
+        r = k * G + ((k & 1) ? G - 1 - c : c);
+    }
+    return decode_rank<SPLIT>(p, tab, r);
+}
+
 // The first item at or after u (in steps of the grid) that has KV work, or
 // `items` when there is none: the items whose Q, K and V are loaded and whose
 // MMAs are issued.
+template <bool SPLIT>
 __device__ __forceinline__ int next_work_item(const FmhaParams &p, const int *tab, int u, int items) {
     for (; u < items; u += gridDim.x) {
-        const Item it = decode_item(p, tab, u);
+        const Item it = decode_item<SPLIT>(p, tab, u);
         if (!it.skip && it.T > 0)
             break;
     }
@@ -298,11 +336,11 @@ __device__ __forceinline__ int next_work_item(const FmhaParams &p, const int *ta
 }
 
 // Loads the two Q tiles of item u into Q slot nq % QBUF once the slot is free.
-template <int HDP>
+template <int HDP, bool SPLIT>
 __device__ __forceinline__ bool load_q_tiles(const FmhaParams &p, const int *tab, int u, int nq, uint8_t *sQ,
                                              uint64_t *q_full, uint64_t *q_empty, int *err) {
     using S = FmhaShape<HDP>;
-    const Item it = decode_item(p, tab, u);
+    const Item it = decode_item<SPLIT>(p, tab, u);
     const int qs = nq % S::QBUF;
     if (!__all_sync(0xffffffffu,
                     mbar_wait(&q_empty[qs], ((nq / S::QBUF) & 1) ^ 1, err, kErrWaitEmpty)))
@@ -329,7 +367,9 @@ __device__ __forceinline__ void warp_arrive(uint64_t *bar) {
         mbar_arrive(bar);
 }
 
-template <int HDP, bool BF16>
+// SPLIT: the launch has split slots (p.split_s > 1); a separate instance so
+// that launches without them run code that has no split branch.
+template <int HDP, bool BF16, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_constant__ FmhaParams p) {
     using S = FmhaShape<HDP>;
     extern __shared__ uint8_t smem_raw[];
@@ -362,8 +402,9 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int *err = p.err;
-    // Sorted item table (after the exchange buffers).
-    int *tab = p.sorted ? reinterpret_cast<int *>(xsum + 2 * 2 * 4 * 2 * 32) : nullptr;
+    // Sorted item table and split slot (after the exchange buffers).
+    int *tab = (SPLIT || p.sorted) ? reinterpret_cast<int *>(xsum + 2 * 2 * 4 * 2 * 32) : nullptr;
+    static_assert(2 * 2 * 4 * 2 * 32 * 8 + (kSplitSlot + 8) * 4 <= 8192 + 4096, "item table space");
     if (p.sorted) {
         int *seq = tab, *pre = tab + kSortMaxBatch;
         const int qblocks = (p.L + 255) / 256;
@@ -396,10 +437,20 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
         }
         __syncthreads();
     }
-    const int items = p.sorted ? (tab[kSortMaxBatch + p.batch] + gridDim.x - 1) / gridDim.x * gridDim.x
-                               : p.batch * p.heads * ((p.L + 255) / 256);
+    const int items = SPLIT ? p.split_items
+                      : p.sorted    ? (tab[kSortMaxBatch + p.batch] + gridDim.x - 1) / gridDim.x * gridDim.x
+                                    : p.batch * p.heads * ((p.L + 255) / 256);
 
     if (threadIdx.x == 0) {
+        if (SPLIT) {
+            // Part q of the tail item of rank split_first + w (v = q * tail + w):
+            // KV tiles [q T / s, (q + 1) T / s) of the item's T.
+            const int v = blockIdx.x, q = v / p.split_tail, w = v - q * p.split_tail;
+            Item it = decode_rank<true>(p, tab, p.split_first + w);
+            const int kb = q * it.T / p.split_s, ke = (q + 1) * it.T / p.split_s;
+            *reinterpret_cast<int4 *>(tab + kSplitSlot) = make_int4(it.b, it.h, it.q0, it.valid);
+            *reinterpret_cast<int4 *>(tab + kSplitSlot + 4) = make_int4(ke - kb, kb, it.skip ? 1 : 0, 0);
+        }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&q_full[i], 1);
             // Released by the MMA warp, or (TMA output) by the two tiles'
@@ -472,9 +523,9 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
             // K and V loads issued by this CTA (Q tiles are loaded by warp 10).
             int nk = 0, nv = 0;
             bool ok = true;
-            for (int u = next_work_item(p, tab, blockIdx.x, items); ok && u < items;
-                 u = next_work_item(p, tab, u + gridDim.x, items)) {
-                const Item it = decode_item(p, tab, u);
+            for (int u = next_work_item<SPLIT>(p, tab, blockIdx.x, items); ok && u < items;
+                 u = next_work_item<SPLIT>(p, tab, u + gridDim.x, items)) {
+                const Item it = decode_item<SPLIT>(p, tab, u);
                 for (int j = 0; j < it.T; ++j) {
                     const int st = nk % S::STAGES;
                     const uint32_t ph = (nk / S::STAGES) & 1;
@@ -484,7 +535,7 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                     if (elect_one()) {
                         mbar_arrive_expect_tx(&k_full[st], S::TILE_BYTES);
                         load_tile<HDP>(sK + st * S::TILE_BYTES, &p.tk0, &p.tk1, &k_full[st],
-                                       j * 128, it.h, it.b);
+                                       ((SPLIT ? it.kb : 0) + j) * 128, it.h, it.b);
                     }
                     __syncwarp();
                     ++nk;
@@ -494,10 +545,10 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                     if (elect_one()) {
                         mbar_arrive_expect_tx(&v_full[st], 128 * 2 * (S::C0 + p.v1_width));
                         uint8_t *vdst = sV + st * S::V_BYTES;
-                        tma_load_4d(vdst, &p.tv0, &v_full[st], 0, j * 128, it.h, it.b);
+                        const int row = ((SPLIT ? it.kb : 0) + j) * 128;
+                        tma_load_4d(vdst, &p.tv0, &v_full[st], 0, row, it.h, it.b);
                         if (S::HDPO > 64 && p.v1_width > 0)
-                            tma_load_4d(vdst + S::V_CH0, &p.tv1, &v_full[st], 64, j * 128, it.h,
-                                        it.b);
+                            tma_load_4d(vdst + S::V_CH0, &p.tv1, &v_full[st], 64, row, it.h, it.b);
                     }
                     __syncwarp();
                     ++nv;
@@ -596,9 +647,9 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                     commit(&k_empty[st]);
                     return true;
                 };
-                for (int u = next_work_item(p, tab, blockIdx.x, items); ok && u < items;) {
-                    const Item it = decode_item(p, tab, u);
-                    const int u_next = next_work_item(p, tab, u + gridDim.x, items);
+                for (int u = next_work_item<SPLIT>(p, tab, blockIdx.x, items); ok && u < items;) {
+                    const Item it = decode_item<SPLIT>(p, tab, u);
+                    const int u_next = next_work_item<SPLIT>(p, tab, u + gridDim.x, items);
                     const int qs = nq % S::QBUF;
                     const uint32_t qbase = sq + qs * 2 * S::TILE_BYTES;
                     if (!first_s_issued) { // S_i(g0) for the item's first KV tile g0 = kv
@@ -655,7 +706,7 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                 int nq = 0, kv = 0, n_items = 0;
                 bool ok = true;
                 for (int u = blockIdx.x; ok && u < items; u += gridDim.x) {
-                    const Item it = decode_item(p, tab, u);
+                    const Item it = decode_item<SPLIT>(p, tab, u);
                     if (it.skip || it.T == 0)
                         continue;
                     const int qs = nq % S::QBUF;
@@ -726,19 +777,19 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
             // the K/V producer never waits for a Q slot.
             const int i = warp - (kMmaWarp + 1);
             int n_items = 0, nq = 0;
-            int uq = next_work_item(p, tab, blockIdx.x, items); // next item whose Q is due
+            int uq = next_work_item<SPLIT>(p, tab, blockIdx.x, items); // next item whose Q is due
             bool ok = true;
             if (i == 0) {
                 for (int k = 0; ok && k < S::QBUF && uq < items; ++k) {
-                    ok = load_q_tiles<HDP>(p, tab, uq, nq, sQ, q_full, q_empty, err);
+                    ok = load_q_tiles<HDP, SPLIT>(p, tab, uq, nq, sQ, q_full, q_empty, err);
                     ++nq;
-                    uq = next_work_item(p, tab, uq + gridDim.x, items);
+                    uq = next_work_item<SPLIT>(p, tab, uq + gridDim.x, items);
                 }
             }
-            for (int u = next_work_item(p, tab, blockIdx.x, items); ok && u < items;
-                 u = next_work_item(p, tab, u + gridDim.x, items)) {
+            for (int u = next_work_item<SPLIT>(p, tab, blockIdx.x, items); ok && u < items;
+                 u = next_work_item<SPLIT>(p, tab, u + gridDim.x, items)) {
                 if (p.o_tma) {
-                    const Item it = decode_item(p, tab, u);
+                    const Item it = decode_item<SPLIT>(p, tab, u);
                     const int qs_out = n_items % S::QBUF;
                     ok = __all_sync(0xffffffffu, mbar_wait(&ebar[i], n_items & 1, err, kErrWaitO));
                     if (!ok)
@@ -747,7 +798,9 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                     if (elect_one()) {
                         uint8_t *stile = sQ + (qs_out * 2 + i) * S::TILE_BYTES;
                         const int row0 = it.q0 + i * 128;
-                        if (row0 < p.L) { // a tile wholly past the end stores nothing
+                        // A tile wholly past the end stores nothing; a split
+                        // part wrote its partial rows to the scratch instead.
+                        if (row0 < p.L && (!SPLIT || it.part < 0)) {
                             tma_store_4d(&p.to0, stile, 0, row0, it.h, it.b);
                             if constexpr (S::C1 > 0)
                                 tma_store_4d(&p.to1, stile + S::CH0_BYTES, S::C0, row0, it.h,
@@ -760,10 +813,10 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                     __syncwarp();
                 }
                 if (i == 0 && uq < items) {
-                    if (!(ok = load_q_tiles<HDP>(p, tab, uq, nq, sQ, q_full, q_empty, err)))
+                    if (!(ok = load_q_tiles<HDP, SPLIT>(p, tab, uq, nq, sQ, q_full, q_empty, err)))
                         break;
                     ++nq;
-                    uq = next_work_item(p, tab, uq + gridDim.x, items);
+                    uq = next_work_item<SPLIT>(p, tab, uq + gridDim.x, items);
                 }
             }
             if (i == 0) {
@@ -799,7 +852,9 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
         [[maybe_unused]] int n_sum = 0;
         bool ok = true;
         for (int u = blockIdx.x; ok && u < items; u += gridDim.x) {
-            const Item it = decode_item(p, tab, u);
+            const Item it = decode_item<SPLIT>(p, tab, u);
+            if (SPLIT && it.part >= 0 && it.part < p.split_tail && threadIdx.x == 0)
+                p.split_hdr[it.part] = make_int4(it.b, it.h, it.q0, it.skip ? 1 : 0); // part 0 of item w
             if (it.skip)
                 continue;
             const int t = it.q0 + i * 128 + r; // query token
@@ -823,7 +878,7 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                     warp_arrive(&s_free[i]);
                 }
                 float *s = reinterpret_cast<float *>(sraw);
-                const int kv0 = j * 128 + hh * kCols;
+                const int kv0 = ((SPLIT ? it.kb : 0) + j) * 128 + hh * kCols;
                 const bool masked = kv0 + kCols > limit;
                 if (masked) {
 #pragma unroll
@@ -869,7 +924,12 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                     l *= alpha;
                     m = mnew;
                 }
-                const float neg_m = -m;
+                float neg_m = -m;
+                if constexpr (SPLIT) {
+                    // A part past a row's block window: every score of the row
+                    // is masked so far (m = -inf) and P must be 0, not 2^NaN.
+                    neg_m = m == -INFINITY ? 0.f : neg_m;
+                }
                 if (OMNI_FMHA_TURN && (i == 1 || g > 0)) {
                     // The tiles take turns for the exp phase: tile 0 runs
                     // iteration g after tile 1 finished g-1, tile 1 after tile 0
@@ -1066,6 +1126,29 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                     l += xs[(hh ^ 1) * 32 + lane];
                 }
             }
+            if constexpr (SPLIT && !kSplit) {
+                if (it.part >= 0) {
+                    // Split part: the unnormalised O row (all HDP columns), the
+                    // row's max (log2 units: P = 2^(s * scale_log2 - m)) and its
+                    // sum of P; fmha_split_combine merges the parts.  An empty
+                    // part (T = 0) writes m = -inf, l = 0, O = 0.
+                    const int prow = it.part * 256 + i * 128 + r;
+                    float4 *po = reinterpret_cast<float4 *>(p.split_o + static_cast<size_t>(prow) * HDP);
+#pragma unroll
+                    for (int cq = 0; cq < kEch; ++cq)
+#pragma unroll
+                        for (int e = 0; e < 16; e += 4)
+                            po[cq * 4 + e / 4] =
+                                make_float4(__uint_as_float(ob[cq][e]), __uint_as_float(ob[cq][e + 1]),
+                                            __uint_as_float(ob[cq][e + 2]), __uint_as_float(ob[cq][e + 3]));
+                    p.split_m[prow] = m;
+                    p.split_l[prow] = l;
+                    if (p.o_tma && it.T > 0)
+                        warp_arrive(&ebar[i]); // the store warp releases the Q slot
+                    __syncwarp();
+                    continue;
+                }
+            }
             const float inv = (it.T > 0 && l > 0.f) ? 1.f / l : 0.f;
             if (p.o_tma && it.T > 0) {
                 // Stage the row of O in the item's Q slot (the same swizzled
@@ -1171,6 +1254,101 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
         tmem_dealloc(tmem, 512);
 }
 
+// Merges the parts of the split items: for row t of tail item w with parts
+// q = 0..s-1 (slot v = q * tail + w), M = max m_q, a_q = 2^(m_q - M),
+// O = (sum a_q O_q) / (sum a_q l_q).  Thread = (row, 8-column group) of one
+// item (blockIdx.y = w); every load (the error word, the item header, each
+// part's m, l and 8 columns of O) is issued before any is used, so the pass
+// costs one round trip to L2, where the parts were just written.
+struct FmhaCombineParams {
+    const int4 *hdr;
+    const float *m, *l, *o;
+    void *out;
+    long long o_sb, o_sh, o_st;
+    int L, hd, hdp, tail, s, out_dtype, out_vec;
+    const int *err;
+};
+
+__global__ void __launch_bounds__(256) fmha_split_combine(const __grid_constant__ FmhaCombineParams c) {
+    const int w = blockIdx.y, ng = c.hdp / 8;
+    const int unit = blockIdx.x * blockDim.x + threadIdx.x;
+    if (unit >= 256 * ng)
+        return;
+    const int row = unit / ng, c0 = (unit - row * ng) * 8;
+    const int e = *c.err;
+    const int4 hd4 = c.hdr[w]; // batch, head, first query row, skip
+    float mq[kSplitMaxParts], lq[kSplitMaxParts];
+    float4 oq[kSplitMaxParts][2];
+#pragma unroll
+    for (int q = 0; q < kSplitMaxParts; ++q) {
+        if (q < c.s) {
+            const int pr = (q * c.tail + w) * 256 + row;
+            mq[q] = c.m[pr];
+            lq[q] = c.l[pr];
+            const float4 *po = reinterpret_cast<const float4 *>(c.o + static_cast<size_t>(pr) * c.hdp + c0);
+            oq[q][0] = po[0];
+            oq[q][1] = po[1];
+        }
+    }
+    const int t = hd4.z + row;
+    // The attention kernel gave up (its parts may be incomplete), a skipped
+    // item, rows past the end or columns past the head: nothing to write.
+    if (e != 0 || hd4.w || t >= c.L || c0 >= c.hd)
+        return;
+    float mmax = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < kSplitMaxParts; ++q)
+        if (q < c.s)
+            mmax = fmaxf(mmax, mq[q]);
+    float acc[8], l = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+        acc[k] = 0.f;
+    if (mmax != -INFINITY) {
+#pragma unroll
+        for (int q = 0; q < kSplitMaxParts; ++q) {
+            if (q < c.s) {
+                const float a = exp2f(mq[q] - mmax);
+                l = fmaf(a, lq[q], l);
+                acc[0] = fmaf(a, oq[q][0].x, acc[0]);
+                acc[1] = fmaf(a, oq[q][0].y, acc[1]);
+                acc[2] = fmaf(a, oq[q][0].z, acc[2]);
+                acc[3] = fmaf(a, oq[q][0].w, acc[3]);
+                acc[4] = fmaf(a, oq[q][1].x, acc[4]);
+                acc[5] = fmaf(a, oq[q][1].y, acc[5]);
+                acc[6] = fmaf(a, oq[q][1].z, acc[6]);
+                acc[7] = fmaf(a, oq[q][1].w, acc[7]);
+            }
+        }
+    }
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+    const long long base = hd4.x * c.o_sb + hd4.y * c.o_sh + static_cast<long long>(t) * c.o_st + c0;
+    const bool whole = c.out_vec && c0 + 8 <= c.hd;
+    if (c.out_dtype == kOutF32) {
+        float *out = static_cast<float *>(c.out) + base;
+        if (whole) {
+            reinterpret_cast<float4 *>(out)[0] = make_float4(acc[0] * inv, acc[1] * inv, acc[2] * inv, acc[3] * inv);
+            reinterpret_cast<float4 *>(out)[1] = make_float4(acc[4] * inv, acc[5] * inv, acc[6] * inv, acc[7] * inv);
+        } else {
+            for (int k = 0; k < 8 && c0 + k < c.hd; ++k)
+                out[k] = acc[k] * inv;
+        }
+        return;
+    }
+    const bool bf = c.out_dtype == kOutBF16;
+    uint16_t *out = static_cast<uint16_t *>(c.out) + base;
+    uint32_t wv[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+        wv[k] = pack2(acc[2 * k] * inv, acc[2 * k + 1] * inv, bf);
+    if (whole) {
+        *reinterpret_cast<uint4 *>(out) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+    } else {
+        for (int k = 0; k < 8 && c0 + k < c.hd; ++k)
+            out[k] = static_cast<uint16_t>(k & 1 ? wv[k >> 1] >> 16 : wv[k >> 1] & 0xffffu);
+    }
+}
+
 // ------------------------------------------------------------------ host side
 // Builds a 4-D (d, token, head, batch) tiled map with a box of
 // box_w x box_rows x 1 x 1 elements.
@@ -1208,20 +1386,90 @@ int padded_head_dim(int hd) {
     return -1;
 }
 
-template <int HDP, bool BF16> int launch_typed(FmhaParams &p, int grid, cudaStream_t stream) {
+template <int HDP, bool BF16, bool SPLIT> int launch_typed(FmhaParams &p, int grid, cudaStream_t stream) {
     using S = FmhaShape<HDP>;
     static std::atomic<unsigned long long> done{0};
-    const cudaError_t attr =
-        set_smem_limit(reinterpret_cast<const void *>(fmha_fwd_kernel<HDP, BF16>), S::SMEM_BYTES, done);
+    const cudaError_t attr = set_smem_limit(reinterpret_cast<const void *>(fmha_fwd_kernel<HDP, BF16, SPLIT>),
+                                            S::SMEM_BYTES, done);
     if (attr != cudaSuccess)
         return static_cast<int>(attr);
-    fmha_fwd_kernel<HDP, BF16><<<grid, kThreads, S::SMEM_BYTES, stream>>>(p);
+    fmha_fwd_kernel<HDP, BF16, SPLIT><<<grid, kThreads, S::SMEM_BYTES, stream>>>(p);
     return static_cast<int>(cudaGetLastError());
 }
 
+// Split slots exist only with bf16 operands (the encoder graphs, which pass
+// split scratch); fmha_launch plans a split for bf16 launches only.
 template <int HDP> int launch_hdp(FmhaParams &p, bool bf16, int grid, cudaStream_t stream) {
-    return bf16 ? launch_typed<HDP, true>(p, grid, stream)
-                : launch_typed<HDP, false>(p, grid, stream);
+    if (p.split_s > 1)
+        return bf16 ? launch_typed<HDP, true, true>(p, grid, stream) : -2;
+    return bf16 ? launch_typed<HDP, true, false>(p, grid, stream)
+                : launch_typed<HDP, false, false>(p, grid, stream);
+}
+
+int fmha_sm_count() {
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0, n = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+            n = 148;
+        sms = n;
+    }
+    return sms;
+}
+
+// Key split of the last round.  N items of up to t_max KV tiles on G CTAs:
+// `full` (0 or 1) whole rounds, then `tail` items.  Each tail item is cut into
+// s = min(G / tail, t_max, 8) parts; the split pays when the parts save at
+// least kSplitMinTiles KV tiles of the last round: a part costs an item
+// transition, and the combine pass (about 4 us on B200) reads its rows once
+// more, against about 1.3 us per KV tile of 256 x 128 scores saved.  With a
+// block window, a part wholly past a row's window leaves that row's max at
+// -inf and its sum at 0, which the combine weights by 0.
+constexpr int kSplitMinTiles = 6;
+constexpr int kSplitHdrBytes = 16384; // int4 per split item: up to 1024 items
+
+struct SplitPlan {
+    int s = 1, first = 0, tail = 0, items = 0;
+};
+
+SplitPlan split_plan(long long n_items, int t_max, int skip_padded_q) {
+    SplitPlan pl;
+    const int G = fmha_sm_count();
+    if (kSplit || skip_padded_q || n_items <= 0 || t_max <= 1 || G > 1024)
+        return pl;
+    const long long full = n_items / G, tail = n_items - full * G;
+    // After more than one whole round the CTAs' finishing times already
+    // spread by about what a split of the last round would save.
+    if (tail == 0 || full > 1)
+        return pl;
+    int s = static_cast<int>(G / tail);
+    s = s < t_max ? s : t_max;
+    s = s < kSplitMaxParts ? s : kSplitMaxParts;
+    if (s < 2 || t_max - (t_max + s - 1) / s < kSplitMinTiles)
+        return pl;
+    pl.s = s;
+    pl.first = static_cast<int>(full * G);
+    pl.tail = static_cast<int>(tail);
+    pl.items = pl.first + pl.tail * s;
+    return pl;
+}
+
+size_t split_bytes(int hdp) {
+    const size_t G = static_cast<size_t>(fmha_sm_count());
+    return kSplitHdrBytes + G * 256 * 4 * 2 + G * 256 * static_cast<size_t>(hdp) * 4;
+}
+
+size_t fmha_split_workspace(int batch, int heads, int L, int head_dim, int valid, int block,
+                            int skip_padded_q) {
+    const int hdp = padded_head_dim(head_dim);
+    if (hdp < 0 || batch <= 0 || heads <= 0 || L <= 0)
+        return 0;
+    const int v = valid > 0 && valid < L ? valid : L;
+    const long long n = static_cast<long long>(batch) * heads * ((L + 255) / 256);
+    (void)block; // rows of a part past their block window come out as empty parts
+    const SplitPlan pl = split_plan(n, (v + 127) / 128, skip_padded_q);
+    return pl.s > 1 ? split_bytes(hdp) : 0;
 }
 
 int fmha_launch(const FmhaArgs &a, cudaStream_t stream) {
@@ -1282,7 +1530,9 @@ int fmha_launch(const FmhaArgs &a, cudaStream_t stream) {
     p.L = a.q.tokens;
     p.hd = a.out_d > 0 ? a.out_d : a.q.d;
     p.valid = a.valid;
-    p.block = a.block;
+    // A window at least as long as the sequence limits nothing: no window
+    // (which allows the sorted item order and the key split).
+    p.block = a.block >= a.q.tokens ? 0 : a.block;
     p.skip_padded_q = a.skip_padded_q;
     p.out_dtype = a.out_dtype;
     const int esize = a.out_dtype == kOutF32 ? 4 : 2;
@@ -1293,32 +1543,74 @@ int fmha_launch(const FmhaArgs &a, cudaStream_t stream) {
     const double scale = a.scale > 0 ? a.scale : 1.0 / std::sqrt(static_cast<double>(p.hd));
     p.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
     p.err = a.err;
-    p.sorted = (a.lengths != nullptr && a.block == 0 && a.q.batch > 1 && a.q.batch <= kSortMaxBatch) ? 1 : 0;
+    p.sorted = (a.lengths != nullptr && p.block == 0 && a.q.batch > 1 && a.q.batch <= kSortMaxBatch) ? 1 : 0;
     // Persistent grid: one CTA per SM, each looping over (batch, head, 256-row) items.
-    static int sms = 0;
-    if (!sms) {
-        int dev = 0;
-        if (cudaGetDevice(&dev) != cudaSuccess ||
-            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-            sms = 148;
-    }
+    const int sms = fmha_sm_count();
     const long long items = static_cast<long long>(p.batch) * p.heads * ((p.L + 255) / 256);
-    const int grid_x = static_cast<int>(items < sms ? items : sms);
+    int grid_x = static_cast<int>(items < sms ? items : sms);
+    // Key split of a partial last round (the whole batch when it has fewer
+    // items than SMs); the lengths bound each item's tiles by L.
+    if (a.split_ws && a.bf16) {
+        const int v = a.lengths ? p.L : (p.valid > 0 && p.valid < p.L ? p.valid : p.L);
+        const SplitPlan pl = split_plan(items, (v + 127) / 128, p.skip_padded_q);
+        if (pl.s > 1 && a.split_ws_bytes >= split_bytes(hdp) &&
+            reinterpret_cast<uintptr_t>(a.split_ws) % 256 == 0) {
+            const size_t G = static_cast<size_t>(sms);
+            char *w = static_cast<char *>(a.split_ws);
+            p.split_s = pl.s;
+            p.split_first = pl.first;
+            p.split_tail = pl.tail;
+            p.split_items = pl.items;
+            p.split_hdr = reinterpret_cast<int4 *>(w);
+            p.split_m = reinterpret_cast<float *>(w + kSplitHdrBytes);
+            p.split_l = p.split_m + G * 256;
+            p.split_o = p.split_l + G * 256;
+            grid_x = sms;
+        }
+    }
+    int rc2 = -2;
     switch (hdp) {
     case 16:
-        return launch_hdp<16>(p, a.bf16, grid_x, stream);
+        rc2 = launch_hdp<16>(p, a.bf16, grid_x, stream);
+        break;
     case 32:
-        return launch_hdp<32>(p, a.bf16, grid_x, stream);
+        rc2 = launch_hdp<32>(p, a.bf16, grid_x, stream);
+        break;
     case 64:
-        return launch_hdp<64>(p, a.bf16, grid_x, stream);
+        rc2 = launch_hdp<64>(p, a.bf16, grid_x, stream);
+        break;
     case 80:
-        return launch_hdp<80>(p, a.bf16, grid_x, stream);
+        rc2 = launch_hdp<80>(p, a.bf16, grid_x, stream);
+        break;
     case 96:
-        return launch_hdp<96>(p, a.bf16, grid_x, stream);
+        rc2 = launch_hdp<96>(p, a.bf16, grid_x, stream);
+        break;
     case 128:
-        return launch_hdp<128>(p, a.bf16, grid_x, stream);
+        rc2 = launch_hdp<128>(p, a.bf16, grid_x, stream);
+        break;
     }
-    return -2;
+    if (rc2 != 0 || p.split_s <= 1)
+        return rc2;
+    FmhaCombineParams c{};
+    c.hdr = p.split_hdr;
+    c.m = p.split_m;
+    c.l = p.split_l;
+    c.o = p.split_o;
+    c.out = p.out;
+    c.o_sb = p.o_sb;
+    c.o_sh = p.o_sh;
+    c.o_st = p.o_st;
+    c.L = p.L;
+    c.hd = p.hd;
+    c.hdp = hdp;
+    c.tail = p.split_tail;
+    c.s = p.split_s;
+    c.out_dtype = p.out_dtype;
+    c.out_vec = p.out_vec;
+    c.err = p.err;
+    const dim3 cgrid(static_cast<unsigned>((256 * (hdp / 8) + 255) / 256), static_cast<unsigned>(p.split_tail));
+    fmha_split_combine<<<cgrid, 256, 0, stream>>>(c);
+    return static_cast<int>(cudaGetLastError());
 }
 
 } // namespace omni_b200

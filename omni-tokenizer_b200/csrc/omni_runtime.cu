@@ -687,12 +687,17 @@ Tensor attention(Context &c, const Tensor &q, const Tensor *k, const Tensor *v, 
     const int dt = q.bf16 ? OMNI_B200_BF16 : OMNI_B200_F32;
     const size_t ws_bytes = attention_rows_workspace(rows, static_cast<int>(heads), static_cast<int>(hd), dt,
                                                      fused ? 1 : 0);
-    Tensor ws_holder;
+    Tensor ws_holder, split_holder;
     void *ws = ws_bytes ? c.scratch(ws_bytes, ws_holder) : nullptr;
+    // Scratch for the key split of a partial last round (small batches).
+    const size_t split_bytes = attention_rows_split_workspace(
+        n, static_cast<int>(batch), static_cast<int>(heads), static_cast<int>(hd), block,
+        valid_dev ? 0 : static_cast<size_t>(valid[0]), dt);
+    void *split = split_bytes ? c.scratch(split_bytes, split_holder) : nullptr;
     op_ok(attention_rows(q.data(), fused ? nullptr : k->data(), fused ? nullptr : v->data(), y.data(), n,
                          static_cast<int>(batch), static_cast<int>(heads), static_cast<int>(hd), block,
                          valid_dev ? 0 : static_cast<size_t>(valid[0]), valid_dev, fused ? 1 : 0, dt, dt, ws,
-                         ws_bytes, c.stream),
+                         ws_bytes, c.stream, split, split_bytes),
           "attention");
     return y;
 }

@@ -197,10 +197,28 @@ int attention_rows_f32(const void *qp, const void *kp, const void *vp, void *out
 // `batch` sequences of n tokens stacked as batch*n rows.  Items are contiguous
 // along the token axis, so the packed copy [heads, batch*n, hdp] is also a
 // (hdp, n, heads, batch) view with s_batch = n*hdp.
+size_t attention_rows_split_workspace(size_t n, int batch, int heads, int head_dim, size_t block,
+                                      size_t valid, int dtype) {
+    if (dtype == OMNI_B200_F32 || n == 0 || n > (1u << 30))
+        return 0;
+    const int ni = static_cast<int>(n);
+    return fmha_split_workspace(batch, heads, ni, head_dim,
+                                valid > n || valid == 0 ? ni : static_cast<int>(valid),
+                                block > n ? ni : static_cast<int>(block), 0);
+}
+
+// Repacking bytes (attention_rows_workspace) rounded up to 256, then the key
+// split scratch: the layout of the workspace that the C ABI's queries size.
+size_t rows_workspace_total(size_t n, int batch, int heads, int head_dim, int dtype, int fused) {
+    const size_t pack = attention_rows_workspace(n * static_cast<size_t>(batch), heads, head_dim, dtype, fused);
+    const size_t split = attention_rows_split_workspace(n, batch, heads, head_dim, 0, n, dtype);
+    return split ? (pack + 255) / 256 * 256 + split : pack;
+}
+
 int attention_rows(const void *q, const void *k, const void *v, void *out, size_t n, int batch,
                    int heads, int head_dim, size_t block, size_t valid, const int *lengths,
                    int fused, int dtype, int out_dtype, void *workspace, size_t workspace_bytes,
-                   cudaStream_t s) {
+                   cudaStream_t s, void *split_ws, size_t split_ws_bytes) {
     g_error.clear();
     if (!q || !out || (!fused && (!k || !v)))
         return fail(1, "attention_rows: null tensor pointer");
@@ -233,6 +251,7 @@ int attention_rows(const void *q, const void *k, const void *v, void *out, size_
     const size_t need = attention_rows_workspace(rows, heads, head_dim, dtype, fused);
     const bool direct = need == 0 && tma_view_ok(qp, view) && tma_view_ok(kp, view) &&
                         tma_view_ok(vp, view);
+    size_t used = 0; // workspace bytes taken by the repacked operands
     if (direct) {
         a.q_ptr = qp;
         a.k_ptr = kp;
@@ -245,6 +264,7 @@ int attention_rows(const void *q, const void *k, const void *v, void *out, size_
             return fail(1, "attention_rows: workspace too small (need " +
                                std::to_string(3 * one) + " bytes)");
         char *w = static_cast<char *>(workspace);
+        used = 3 * one;
         const void *src[3] = {qp, kp, vp};
         for (int i = 0; i < 3; ++i) {
             const int rc = pack_heads(src[i], dtype, s_token, head_dim, static_cast<int>(rows), heads,
@@ -278,6 +298,17 @@ int attention_rows(const void *q, const void *k, const void *v, void *out, size_
     a.scale = 1.0 / std::sqrt(static_cast<double>(head_dim));
     a.out_d = head_dim; // packed operands are hdp wide; the output keeps head_dim
     a.err = kernel_error_word();
+    a.split_ws = split_ws;
+    a.split_ws_bytes = split_ws_bytes;
+    if (!split_ws && workspace) {
+        // The key split scratch follows the repacking bytes when the caller's
+        // workspace has room for it (sized by rows_workspace_total).
+        const size_t at = (used + 255) / 256 * 256;
+        if (workspace_bytes > at) {
+            a.split_ws = static_cast<char *>(workspace) + at;
+            a.split_ws_bytes = workspace_bytes - at;
+        }
+    }
     if (!a.err)
         return fail(7, "attention_rows: no CUDA device");
     return launch_status(fmha_launch(a, s), "attention_rows");
@@ -380,7 +411,7 @@ int omni_b200_attention_bhld(const void *q, const void *k, const void *v, void *
 }
 
 size_t omni_b200_attention_rows_workspace(size_t n, int heads, int head_dim, int dtype, int fused) {
-    return attention_rows_workspace(n, heads, head_dim, dtype, fused);
+    return rows_workspace_total(n, 1, heads, head_dim, dtype, fused);
 }
 
 int omni_b200_attention_rows(const void *q, const void *k, const void *v, void *out, size_t n,
@@ -388,6 +419,21 @@ int omni_b200_attention_rows(const void *q, const void *k, const void *v, void *
                              int dtype, int out_dtype, void *workspace, size_t workspace_bytes,
                              void *stream) {
     return attention_rows(q, k, v, out, n, 1, heads, head_dim, block, valid, nullptr, fused, dtype,
+                          out_dtype, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+size_t omni_b200_attention_rows_batch_workspace(size_t n, int batch, int heads, int head_dim, int dtype,
+                                                int fused) {
+    if (batch <= 0)
+        return 0;
+    return rows_workspace_total(n, batch, heads, head_dim, dtype, fused);
+}
+
+int omni_b200_attention_rows_batch(const void *q, const void *k, const void *v, void *out, size_t n,
+                                   int batch, int heads, int head_dim, size_t block, size_t valid,
+                                   const int32_t *lengths, int fused, int dtype, int out_dtype,
+                                   void *workspace, size_t workspace_bytes, void *stream) {
+    return attention_rows(q, k, v, out, n, batch, heads, head_dim, block, valid, lengths, fused, dtype,
                           out_dtype, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 

@@ -44,6 +44,13 @@ SIGNATURES = {
         [_P, _P, _P, _P, C.c_size_t, C.c_int, C.c_int, C.c_size_t, C.c_size_t, C.c_int, C.c_int, C.c_int, _P,
          C.c_size_t, _P],
     ),
+    "omni_b200_attention_rows_batch_workspace": (
+        C.c_size_t, [C.c_size_t, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int]),
+    "omni_b200_attention_rows_batch": (
+        C.c_int,
+        [_P, _P, _P, _P, C.c_size_t, C.c_int, C.c_int, C.c_int, C.c_size_t, C.c_size_t, _P, C.c_int, C.c_int,
+         C.c_int, _P, C.c_size_t, _P],
+    ),
     "omni_b200_squares": (C.c_int, [_P, _P, C.c_size_t, C.c_size_t, C.c_int, C.c_int, _P]),
     "omni_b200_vq_argmin": (
         C.c_int,
@@ -183,20 +190,40 @@ def _addr(obj):
     return obj.ctypes.data
 
 
-def attention_rows(q, k, v, heads, block=0, valid=None, fused=False, out_dtype=None, stream=None):
-    """Ops::attention on the reference's row-major layout (CUDA tensors)."""
+def attention_rows(q, k, v, heads, block=0, valid=None, fused=False, out_dtype=None, stream=None,
+                   batch=1, lengths=None, workspace=True):
+    """Ops::attention on the reference's row-major layout (CUDA tensors).
+
+    batch > 1: `batch` sequences of q.shape[0] // batch rows each, keys of
+    sequence b limited to lengths[b] (a CUDA int32 tensor) when given.
+    workspace=False passes only the repacking bytes (no key split scratch)."""
     import torch
 
-    n = q.shape[0]
+    rows = q.shape[0]
+    n = rows // batch
     d = q.shape[1] // 3 if fused else q.shape[1]
     hd = d // heads
     valid = n if valid is None else valid
-    out = torch.empty((n, d), dtype=out_dtype or q.dtype, device=q.device)
+    out = torch.empty((rows, d), dtype=out_dtype or q.dtype, device=q.device)
     lib = library()
-    ws_bytes = lib.lib.omni_b200_attention_rows_workspace(n, heads, hd, _dtype_code(q), int(fused))
+    if batch == 1 and lengths is None:
+        ws_bytes = lib.lib.omni_b200_attention_rows_workspace(n, heads, hd, _dtype_code(q), int(fused))
+    else:
+        ws_bytes = lib.lib.omni_b200_attention_rows_batch_workspace(n, batch, heads, hd, _dtype_code(q),
+                                                                    int(fused))
+    if not workspace:
+        ws_bytes = 0
+        if _dtype_code(q) == 0 or hd % 8 or (3 * d if fused else d) % 8:
+            raise ValueError("workspace=False needs rows that are read in place")
     ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=q.device)
-    lib.check(lib.lib.omni_b200_attention_rows(
-        q.data_ptr(), None if fused else k.data_ptr(), None if fused else v.data_ptr(), out.data_ptr(), n, heads,
-        hd, block, valid, int(fused), _dtype_code(q), _dtype_code(out), ws.data_ptr(), ws_bytes,
-        _stream_ptr(stream)))
+    if batch == 1 and lengths is None:
+        lib.check(lib.lib.omni_b200_attention_rows(
+            q.data_ptr(), None if fused else k.data_ptr(), None if fused else v.data_ptr(), out.data_ptr(), n,
+            heads, hd, block, valid, int(fused), _dtype_code(q), _dtype_code(out), ws.data_ptr(), ws_bytes,
+            _stream_ptr(stream)))
+    else:
+        lib.check(lib.lib.omni_b200_attention_rows_batch(
+            q.data_ptr(), None if fused else k.data_ptr(), None if fused else v.data_ptr(), out.data_ptr(), n,
+            batch, heads, hd, block, valid, None if lengths is None else lengths.data_ptr(), int(fused),
+            _dtype_code(q), _dtype_code(out), ws.data_ptr(), ws_bytes, _stream_ptr(stream)))
     return out

@@ -53,7 +53,18 @@ def test_workspace_queries():
     lib = load_package().library()
     # bf16 rows of 72-wide heads and fp32 rows of 64-wide heads are read in
     # place; fp32 heads of 7 (28-byte rows) are repacked to fp32 [heads, n, 32].
+    # 16-bit rows whose (query block, head) items leave the last round of SMs
+    # mostly empty get key split scratch: 4 heads x 5 blocks of 1200 rows are 20
+    # items (7 parts of 1-2 of the 10 KV tiles).  16 x 3 blocks of 729 rows (48
+    # items of 6 tiles) would save 4 tiles, below what the combine pass costs;
+    # 16 x 6 blocks of 1500 rows are 96 items (a part would need a second round).
+    sms = 148  # the SM count without a device
+    assert lib.lib.omni_b200_attention_rows_workspace(1200, 4, 72, 1, 0) >= sms * 256 * (80 + 2) * 4
     assert lib.lib.omni_b200_attention_rows_workspace(729, 16, 72, 1, 0) == 0
+    assert lib.lib.omni_b200_attention_rows_workspace(1500, 16, 64, 1, 0) == 0
+    assert lib.lib.omni_b200_attention_rows_batch_workspace(1500, 1, 16, 64, 1, 0) == 0
+    assert lib.lib.omni_b200_attention_rows_batch_workspace(1500, 2, 16, 64, 1, 1) >= sms * 256 * 66 * 4
+    assert lib.lib.omni_b200_attention_rows_batch_workspace(1500, 2, 16, 64, 0, 1) == 0  # fp32: no split
     assert lib.lib.omni_b200_attention_rows_workspace(1500, 20, 64, 0, 0) == 0
     assert lib.lib.omni_b200_attention_rows_workspace(129, 2, 7, 0, 0) >= 3 * 2 * 129 * 32 * 4
     assert lib.lib.omni_b200_attention_rows_workspace(129, 2, 7, 1, 0) >= 3 * 2 * 129 * 16 * 2

@@ -164,6 +164,84 @@ def test_rows_matches_oracle(ob, n, heads, hd, block, valid, fused, dtype):
     _close(out.cpu().numpy(), want, f"rows n{n} h{heads} hd{hd} block{block} valid{valid}")
 
 
+# Key split of a partial last round (16-bit operands): the (query block, head)
+# items of a last round that would leave most SMs idle are cut along the keys
+# into parts on the idle SMs and merged by a second pass.  The split runs when
+# the workspace holds its scratch (the workspace query sizes it);
+# workspace=False runs the same call unsplit.
+SPLIT_ROW_CASES = [
+    # n, heads, hd, block, valid, fused
+    (1200, 4, 72, 0, 1200, False),    # 20 items: 7 parts of 1-2 of 10 KV tiles (head dim 72 -> 80)
+    (2049, 2, 96, 0, 2049, True),     # 18 items: 8 parts of 2-3 of 17 tiles
+    (1000, 4, 64, 0, 900, False),     # 16 items, keys limited to 900: 8 parts of one of the 8 tiles
+    (1500, 2, 64, 0, 1500, True),     # 12 items: 8 parts of 1-2 of 12 tiles
+    (1024, 2, 128, 0, 1024, False),   # 8 items: 8 parts of one tile
+    (1500, 3, 32, 0, 1450, True),     # 18 items, head dim 32
+    (1500, 2, 64, 200, 1497, True),   # block window: parts past a row's window, empty parts
+    (1000, 4, 64, 300, 1000, False),
+    (1500, 2, 64, 1500, 1500, False), # a window as long as the sequence limits nothing
+]
+
+
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("n,heads,hd,block,valid,fused", SPLIT_ROW_CASES)
+def test_rows_key_split_matches_oracle(ob, n, heads, hd, block, valid, fused, out_dtype):
+    lib = ob.library()
+    assert lib.lib.omni_b200_attention_rows_workspace(n, heads, hd, 1, int(fused)) > 0  # a split is planned
+    d = heads * hd
+    cols = 3 * d if fused else d
+    q = O.round_bf16(O.lcg_values(n * cols, 321).reshape(n, cols))
+    k = O.round_bf16(O.lcg_values(n * d, 654).reshape(n, d))
+    v = O.round_bf16(O.lcg_values(n * d, 987).reshape(n, d))
+    tq, tk, tv = (torch.from_numpy(x).to(torch.bfloat16).cuda() for x in (q, k, v))
+    kw = dict(block=block, valid=valid, fused=fused, out_dtype=out_dtype)
+    split = ob.attention_rows(tq, tk, tv, heads, **kw)
+    plain = ob.attention_rows(tq, tk, tv, heads, workspace=False, **kw)
+    lib.sync_check()
+    want = O.attention(q, k, v, heads, block, valid, fused, bf16=False)
+    got = split.float().cpu().numpy()
+    what = f"n{n} h{heads} hd{hd} block{block} valid{valid}"
+    _close(got, want, "split " + what)
+    _close(plain.float().cpu().numpy(), want, "unsplit " + what)
+    # The parts round P relative to their own row maxima: the two runs agree to
+    # within the rounding of P, not bit for bit.
+    assert np.abs(got - plain.float().cpu().numpy()).max() <= 1e-2
+
+
+@pytest.mark.parametrize("heads,lens,block", [
+    (16, [1500, 1100], 0),     # 192 items: 148 whole, the 44 of the shorter sequence in 3 parts
+    (16, [1500, 1100], 1500),  # the audio graphs' window of the whole sequence: the same plan
+    (16, [1500, 90], 0),       # the short sequence's items have one KV tile: two empty parts each
+    (16, [1500, 0], 0),        # an empty sequence: every part empty, rows of zeros
+    (8, [1000], 0),            # one sequence with a device length: 48 items in 3 parts
+    (8, [1000], 256),          # ... with a block window
+])
+def test_rows_batch_key_split_with_lengths(ob, heads, lens, block):
+    """Stacked sequences with device key lengths, as the encoder's batched audio
+    call runs them: items in longest-first order, the last round's items split
+    along the keys (parts past a short sequence's tiles are empty)."""
+    n, hd, batch = 1500, 64, len(lens)
+    d = heads * hd
+    lib = ob.library()
+    assert lib.lib.omni_b200_attention_rows_batch_workspace(n, batch, heads, hd, 1, 1) > 0
+    q = O.round_bf16(O.lcg_values(batch * n * 3 * d, 77).reshape(batch * n, 3 * d))
+    tq = torch.from_numpy(q).to(torch.bfloat16).cuda()
+    lengths = torch.tensor(lens, dtype=torch.int32).cuda()
+    out = ob.attention_rows(tq, None, None, heads, block=block, fused=True, batch=batch, lengths=lengths,
+                            out_dtype=torch.float32)
+    out16 = ob.attention_rows(tq, None, None, heads, block=block, fused=True, batch=batch, lengths=lengths)
+    lib.sync_check()
+    got, got16 = out.cpu().numpy(), out16.float().cpu().numpy()
+    for b, m in enumerate(lens):
+        rows = slice(b * n, (b + 1) * n)
+        if m == 0:
+            assert np.all(got[rows] == 0.0) and np.all(got16[rows] == 0.0), f"sequence {b}: zeros"
+            continue
+        want = O.attention(q[rows], None, None, heads, block, m, True, bf16=False)
+        _close(got[rows], want, f"sequence {b} (valid {m})")
+        _close(got16[rows], want, f"sequence {b} (valid {m}, bf16 out)")
+
+
 @pytest.mark.parametrize("n,hd", [(401, 64), (601, 7), (1025, 64)])
 def test_mask_semantics(ob, n, hd):
     """tests/native_cuda_attention.cpp:199-218 through the rows entry point."""
