@@ -93,18 +93,6 @@ OMNI_B200_API int omni_b200_attention_rows_batch(const void *q, const void *k, c
                                                  int out_dtype, void *workspace,
                                                  size_t workspace_bytes, void *stream);
 
-/* Ops::linear in the bf16 profile (omni-tokenizer src/internal.h:75, semantics of
- * src/cpu.cpp:47-69): y = r(x W^T + b), fp32 sums, one rounding to bf16 after
- * the bias.  x is [rows, in_features], weight [out_features, in_features] (the
- * file layout), bias [out_features] or NULL, y [rows, out_features]; all bf16
- * row-major, 16-byte aligned, out_features and in_features multiples of 8.
- * The tcgen05 GEMM that the encoder graphs use for their large linears;
- * `workspace` of omni_b200_linear_workspace() bytes (may be 0 and NULL). */
-OMNI_B200_API size_t omni_b200_linear_workspace(size_t rows, int out_features, int in_features, int has_bias);
-OMNI_B200_API int omni_b200_linear(const void *x, const void *weight, const void *bias, void *y, size_t rows,
-                                   int out_features, int in_features, void *workspace,
-                                   size_t workspace_bytes, void *stream);
-
 /* Ops::squares (omni-tokenizer src/internal.h:86, semantics of
  * src/cpu.cpp:216-226): out[r] = sum over columns in order of x[r,j]^2, with
  * every square and the total rounded to bf16 when dtype is BF16.  x is

@@ -29,22 +29,6 @@ FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-fvisibility=hid
          "-I", str(ROOT / "include"), "-I", str(CSRC)]
 
 
-# Sources built on CUTLASS/CuTe sm100 templates: the header tree that ships
-# with flashinfer in this environment (CUTLASS 4.x), header-only.
-CUTLASS_SOURCES = {"gemm_sm100.cu"}
-
-
-def cutlass_include() -> Path:
-    import site
-
-    roots = [Path(p) for p in site.getsitepackages()] + [Path(site.getusersitepackages())]
-    for root in roots:
-        cand = root / "flashinfer" / "data" / "cutlass" / "include"
-        if (cand / "cutlass" / "gemm" / "collective" / "builders" / "sm100_umma_builder.inl").exists():
-            return cand
-    raise RuntimeError("CUTLASS headers with sm100 collectives not found (flashinfer/data/cutlass/include)")
-
-
 def nvcc() -> str:
     for cand in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
         if cand and Path(cand).exists():
@@ -80,10 +64,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
 
     def compile_one(job):
         src, obj = job
-        extra = []
-        if src.name in CUTLASS_SOURCES:
-            extra = ["-I", str(cutlass_include()), "--expt-relaxed-constexpr", "-diag-suppress", "20012"]
-        cmd = [nvcc()] + ARCH + FLAGS + extra + ["-c", str(src), "-o", str(obj)]
+        cmd = [nvcc()] + ARCH + FLAGS + ["-c", str(src), "-o", str(obj)]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"nvcc failed for {src.name}:\n{r.stderr}")

@@ -17,7 +17,6 @@
 // per model) and activations with the reference's bf16 rounding points, the
 // tcgen05 attention kernel, fp32 VQ.
 #include "fmha.h"
-#include "gemm_sm100.h"
 #include "graph_kernels.h"
 #include "omni_abi.h"
 #include "omni_b200.h"
@@ -453,10 +452,6 @@ struct Context {
     uint64_t graph_launches = 0;
     bool capturing = false; // inside a stream capture: no synchronising retries
     bool graphs = true;     // OMNI_B200_GRAPHS=0 turns replay off
-    // bf16 linears on this library's tcgen05 GEMM: 1 where it is the faster
-    // choice (OMNI_B200_TC_LINEAR unset or 1), 0 never (cuBLASLt), 2 whenever
-    // the shape allows (tests of the path on small models).
-    int tc_linear = 1;
     void drop_replay() {
         if (replay.exec)
             cudaGraphExecDestroy(replay.exec);
@@ -600,25 +595,6 @@ Tensor linear(Context &c, const Tensor &x, const Tensor &w, const Tensor *b,
     if (m == 0)
         return y;
     const bool fused_bias = b && !bias_after_round;
-    // Large bf16 linears: this library's tcgen05 GEMM (bias in its epilogue,
-    // one rounding); smaller ones and every other case: cuBLASLt.
-    const void *bias_ptr = fused_bias ? b->data() : nullptr;
-    const int mi = static_cast<int>(m), ni = static_cast<int>(n), ki = static_cast<int>(k);
-    if (c.tc_linear && x.bf16 && w.bf16 && (!fused_bias || b->bf16) && m < (1u << 31) &&
-        (c.tc_linear == 2 || linear_bf16_preferred(mi, ni, ki)) &&
-        linear_bf16_supported(x.data(), w.data(), bias_ptr, y.data(), mi, ni, ki)) {
-        const size_t ws_bytes = linear_bf16_workspace(mi, ni, ki, fused_bias);
-        Tensor ws_holder;
-        void *ws = ws_bytes ? c.scratch(ws_bytes, ws_holder) : nullptr;
-        const int rc = linear_bf16(x.data(), w.data(), bias_ptr, y.data(), mi, ni, ki, ws, ws_bytes, c.stream);
-        if (rc > 0)
-            cuda_ok(static_cast<cudaError_t>(rc), "linear");
-        if (rc == 0) {
-            if (b && bias_after_round)
-                cuda_ok(static_cast<cudaError_t>(graph::bias(y.data(), b->data(), y.bf16, m, n, c.stream)), "bias");
-            return y;
-        }
-    }
     const bool lt_ok = c.lt && w.bf16 == x.bf16 && (!fused_bias || b->bf16 == x.bf16) &&
                        (x.bf16 || !c.fp32_emulated) && lt_linear(c, x, w, fused_bias ? b->data() : nullptr, y);
     if (!lt_ok) {
@@ -1289,8 +1265,6 @@ int omni_context_create(omni_model *m, omni_context **out) {
         omni_b200::rt::blas_ok(cublasSetWorkspace(c->impl.blas, c->impl.blas_ws, size_t(32) << 20), "cuBLAS workspace");
         const char *graphs = std::getenv("OMNI_B200_GRAPHS");
         c->impl.graphs = !(graphs && *graphs == '0');
-        const char *tcl = std::getenv("OMNI_B200_TC_LINEAR");
-        c->impl.tc_linear = tcl && *tcl == '0' ? 0 : tcl && *tcl == '2' ? 2 : 1;
         omni_b200::rt::cuda_ok(cudaStreamCreateWithFlags(&c->impl.copy, cudaStreamNonBlocking), "stream create");
         omni_b200::rt::cuda_ok(cudaHostAlloc(reinterpret_cast<void **>(&c->impl.cancel_host), sizeof(int),
                                              cudaHostAllocMapped),

@@ -2,7 +2,6 @@
 #include "omni_b200.h"
 
 #include "fmha.h"
-#include "gemm_sm100.h"
 #include "norms.h"
 #include "pack.h"
 #include "sm100.cuh"
@@ -436,34 +435,6 @@ int omni_b200_attention_rows_batch(const void *q, const void *k, const void *v, 
                                    void *workspace, size_t workspace_bytes, void *stream) {
     return attention_rows(q, k, v, out, n, batch, heads, head_dim, block, valid, lengths, fused, dtype,
                           out_dtype, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
-}
-
-size_t omni_b200_linear_workspace(size_t rows, int out_features, int in_features, int has_bias) {
-    if (rows == 0 || rows > 0x7fffffffu || out_features <= 0 || in_features <= 0)
-        return 0;
-    return linear_bf16_workspace(static_cast<int>(rows), out_features, in_features, has_bias != 0);
-}
-
-int omni_b200_linear(const void *x, const void *weight, const void *bias, void *y, size_t rows, int out_features,
-                     int in_features, void *workspace, size_t workspace_bytes, void *stream) {
-    g_error.clear();
-    if (!x || !weight || !y)
-        return fail(1, "linear: null pointer");
-    if (rows == 0 || rows > 0x7fffffffu || out_features <= 0 || in_features <= 0)
-        return fail(1, "linear: sizes must be positive (rows below 2^31)");
-    const int m = static_cast<int>(rows);
-    if (!linear_bf16_supported(x, weight, bias, y, m, out_features, in_features))
-        return fail(1, "linear: features must be multiples of 8 and pointers 16-byte aligned");
-    const size_t need = linear_bf16_workspace(m, out_features, in_features, bias != nullptr);
-    if (need > workspace_bytes || (need && !workspace))
-        return fail(1, "linear: workspace too small (need " + std::to_string(need) + " bytes)");
-    const int rc = linear_bf16(x, weight, bias, y, m, out_features, in_features, workspace, workspace_bytes,
-                               static_cast<cudaStream_t>(stream));
-    if (rc > 0)
-        return cuda_fail(static_cast<cudaError_t>(rc), "linear");
-    if (rc < 0)
-        return fail(4, "linear: the GEMM rejected the shape (code " + std::to_string(rc) + ")");
-    return 0;
 }
 
 int omni_b200_squares(const void *x, void *out, size_t rows, size_t cols, int dtype, int out_dtype,

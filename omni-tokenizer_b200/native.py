@@ -51,9 +51,6 @@ SIGNATURES = {
         [_P, _P, _P, _P, C.c_size_t, C.c_int, C.c_int, C.c_int, C.c_size_t, C.c_size_t, _P, C.c_int, C.c_int,
          C.c_int, _P, C.c_size_t, _P],
     ),
-    "omni_b200_linear_workspace": (C.c_size_t, [C.c_size_t, C.c_int, C.c_int, C.c_int]),
-    "omni_b200_linear": (
-        C.c_int, [_P, _P, _P, _P, C.c_size_t, C.c_int, C.c_int, _P, C.c_size_t, _P]),
     "omni_b200_squares": (C.c_int, [_P, _P, C.c_size_t, C.c_size_t, C.c_int, C.c_int, _P]),
     "omni_b200_vq_argmin": (
         C.c_int,
@@ -191,22 +188,6 @@ def _addr(obj):
     if hasattr(obj, "data_ptr"):
         return obj.data_ptr()
     return obj.ctypes.data
-
-
-def linear(x, weight, bias=None, stream=None):
-    """Ops::linear on bf16 CUDA tensors: returns r(x @ weight.T + bias) as bf16
-    [rows, out_features] (bias may be None)."""
-    import torch
-
-    rows, k = x.shape
-    n = weight.shape[0]
-    y = torch.empty((rows, n), dtype=torch.bfloat16, device=x.device)
-    lib = library()
-    ws_bytes = lib.lib.omni_b200_linear_workspace(rows, n, k, int(bias is not None))
-    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=x.device)
-    lib.check(lib.lib.omni_b200_linear(x.data_ptr(), weight.data_ptr(), None if bias is None else bias.data_ptr(),
-                                       y.data_ptr(), rows, n, k, ws.data_ptr(), ws_bytes, _stream_ptr(stream)))
-    return y
 
 
 def attention_rows(q, k, v, heads, block=0, valid=None, fused=False, out_dtype=None, stream=None,

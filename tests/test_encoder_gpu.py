@@ -106,11 +106,7 @@ def test_audio_encoder_matches_reference(abi, ours, golden):
         s.close()
 
 
-@pytest.mark.parametrize("tc_linear", ["1", "2"])
-def test_image_encoder_matches_reference(abi, ours, golden, monkeypatch, tc_linear):
-    """tc_linear 2 runs every linear of the (small) golden model on the
-    library's tcgen05 GEMM, which otherwise only takes large linears."""
-    monkeypatch.setenv("OMNI_B200_TC_LINEAR", tc_linear)
+def test_image_encoder_matches_reference(abi, ours, golden):
     cb = _codebook("image")
     with ours.load(GOLDEN / "image.omni", backend=abi.CUDA) as m:
         s = m.context()
@@ -234,21 +230,18 @@ def test_audio_fp32_emulation_matches_reference(abi, ours, golden, tmp_path):
     np.testing.assert_allclose(got["features_batch"], golden["audio_batch_features"], rtol=1e-4, atol=1e-4)
 
 
-@pytest.mark.parametrize("tc_linear", ["1", "2"])
-def test_audio_bf16_mode_matches_graph_oracle(abi, ours, golden, monkeypatch, tc_linear):
+def test_audio_bf16_mode_matches_graph_oracle(abi, ours, golden, monkeypatch):
     """OMNI_B200_AUDIO_BF16=1: the audio graph in bf16 (bf16 weights and
     activations, the reference's bf16 rounding points) against the numpy graph
     restatement in the same profile (oracle/encoder.py, itself pinned to the
     reference's fixtures).  Summation orders differ, so a rounded intermediate
     may land one bf16 ulp apart: features within 4 ulps of the largest
-    feature, on average within a quarter ulp.  tc_linear 2: every linear on
-    the library's tcgen05 GEMM."""
+    feature, on average within a quarter ulp."""
     from oracle import encoder as E
 
     model = E.load_model(GOLDEN / "audio.omni")
     cb = _codebook("audio")
     monkeypatch.setenv("OMNI_B200_AUDIO_BF16", "1")
-    monkeypatch.setenv("OMNI_B200_TC_LINEAR", tc_linear)
     with ours.load(GOLDEN / "audio.omni") as m:
         s = m.context()
         cases = [(golden[f"audio{i}_mel"][None], [int(golden[f"audio{i}_valid"])]) for i in range(3)]
@@ -493,24 +486,3 @@ def test_repeated_batches_replay_a_cuda_graph(abi, ours, golden, monkeypatch):
         assert s.graph_launches == 2
         s.close()
         eager.close()
-
-
-def test_image_replay_with_tcgen05_linears(abi, ours, golden, monkeypatch):
-    """The image graph with every linear on the library's tcgen05 GEMM
-    (OMNI_B200_TC_LINEAR=2), captured into a CUDA graph and replayed: codes
-    bit-identical to an eager context's."""
-    monkeypatch.setenv("OMNI_B200_TC_LINEAR", "2")
-    dev = torch.from_numpy(golden["image_batch_pixels"]).cuda()
-    with ours.load(GOLDEN / "image.omni") as m:
-        monkeypatch.setenv("OMNI_B200_GRAPHS", "0")
-        eager = m.context()
-        monkeypatch.setenv("OMNI_B200_GRAPHS", "1")
-        s = m.context()
-        want = eager.encode_images(tuple(dev.shape), patch=8, device_ptr=dev.data_ptr())
-        for _ in range(3):
-            got = s.encode_images(tuple(dev.shape), patch=8, device_ptr=dev.data_ptr())
-            np.testing.assert_array_equal(got, want)
-        assert s.graph_launches == 2  # captured on the second call, replayed on the third
-        assert eager.graph_launches == 0
-        eager.close()
-        s.close()
