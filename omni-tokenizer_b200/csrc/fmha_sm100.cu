@@ -1269,7 +1269,11 @@ struct FmhaCombineParams {
     const int *err;
 };
 
-__global__ void __launch_bounds__(256) fmha_split_combine(const __grid_constant__ FmhaCombineParams c) {
+// MAXP: the most parts the instance merges (4: 64 registers, four blocks of
+// 256 threads per SM, so a two-segment audio layer's 352 blocks fit in one
+// wave; 8: twice the registers and blocks).
+template <int MAXP>
+__global__ void __launch_bounds__(256, MAXP <= 4 ? 4 : 2) fmha_split_combine(const __grid_constant__ FmhaCombineParams c) {
     const int w = blockIdx.y, ng = c.hdp / 8;
     const int unit = blockIdx.x * blockDim.x + threadIdx.x;
     if (unit >= 256 * ng)
@@ -1277,10 +1281,10 @@ __global__ void __launch_bounds__(256) fmha_split_combine(const __grid_constant_
     const int row = unit / ng, c0 = (unit - row * ng) * 8;
     const int e = *c.err;
     const int4 hd4 = c.hdr[w]; // batch, head, first query row, skip
-    float mq[kSplitMaxParts], lq[kSplitMaxParts];
-    float4 oq[kSplitMaxParts][2];
+    float mq[MAXP], lq[MAXP];
+    float4 oq[MAXP][2];
 #pragma unroll
-    for (int q = 0; q < kSplitMaxParts; ++q) {
+    for (int q = 0; q < MAXP; ++q) {
         if (q < c.s) {
             const int pr = (q * c.tail + w) * 256 + row;
             mq[q] = c.m[pr];
@@ -1297,7 +1301,7 @@ __global__ void __launch_bounds__(256) fmha_split_combine(const __grid_constant_
         return;
     float mmax = -INFINITY;
 #pragma unroll
-    for (int q = 0; q < kSplitMaxParts; ++q)
+    for (int q = 0; q < MAXP; ++q)
         if (q < c.s)
             mmax = fmaxf(mmax, mq[q]);
     float acc[8], l = 0.f;
@@ -1306,7 +1310,7 @@ __global__ void __launch_bounds__(256) fmha_split_combine(const __grid_constant_
         acc[k] = 0.f;
     if (mmax != -INFINITY) {
 #pragma unroll
-        for (int q = 0; q < kSplitMaxParts; ++q) {
+        for (int q = 0; q < MAXP; ++q) {
             if (q < c.s) {
                 const float a = exp2f(mq[q] - mmax);
                 l = fmaf(a, lq[q], l);
@@ -1609,7 +1613,10 @@ int fmha_launch(const FmhaArgs &a, cudaStream_t stream) {
     c.out_vec = p.out_vec;
     c.err = p.err;
     const dim3 cgrid(static_cast<unsigned>((256 * (hdp / 8) + 255) / 256), static_cast<unsigned>(p.split_tail));
-    fmha_split_combine<<<cgrid, 256, 0, stream>>>(c);
+    if (p.split_s <= 4)
+        fmha_split_combine<4><<<cgrid, 256, 0, stream>>>(c);
+    else
+        fmha_split_combine<kSplitMaxParts><<<cgrid, 256, 0, stream>>>(c);
     return static_cast<int>(cudaGetLastError());
 }
 
