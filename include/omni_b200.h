@@ -93,6 +93,13 @@ OMNI_B200_API int omni_b200_attention_rows_batch(const void *q, const void *k, c
                                                  int out_dtype, void *workspace,
                                                  size_t workspace_bytes, void *stream);
 
+/* Ops::gelu (omni-tokenizer src/internal.h:77, semantics of src/cpu.cpp:91-96),
+ * in place on n elements of dtype (F32 or BF16): x = r(0.5 x (1 + erf(x *
+ * 0.70710678...))), each step an fp32 operation, r the rounding to bf16 for
+ * BF16.  bf16 inputs are looked up in a table built once per device from that
+ * expression (the first call on a device builds it and synchronises the stream). */
+OMNI_B200_API int omni_b200_gelu(void *x, size_t n, int dtype, void *stream);
+
 /* Ops::squares (omni-tokenizer src/internal.h:86, semantics of
  * src/cpu.cpp:216-226): out[r] = sum over columns in order of x[r,j]^2, with
  * every square and the total rounded to bf16 when dtype is BF16.  x is

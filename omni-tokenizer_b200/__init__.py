@@ -6,6 +6,6 @@ bench.py or __graft_entry__.py, or bind libomni_b200.so directly with ctypes
 (native.py declares every op-level signature, abi.py the omni_* ones).
 """
 
-from .native import NativeError, Library, Context, library, attention_bhld, attention_rows  # noqa: F401
+from .native import NativeError, Library, Context, library, attention_bhld, attention_rows, gelu_  # noqa: F401
 
 __version__ = "0.1.0"

@@ -117,16 +117,35 @@ __global__ void k_gelu_table_build() {
     }
 }
 
+// The table kernel keeps only the common part of the table in shared memory:
+// bf16 inputs with exponent field in [kGeluE0, kGeluE1] (|z| in [2^-25, 16)),
+// both signs -- two contiguous slices of g_gelu_bf16, 14.8 KB -- and reads the
+// rare rest (tiny or large |z|, zeros, infinities, NaN) from the full table in
+// global memory.  So every result is the full table's entry, bit for bit.
+// (The whole 128 KB table per block cost as much traffic as the data itself on
+// small activations.)
+constexpr int kGeluE0 = 102, kGeluE1 = 130, kGeluNE = kGeluE1 - kGeluE0 + 1;
+constexpr int kGeluSlice = kGeluNE * 128; // entries per sign
 constexpr int kGeluTableThreads = 1024;
-constexpr size_t kGeluTableSmem = 65536 * sizeof(uint16_t);
 
-__global__ void __launch_bounds__(kGeluTableThreads) k_gelu_table(uint4 *__restrict__ x, size_t nvec) {
-    extern __shared__ uint4 table4[];
-    const uint4 *src = reinterpret_cast<const uint4 *>(g_gelu_bf16);
-    for (int i = threadIdx.x; i < 65536 / 8; i += kGeluTableThreads)
-        table4[i] = src[i];
+__global__ void __launch_bounds__(kGeluTableThreads, 1) k_gelu_table(uint4 *__restrict__ x, size_t nvec) {
+    __shared__ __align__(16) uint16_t table[2 * kGeluSlice];
+    static_assert((kGeluE0 * 128) % 8 == 0 && kGeluSlice % 8 == 0, "16-byte slices");
+    const uint4 *lo = reinterpret_cast<const uint4 *>(g_gelu_bf16 + kGeluE0 * 128);
+    const uint4 *hi = reinterpret_cast<const uint4 *>(g_gelu_bf16 + 0x8000 + kGeluE0 * 128);
+    uint4 *t4 = reinterpret_cast<uint4 *>(table);
+    for (int i = threadIdx.x; i < kGeluSlice / 8; i += kGeluTableThreads) {
+        t4[i] = lo[i];
+        t4[kGeluSlice / 8 + i] = hi[i];
+    }
     __syncthreads();
-    const uint16_t *table = reinterpret_cast<const uint16_t *>(table4);
+    auto look = [&](uint32_t b) -> uint32_t {
+        const uint32_t e = (b >> 7) & 0xffu;
+        const uint32_t k = e - kGeluE0; // wraps for e < kGeluE0
+        if (k < static_cast<uint32_t>(kGeluNE))
+            return table[(b >> 15) * kGeluSlice + k * 128 + (b & 127u)];
+        return __ldg(g_gelu_bf16 + b);
+    };
     const size_t stride = static_cast<size_t>(gridDim.x) * kGeluTableThreads;
     constexpr int U = 4; // vectors in flight per thread
     for (size_t i = blockIdx.x * static_cast<size_t>(kGeluTableThreads) + threadIdx.x; i < nvec; i += U * stride) {
@@ -140,7 +159,7 @@ __global__ void __launch_bounds__(kGeluTableThreads) k_gelu_table(uint4 *__restr
             uint32_t *w = reinterpret_cast<uint32_t *>(&v[u]);
 #pragma unroll
             for (int k = 0; k < 4; ++k)
-                w[k] = table[w[k] & 0xffffu] | (static_cast<uint32_t>(table[w[k] >> 16]) << 16);
+                w[k] = look(w[k] & 0xffffu) | (look(w[k] >> 16) << 16);
         }
 #pragma unroll
         for (int u = 0; u < U; ++u)
@@ -670,9 +689,8 @@ int layer_norm(const void *x, const void *w, const void *b, void *y, bool bf16, 
     return status();
 }
 namespace {
-// The table is built once per device; the table kernel's shared-memory limit
-// is raised once per device as well.
-std::atomic<unsigned long long> g_gelu_table_ready{0}, g_gelu_smem_set{0};
+// The table is built once per device.
+std::atomic<unsigned long long> g_gelu_table_ready{0};
 std::mutex g_gelu_mutex;
 
 bool gelu_table(cudaStream_t s) {
@@ -684,9 +702,6 @@ bool gelu_table(cudaStream_t s) {
         return true;
     std::lock_guard<std::mutex> guard(g_gelu_mutex);
     if (!(g_gelu_table_ready.load() & bit)) {
-        if (set_smem_limit(reinterpret_cast<const void *>(k_gelu_table), static_cast<int>(kGeluTableSmem),
-                           g_gelu_smem_set) != cudaSuccess)
-            return false;
         k_gelu_table_build<<<64, 1024, 0, s>>>();
         if (cudaGetLastError() != cudaSuccess || cudaStreamSynchronize(s) != cudaSuccess)
             return false;
@@ -703,9 +718,11 @@ int gelu(void *x, bool bf16, size_t n, cudaStream_t s) {
             int sms = 148, dev = 0;
             cudaGetDevice(&dev);
             cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+            // One block per SM, each loading the 14.8 KB of table once.
             const size_t want = (nvec + kGeluTableThreads - 1) / kGeluTableThreads;
-            const unsigned grid = static_cast<unsigned>(want < static_cast<size_t>(sms) ? want : sms);
-            k_gelu_table<<<grid, kGeluTableThreads, kGeluTableSmem, s>>>(static_cast<uint4 *>(x), nvec);
+            const size_t cap = static_cast<size_t>(sms);
+            const unsigned grid = static_cast<unsigned>(want < cap ? want : cap);
+            k_gelu_table<<<grid, kGeluTableThreads, 0, s>>>(static_cast<uint4 *>(x), nvec);
         } else if (bf16) {
             k_gelu_vec<true><<<blocks_for(nvec, 256), 256, 0, s>>>(x, nvec);
         } else {

@@ -2,6 +2,7 @@
 #include "omni_b200.h"
 
 #include "fmha.h"
+#include "graph_kernels.h"
 #include "norms.h"
 #include "pack.h"
 #include "sm100.cuh"
@@ -435,6 +436,18 @@ int omni_b200_attention_rows_batch(const void *q, const void *k, const void *v, 
                                    void *workspace, size_t workspace_bytes, void *stream) {
     return attention_rows(q, k, v, out, n, batch, heads, head_dim, block, valid, lengths, fused, dtype,
                           out_dtype, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int omni_b200_gelu(void *x, size_t n, int dtype, void *stream) {
+    g_error.clear();
+    if (!x && n)
+        return fail(1, "gelu: null pointer");
+    if (dtype != OMNI_B200_F32 && dtype != OMNI_B200_BF16)
+        return fail(1, "gelu: dtype must be F32 or BF16");
+    if (n == 0)
+        return 0;
+    const int rc = graph::gelu(x, dtype == OMNI_B200_BF16, n, static_cast<cudaStream_t>(stream));
+    return rc ? cuda_fail(static_cast<cudaError_t>(rc), "gelu") : 0;
 }
 
 int omni_b200_squares(const void *x, void *out, size_t rows, size_t cols, int dtype, int out_dtype,

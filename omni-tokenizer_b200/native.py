@@ -51,6 +51,7 @@ SIGNATURES = {
         [_P, _P, _P, _P, C.c_size_t, C.c_int, C.c_int, C.c_int, C.c_size_t, C.c_size_t, _P, C.c_int, C.c_int,
          C.c_int, _P, C.c_size_t, _P],
     ),
+    "omni_b200_gelu": (C.c_int, [_P, C.c_size_t, C.c_int, _P]),
     "omni_b200_squares": (C.c_int, [_P, _P, C.c_size_t, C.c_size_t, C.c_int, C.c_int, _P]),
     "omni_b200_vq_argmin": (
         C.c_int,
@@ -188,6 +189,13 @@ def _addr(obj):
     if hasattr(obj, "data_ptr"):
         return obj.data_ptr()
     return obj.ctypes.data
+
+
+def gelu_(x, stream=None):
+    """Ops::gelu in place on a contiguous fp32 or bf16 CUDA tensor."""
+    lib = library()
+    lib.check(lib.lib.omni_b200_gelu(x.data_ptr(), x.numel(), _dtype_code(x), _stream_ptr(stream)))
+    return x
 
 
 def attention_rows(q, k, v, heads, block=0, valid=None, fused=False, out_dtype=None, stream=None,
